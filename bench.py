@@ -1,0 +1,325 @@
+"""Benchmark: SAM ViT-H image encoder with SparseSAM (density 0.3) on B200.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+    (N > 1: launched by torchrun, one rank per GPU)
+
+A step is one SparseSAM-patched encoder forward over one batch of synthetic
+1024x1024 images (batch 64 per GPU; images are independent shards, no collective
+on the data path -> weak scaling). Prints ONE JSON line on rank 0:
+
+  value  images/s over all ranks with the batch already in HBM (device-timed,
+         CUDA events, barrier + synchronize on both sides, max over ranks)
+  e2e    the same metric through the public API with host buffers: pinned host
+         images -> device, encoder(x), features -> host, all inside the timed region
+  roofline  the dominant kernel (the tcgen05 GEMM), achieved TFLOP/s from CUDA
+         events around its launches in the timed region vs the measured peak
+  cpu_baseline  the CPU restatement of the reference path (oracle/) on the host
+         cores, rank 0 at N=1, on a bounded sample (one image)
+
+--impl reference times the reference's CPU path (the oracle restatement: the
+reference's own GPU kernel is a CuTe-DSL SM80 JIT that is not part of this
+build) with all host threads, on the same metric, one image per step.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+REPO = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, REPO)
+
+METRIC = "SAM ViT-H encoder images/sec @1024², d=0.3, bf16, 1/2/4/8 B200; % TC peak"
+ARCH = "vit_h"
+PER_GPU_BATCH = 64
+RATIO = 0.3
+IMG = 1024
+
+
+def encoder_flops(arch: str, ratio: float, img: int = 1024, mlp_merge: bool = True) -> float:
+    """Algorithmic FLOPs per image, valid-token convention: qkv/proj on the real
+    tokens, windowed attention over valid queries x enabled keys, global attention
+    over enabled 64x64 block pairs, MLP at keep_n in the sparse-MLP blocks, plus
+    patch embedding and neck; LN / softmax / rel-pos / scoring excluded."""
+    from oracle.order import a_shape_n_init, keep_n_for
+    from sparsesam_b200.host import VIT_CONFIGS
+    cfg = VIT_CONFIGS[arch]
+    C, depth, heads, gidx = cfg["embed_dim"], cfg["depth"], cfg["num_heads"], set(cfg["global_attn_indexes"])
+    d = C // heads
+    g = img // 16
+    T = g * g
+    fl = 2.0 * T * 768 * C                                     # patch embedding
+    seen_global = False
+    for i in range(depth):
+        fl += 2.0 * T * C * 4 * C                              # qkv + proj
+        if i in gidx:
+            nb = -(-T // 64)
+            n_init = a_shape_n_init(T, 64, ratio, True)
+            pairs = sum(64 * (min(n_init, nb) * 64 + (64 if m >= n_init else 0)) for m in range(nb))
+            fl += 4.0 * d * heads * pairs
+        else:
+            keys = min(a_shape_n_init(196, 64, ratio, False) * 64, 196)
+            fl += 4.0 * d * heads * T * keys
+        sparse_mlp = mlp_merge and ratio < 1.0 and i not in gidx and seen_global
+        rows = keep_n_for(ratio, T) if sparse_mlp else T
+        fl += 2.0 * 2 * rows * C * 4 * C                       # fc1 + fc2
+        seen_global = seen_global or i in gidx
+    fl += 2.0 * T * (C * 256 + 9 * 256 * 256)                  # neck
+    return fl
+
+
+def _peaks() -> dict:
+    path = os.path.join(REPO, "MEASURED_PEAKS.json")
+    if os.path.exists(path):
+        with open(path) as f:
+            p = json.load(f)
+        return {"bf16_tflops": p["bf16_tflops"], "bf16_tflops_sustained": p["bf16_tflops_sustained"],
+                "hbm_gbs": p["hbm_gbs"], "source": "measured"}
+    return {"bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0, "hbm_gbs": 6650.0, "source": "fallback"}
+
+
+class ClockSampler:
+    """nvidia-smi clocks / throttle reasons sampled every 200 ms during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device_index: int):
+        self.idx = device_index
+        self.proc = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "200",
+                 "-i", str(self.idx)], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+
+    def stop(self) -> dict | None:
+        if self.proc is None:
+            return None
+        self.proc.terminate()
+        try:
+            out, _ = self.proc.communicate(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+            out, _ = self.proc.communicate()
+        sm, mx, reasons = [], 0.0, set()
+        names = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
+        for line in out.strip().splitlines():
+            parts = [x.strip() for x in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                mx = max(mx, float(parts[2]))
+            except ValueError:
+                continue
+            for n, v in zip(names, parts[5:9]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        if not sm:
+            return None
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": mx, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+def cpu_baseline(sample_images: int = 1) -> dict:
+    """The CPU restatement (oracle/) of the reference path on this host's cores."""
+    import torch
+
+    from oracle import encoder as oenc
+    from sparsesam_b200 import host
+    cores = len(os.sched_getaffinity(0))
+    torch.set_num_threads(cores)
+    enc = host.build_image_encoder(ARCH, seed=0).eval()
+    img = host.synthetic_images(sample_images, seed=0, img_size=IMG)
+    t0 = time.perf_counter()
+    oenc.encoder_forward(enc, img, RATIO)
+    dt = time.perf_counter() - t0
+    return {"value": sample_images / dt, "unit": "images/s", "cores": cores, "kind": "port",
+            "sample": f"{sample_images} image(s) of the same workload (ViT-H, 1024^2, d={RATIO}), fp32 torch on CPU,"
+                      f" {dt:.1f} s"}
+
+
+def run_reference(args) -> None:
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    import torch
+
+    from oracle import encoder as oenc
+    from sparsesam_b200 import host
+    cores = len(os.sched_getaffinity(0))
+    torch.set_num_threads(cores)
+    enc = host.build_image_encoder(ARCH, seed=0).eval()
+    img = host.synthetic_images(1, seed=0, img_size=IMG)
+    for _ in range(min(args.warmup, 1)):
+        oenc.encoder_forward(enc, img, RATIO)
+    steps = max(1, min(args.steps, 3))
+    t0 = time.perf_counter()
+    for _ in range(steps):
+        oenc.encoder_forward(enc, img, RATIO)
+    dt = (time.perf_counter() - t0) / steps
+    v = 1.0 / dt
+    line = {"impl": "reference", "metric": METRIC, "value": v, "unit": "images/s", "n_gpus": args.gpus,
+            "steps": steps, "warmup": min(args.warmup, 1), "ms_per_step": dt * 1e3, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "config": {"workload": f"SAM ViT-H encoder 1024x1024, d={RATIO}, one image per step (CPU sample)",
+                       "global_batch": 1, "ratio": RATIO},
+            "cpu_baseline": {"value": v, "unit": "images/s", "cores": cores, "kind": "port",
+                             "sample": "one ViT-H image per step through the oracle restatement of the reference "
+                                       "path (the reference's own kernel is a CuTe-DSL SM80 JIT)"},
+            "e2e": {"value": v, "unit": "images/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+def run_ours(args) -> None:
+    import torch
+    import torch.distributed as dist
+
+    from sparsesam_b200 import _lib, host, ops, registry
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=dev)
+
+    batch = args.batch
+    enc = host.build_image_encoder(ARCH, seed=0, device=dev).eval()
+    registry.apply_sam(enc, "sparsesam", ratio=RATIO)
+    # each rank owns its own shard of images (seeded by rank)
+    x_host = host.synthetic_images(batch, seed=1000 + rank, img_size=IMG).pin_memory()
+    x_dev = x_host.to(dev)
+    feat_host = torch.empty(batch, 256, IMG // 16, IMG // 16, dtype=torch.float32).pin_memory()
+
+    def barrier():
+        if world > 1:
+            dist.barrier(device_ids=[local])
+
+    def timed(fn, steps):
+        barrier()
+        torch.cuda.synchronize()
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s.record()
+        for _ in range(steps):
+            fn()
+        e.record()
+        torch.cuda.synchronize()
+        barrier()
+        ms = s.elapsed_time(e)
+        if world > 1:
+            t = torch.tensor([ms], device=dev)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            ms = float(t.item())
+        return ms
+
+    with torch.no_grad():
+        def step_device():
+            enc(x_dev)
+
+        def step_e2e():
+            xd = x_host.to(dev, non_blocking=True)
+            feats, _ = enc(xd)
+            feat_host.copy_(feats, non_blocking=True)
+
+        for _ in range(args.warmup):
+            step_device()
+        torch.cuda.synchronize()
+        clocks = ClockSampler(local)
+        clocks.start()
+        ops.KernelTimer.records = []
+        ops.KernelTimer.active = True
+        launches0 = _lib.launch_count
+        ms = timed(step_device, args.steps)
+        launches = (_lib.launch_count - launches0) // max(1, args.steps)
+        ops.KernelTimer.active = False
+        clk = clocks.stop()
+        step_e2e()
+        ms_e2e = timed(step_e2e, args.steps)
+    err = ops.device_error()
+    if err != 0:
+        raise RuntimeError(f"device error flag {err}")
+
+    # dominant kernel: the GEMM (tcgen05); per-launch averages over the timed region
+    g = [(fl, st.elapsed_time(en)) for kind, fl, st, en in ops.KernelTimer.records if kind == "gemm"]
+    a = [(fl, st.elapsed_time(en)) for kind, fl, st, en in ops.KernelTimer.records if kind == "attention"]
+    peaks = _peaks()
+    g_tflops = sum(f for f, _ in g) / (sum(t for _, t in g) * 1e-3) / 1e12 if g else None
+    a_tflops = sum(f for f, _ in a) / (sum(t for _, t in a) * 1e-3) / 1e12 if a else None
+    gemm_ms_step = sum(t for _, t in g) / args.steps
+    attn_ms_step = sum(t for _, t in a) / args.steps
+
+    imgs_total = batch * world * args.steps
+    value = imgs_total / (ms * 1e-3)
+    e2e = imgs_total / (ms_e2e * 1e-3)
+    flops_img = encoder_flops(ARCH, RATIO)
+    enc_tflops = flops_img * value / world / 1e12          # per GPU
+    if rank != 0:
+        if world > 1:
+            dist.destroy_process_group()
+        return
+    traffic = None
+    tpath = os.path.join(REPO, "profiles", "gemm_traffic.json")
+    if os.path.exists(tpath):
+        with open(tpath) as f:
+            traffic = json.load(f).get("bytes_per_launch")
+    line = {
+        "metric": METRIC, "value": value, "unit": "images/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+        "config": {"workload": f"SAM ViT-H image encoder (configs[4]), 1024x1024, SparseSAM density {RATIO}, "
+                               f"{batch} images per GPU, seed-0 random weights",
+                   "global_batch": batch * world, "per_gpu_batch": batch, "ratio": RATIO,
+                   "parallelism": f"dp{world} (independent image shards, no collective)",
+                   "l2": "inputs larger than L2 (805 MB of images and GBs of activations per step)"},
+        "e2e": {"value": e2e, "unit": "images/s", "h2d_bytes_per_step": x_host.numel() * 4,
+                "d2h_bytes_per_step": feat_host.numel() * 4},
+        "gpu_launches": launches,
+        "tc_peak_frac": {"encoder_tflops_per_gpu": enc_tflops, "flops_per_image": flops_img,
+                         "peak_tflops": peaks["bf16_tflops"], "frac": enc_tflops / peaks["bf16_tflops"],
+                         "peak_source": peaks["source"] + " burst bf16"},
+        "roofline": {"kernel": "gemm_bf16_tn (tcgen05)", "bound": "tensor", "achieved": g_tflops,
+                     "peak": peaks["bf16_tflops_sustained"], "unit": "TFLOP/s",
+                     "frac": (g_tflops / peaks["bf16_tflops_sustained"]) if g_tflops else None,
+                     "traffic": traffic, "peak_source": peaks["source"] + " sustained bf16",
+                     "gemm_ms_per_step": gemm_ms_step, "attention_ms_per_step": attn_ms_step,
+                     "attention_tflops": a_tflops},
+        "clocks": clk,
+    }
+    if world == 1 and not args.no_cpu_baseline:
+        line["cpu_baseline"] = cpu_baseline(1)
+    print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.destroy_process_group()
+
+
+def main() -> None:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=5)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
+    ap.add_argument("--batch", type=int, default=PER_GPU_BATCH)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3 and args.impl == "ours":
+        args.warmup = 3
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

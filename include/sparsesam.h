@@ -1,0 +1,193 @@
+/*
+ * sparsesam.h — C ABI of the B200 (sm_100a) SparseSAM image-encoder hot path.
+ *
+ * Conventions shared by every entry point:
+ *   - All tensor arguments are caller-owned DEVICE pointers; nothing on the hot
+ *     path allocates. Composite calls that need intermediates take a caller
+ *     workspace whose size the matching *_workspace_size() query returns.
+ *   - `stream` is a cudaStream_t passed as void*; NULL means the legacy stream.
+ *   - Every call returns an int status (SSAM_OK or an SSAM_ERR_* code); no C++
+ *     exception crosses this boundary. Calls only enqueue work: device-side
+ *     failures (a bounded wait that ran out) are reported by ssam_device_error().
+ *   - bf16 tensors are passed as `void*` holding IEEE bfloat16 values; fp32 as float*.
+ *   - Calls are re-entrant: the only library globals are the device error flag
+ *     and per-process caches of immutable launch configuration.
+ *
+ * Reference paths below are relative to the hchautran/SparseSAM repository.
+ */
+#ifndef SPARSESAM_B200_H_
+#define SPARSESAM_B200_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define SSAM_OK 0
+#define SSAM_ERR_INVALID 1     /* bad argument: null pointer, shape, ratio, mode   */
+#define SSAM_ERR_ALIGN 2       /* pointer or leading dimension misaligned for TMA  */
+#define SSAM_ERR_UNSUPPORTED 3 /* shape outside what the kernels implement         */
+#define SSAM_ERR_CUDA 4        /* CUDA runtime / driver error while launching      */
+#define SSAM_ERR_TIMEOUT 5     /* a bounded device-side wait ran out               */
+
+/* GEMM epilogues (ssam_gemm_bf16). */
+#define SSAM_EPI_BF16 0      /* out_bf16[r, n] = acc + bias[n]                         */
+#define SSAM_EPI_GELU_BF16 1 /* out_bf16[r, n] = gelu_erf(acc + bias[n])               */
+#define SSAM_EPI_ADD_F32 2   /* out_f32[rows[r], n] += acc + bias[n]; rows[r] < 0 skip */
+#define SSAM_EPI_F32 3       /* out_f32[r, n] = acc + bias[n]                          */
+
+/* Stripe-sort layouts and rankings (perm_mode = <space>_<layout>_<ranking>). */
+#define SSAM_LAYOUT_INTERLEAVE 0
+#define SSAM_LAYOUT_NAIVE 1
+#define SSAM_RANKING_SORT 0
+#define SSAM_RANKING_NOSORT 1
+
+/* Library version (major*10000 + minor*100 + patch). */
+int ssam_version(void);
+
+/* Human-readable text for a status code. */
+const char* ssam_status_string(int status);
+
+/* Synchronises the current device and returns the device-side error flag
+ * (SSAM_OK when no kernel raised one). `reset` != 0 clears it. */
+int ssam_device_error(int reset);
+
+/* ---------------------------------------------------------------------------
+ * a1. Morton (Z-curve) raster->Z permutation of an H x W grid.
+ * Replaces algos/sparsesam/z_utils.py:35-49 (encode), :65-85 (_compute_z_order),
+ * :88-101 (get_z_order) and :104-113 (get_z_inverse).
+ * perm[i] = raster index of the i-th token in Z order; inv_perm may be NULL.
+ * ------------------------------------------------------------------------- */
+int ssam_zorder(int H, int W, int32_t* perm, int32_t* inv_perm, void* stream);
+
+/* ---------------------------------------------------------------------------
+ * a2. Stripe-Sort permutation of every (sequence, head) row of K.
+ * Replaces algos/sparsesam/sam.py:105-164 (tile_stride_matching), as called at
+ * sam.py:193-204.
+ *   K of row r = s*heads + h, token t, channel c is read at
+ *     k[(s*H*W + t)*ld + h*d + c]            (bf16; `k` already points at K)
+ *   base_perm : int32[H*W] space-filling order (ssam_zorder output for "z").
+ *   Outputs (int32, [rows, H*W]): perm (interleave or naive layout), inv_perm,
+ *   inv_perm_group. Group scores are computed in fp64; ties in the descending
+ *   group ranking are broken by lowest group index.
+ * ------------------------------------------------------------------------- */
+int ssam_stripe_sort_perm(const void* k, int64_t ld, int n_seq, int heads, int H, int W, int d,
+                          int group_size, int layout, int ranking, const int32_t* base_perm,
+                          int32_t* perm, int32_t* inv_perm, int32_t* inv_perm_group, void* stream);
+
+/* ---------------------------------------------------------------------------
+ * a7. A-shape block-mask parameters. Replaces sam.py:219-223.
+ * Returns n_init_blocks = int(ratio*ceil(N/n_block)) (+1 when !is_global), or
+ * -1 on invalid input.
+ * ------------------------------------------------------------------------- */
+int ssam_a_shape_n_init(int N, int n_block, double ratio, int is_global);
+
+/* Host-side (num_m x num_n) uint8 block mask equal to the inline predicate of
+ * algos/kernels/flash_attn.py:132-145: enabled = n < n_init || (diag && n == m). */
+int ssam_a_shape_mask(int N, int m_block, int n_block, int n_init, int with_diag, uint8_t* mask);
+
+/* ---------------------------------------------------------------------------
+ * a3+a4+a5+a6+a8. Stripe-Sort block-sparse attention with SAM's decomposed
+ * relative-position bias, fused with the permutation gathers and the inverse
+ * permutation / head merge.
+ * Replaces sam.py:32-49 (get_rel_pos), sam.py:62-73 (compute_rel_bias),
+ * sam.py:206-209 (q/k/v gathers), the kernel
+ * algos/kernels/flash_attn.py:577-874 (call_a_shape / kernel_a_shape) with
+ * :877-909 (_pos_modify_scores), and sam.py:231-232 (inverse gather + merge).
+ *   qkv : bf16 [n_seq*win*win, 3*heads*d] rows, leading dim ld_qkv (elements);
+ *         q | k | v column blocks, each head d contiguous (SAM qkv Linear order).
+ *   rel_pos_h / rel_pos_w : bf16 [2*win-1, d] tables (Attention.rel_pos_h/w).
+ *   perm  : int32 [n_seq*heads, win*win] permutation of every row.
+ *   out   : bf16 [n_seq*win*win, heads*d] in raster token order, leading dim ld_out.
+ *   n_init_blocks / with_diag : A-shape mask over 64-token blocks.
+ * d must be 64 or 80.
+ * ------------------------------------------------------------------------- */
+int ssam_sparse_attn_fwd(const void* qkv, int64_t ld_qkv, int n_seq, int heads, int win, int d,
+                         const void* rel_pos_h, const void* rel_pos_w, const int32_t* perm,
+                         int n_init_blocks, int with_diag, float scale, void* out, int64_t ld_out,
+                         void* stream);
+
+/* ---------------------------------------------------------------------------
+ * a10 (selection). Keep set of the Residual-Consistency MLP.
+ * Replaces sam.py:277-280: avg_rank = mean over heads of inv_perm_group, then
+ * topk(keep_n, largest=False). Ordering key is (sum of per-head ranks, token
+ * index), i.e. ties go to the lowest token index.
+ *   inv_perm_group : int32 [B*heads, N];  idx : int32 [B, keep_n] (token index,
+ *   ascending key order);  rows (may be NULL): int32 [B*keep_n] = b*N + idx.
+ * ------------------------------------------------------------------------- */
+int ssam_keep_select(const int32_t* inv_perm_group, int B, int heads, int N, int keep_n, int32_t* idx,
+                     int32_t* rows, void* stream);
+
+/* ---------------------------------------------------------------------------
+ * a9 / a10 data movement. Row-gathered LayerNorm:
+ *   out[r, :] = bf16(LN(x[src_rows[r], :]) * w + b), or 0 when src_rows[r] < 0.
+ * src_rows == NULL means identity. Covers norm1 + window_partition (sam.py:248,
+ * 252), norm2 of the kept tokens (sam.py:282-283) and the dense norm2.
+ * ------------------------------------------------------------------------- */
+int ssam_layernorm_gather(const float* x, int64_t ldx, const int32_t* src_rows, int n_rows, int C,
+                          const float* w, const float* b, float eps, void* out, int64_t ld_out, void* stream);
+
+/* Row map of window_partition for a (B, H, W) token grid and window ws:
+ * rows[(b*nwh*nww + wy*nww + wx)*ws*ws + ty*ws + tx] = b*H*W + y*W + x, or -1 in
+ * the zero padding. The same map unpartitions (proj epilogue skips -1 rows). */
+int ssam_window_rows(int B, int H, int W, int ws, int32_t* rows, void* stream);
+
+/* ---------------------------------------------------------------------------
+ * GEMM on the 5th-generation tensor cores (tcgen05 + TMEM, TMA-fed):
+ *   acc[r, n] = sum_k A[r, k] * B[n, k]        (A: M x K, B: N x K, bf16, K-major)
+ * then the epilogue selected by `epilogue` (SSAM_EPI_*). `bias` may be NULL.
+ * out_rows is only read by SSAM_EPI_ADD_F32 (NULL = identity).
+ * Used for Attention.qkv / Attention.proj (sam.py:182, 233), MLPBlock lin1/lin2
+ * (sam.py:283, 286), patch embedding and the neck convolutions.
+ * Requirements: lda, ldb multiples of 8; K multiple of 8; N multiple of 32.
+ * ------------------------------------------------------------------------- */
+int ssam_gemm_bf16(const void* A, int64_t lda, const void* B, int64_t ldb, int M, int N, int K,
+                   const float* bias, int epilogue, void* out, int64_t ldo, const int32_t* out_rows,
+                   void* stream);
+
+/* ---------------------------------------------------------------------------
+ * a10 (compute). Residual-Consistency MLP on a row subset, in place:
+ *   x[rows[r]] += lin2(gelu(lin1(LN(x[rows[r]]))))   for r < n_rows
+ * rows == NULL means the dense MLP over the first n_rows rows.
+ * Replaces sam.py:281-288. Intermediates live in the caller workspace of
+ * ssam_rc_mlp_workspace_size(n_rows, C, hidden) bytes.
+ * ------------------------------------------------------------------------- */
+size_t ssam_rc_mlp_workspace_size(int n_rows, int C, int hidden);
+int ssam_rc_mlp_fwd(float* x, int64_t ldx, const int32_t* rows, int n_rows, int C, int hidden,
+                    const float* ln_w, const float* ln_b, float eps, const void* w1, const float* b1,
+                    const void* w2, const float* b2, void* workspace, size_t workspace_bytes, void* stream);
+
+/* ---------------------------------------------------------------------------
+ * Encoder stem and neck data movement (host model pieces kept by the patch).
+ * ------------------------------------------------------------------------- */
+/* Patch-embed im2col: img fp32 NCHW (B, Cin, H, W) -> bf16 [B*(H/p)*(W/p), Cin*p*p]
+ * in (cin, ky, kx) column order, matching a Conv2d(Cin, C, p, stride p) weight view. */
+int ssam_patch_im2col(const float* img, int B, int Cin, int H, int W, int p, void* out, void* stream);
+
+/* x[b, t, :] = pos[t, :] for every image b (fp32, T tokens x C). */
+int ssam_broadcast_rows(const float* pos, int B, int T, int C, float* x, void* stream);
+
+/* 3x3 / pad 1 im2col over a channels-last bf16 grid (B, H, W, C) ->
+ * bf16 [B*H*W, 9*C] in (ky, kx, c) column order, i.e. matching a Conv2d weight
+ * permuted to (Cout, 3, 3, Cin). */
+int ssam_im2col3x3_nhwc(const void* in, int B, int H, int W, int C, void* out, void* stream);
+
+/* Channels-last fp32 (B, H*W, C) -> channels-first fp32 (B, C, H*W). */
+int ssam_nhwc_to_nchw(const float* in, int B, int HW, int C, float* out, void* stream);
+
+/* Row LayerNorm fp32 -> fp32 or bf16, used by the neck LayerNorm2d. out_bf16 != 0 selects bf16. */
+int ssam_layernorm_rows(const float* x, int n_rows, int C, const float* w, const float* b, float eps,
+                        void* out, int out_bf16, void* stream);
+
+/* hi/lo split of fp32 rows into bf16: out[r] = [bf16(x[r]) | bf16(x[r] - bf16(x[r]))]
+ * (2*C columns). A GEMM of the split rows against [W | W] carries the fp32
+ * activation into the tensor-core GEMM (used for the neck convolutions). */
+int ssam_split_bf16x2(const float* x, int n_rows, int C, void* out, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* SPARSESAM_B200_H_ */

@@ -1,0 +1,312 @@
+// Persistent, warp-specialised bf16 GEMM on the sm_100a tensor cores.
+//
+//   acc[r, n] = sum_k A[r, k] * B[n, k]      A: M x K, B: N x K (both K-major)
+//
+// Roles per CTA (one CTA per SM, 192 threads):
+//   warp 0      : TMA producer — 128x64 A tile + 256x64 B tile per stage (SW128).
+//   warp 1      : UMMA issuer  — tcgen05.mma M=128 N=256 K=16, fp32 accumulator
+//                 in TMEM, two accumulator buffers (2 x 256 columns).
+//   warps 2..5  : epilogue     — tcgen05.ld rows out of TMEM, fused bias /
+//                 GELU / fp32 residual add through an optional row map.
+// Every wait is bounded; on timeout the CTA records SSAM_ERR_TIMEOUT, drains the
+// copies and MMAs it issued, frees TMEM and returns.
+//
+// Used for the SAM Attention.qkv / Attention.proj linears (algos/sparsesam/sam.py:182,233),
+// MLPBlock lin1/lin2 (sam.py:283,286), the patch embedding and the neck convolutions.
+#include "common.cuh"
+#include "host_util.h"
+
+namespace ssam {
+
+constexpr int kGemmBM = 128;
+constexpr int kGemmBN = 256;
+constexpr int kGemmBK = 64;
+constexpr int kGemmStages = 4;
+constexpr int kGemmABytes = kGemmBM * kGemmBK * 2;  // 16 KB
+constexpr int kGemmBBytes = kGemmBN * kGemmBK * 2;  // 32 KB
+constexpr int kGemmStageBytes = kGemmABytes + kGemmBBytes;
+constexpr int kGemmThreads = 192;
+constexpr int kGemmTmemCols = 512;
+constexpr int kGemmSmemBytes = kGemmStages * kGemmStageBytes + 1024 /*align slack*/ + 256 /*barriers*/;
+
+struct GemmParams {
+  int M, N, K;
+  const float* bias;
+  void* out;
+  int64_t ldo;
+  const int32_t* out_rows;
+};
+
+template <int EPI>
+__device__ __forceinline__ void gemm_epilogue_chunk(const GemmParams& p, int row, int col0, const uint32_t (&r)[32]) {
+  float v[32];
+#pragma unroll
+  for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+  if (p.bias != nullptr) {
+    const float4* b4 = reinterpret_cast<const float4*>(p.bias + col0);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const float4 b = __ldg(b4 + i);
+      v[4 * i + 0] += b.x;
+      v[4 * i + 1] += b.y;
+      v[4 * i + 2] += b.z;
+      v[4 * i + 3] += b.w;
+    }
+  }
+  if constexpr (EPI == SSAM_EPI_BF16 || EPI == SSAM_EPI_GELU_BF16) {
+    if constexpr (EPI == SSAM_EPI_GELU_BF16) {
+#pragma unroll
+      for (int i = 0; i < 32; ++i) v[i] = gelu_exact(v[i]);
+    }
+    uint4* dst = reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(p.out) + static_cast<int64_t>(row) * p.ldo + col0);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      uint4 q;
+      q.x = pack_bf16x2(v[8 * i + 0], v[8 * i + 1]);
+      q.y = pack_bf16x2(v[8 * i + 2], v[8 * i + 3]);
+      q.z = pack_bf16x2(v[8 * i + 4], v[8 * i + 5]);
+      q.w = pack_bf16x2(v[8 * i + 6], v[8 * i + 7]);
+      dst[i] = q;
+    }
+  } else if constexpr (EPI == SSAM_EPI_F32) {
+    float4* dst = reinterpret_cast<float4*>(static_cast<float*>(p.out) + static_cast<int64_t>(row) * p.ldo + col0);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) dst[i] = make_float4(v[4 * i + 0], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
+  } else {
+    const int orow = p.out_rows != nullptr ? __ldg(p.out_rows + row) : row;
+    if (orow < 0) return;
+    float4* dst = reinterpret_cast<float4*>(static_cast<float*>(p.out) + static_cast<int64_t>(orow) * p.ldo + col0);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      float4 o = dst[i];
+      o.x += v[4 * i + 0];
+      o.y += v[4 * i + 1];
+      o.z += v[4 * i + 2];
+      o.w += v[4 * i + 3];
+      dst[i] = o;
+    }
+  }
+}
+
+template <int EPI>
+__global__ void __launch_bounds__(kGemmThreads, 1)
+    gemm_bf16_tn_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                        const GemmParams p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sA = smem;
+  uint8_t* sB = smem + kGemmStages * kGemmABytes;
+  uint64_t* full_bar = reinterpret_cast<uint64_t*>(smem + kGemmStages * kGemmStageBytes);
+  uint64_t* empty_bar = full_bar + kGemmStages;
+  uint64_t* tfull_bar = empty_bar + kGemmStages;  // [2]
+  uint64_t* tempty_bar = tfull_bar + 2;           // [2]
+  uint64_t* drain_bar = tempty_bar + 2;           // [1]
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(drain_bar + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int m_tiles = (p.M + kGemmBM - 1) / kGemmBM;
+  const int n_tiles = (p.N + kGemmBN - 1) / kGemmBN;
+  const int num_tiles = m_tiles * n_tiles;
+  const int kblocks = (p.K + kGemmBK - 1) / kGemmBK;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kGemmStages; ++s) {
+      mbar_init(&full_bar[s], 1);
+      mbar_init(&empty_bar[s], 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&tfull_bar[a], 1);
+      mbar_init(&tempty_bar[a], 128);
+    }
+    mbar_init(drain_bar, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&tmA);
+    tma_prefetch_desc(&tmB);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_holder, kGemmTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_holder;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      // ---------------- TMA producer ----------------
+      int stage = 0;
+      uint32_t phase = 0;
+      uint32_t issued_mask = 0;      // stages holding a load the MMA warp may not have consumed
+      uint32_t issued_parity = 0;    // parity of the latest load per stage
+      for (int tile = blockIdx.x; tile < num_tiles && !*abort_flag; tile += gridDim.x) {
+        const int mb = tile / n_tiles;
+        const int nb = tile - mb * n_tiles;
+        for (int kb = 0; kb < kblocks; ++kb) {
+          if (!mbar_wait(&empty_bar[stage], phase ^ 1)) {
+            *abort_flag = 1;
+            break;
+          }
+          mbar_arrive_expect_tx(&full_bar[stage], kGemmStageBytes);
+          tma_load_2d(sA + stage * kGemmABytes, &tmA, &full_bar[stage], kb * kGemmBK, mb * kGemmBM);
+          tma_load_2d(sB + stage * kGemmBBytes, &tmB, &full_bar[stage], kb * kGemmBK, nb * kGemmBN);
+          issued_mask |= 1u << stage;
+          issued_parity = (issued_parity & ~(1u << stage)) | (phase << stage);
+          if (++stage == kGemmStages) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+      }
+      if (*abort_flag) {
+        // Drain: every load this thread issued must land before the CTA exits.
+        for (int s = 0; s < kGemmStages; ++s)
+          if (issued_mask & (1u << s)) mbar_wait(&full_bar[s], (issued_parity >> s) & 1u);
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      // ---------------- UMMA issuer ----------------
+      const uint32_t idesc = make_idesc_bf16(kGemmBM, kGemmBN, 0, 0);
+      int stage = 0;
+      uint32_t phase = 0;
+      int local = 0;
+      for (int tile = blockIdx.x; tile < num_tiles && !*abort_flag; tile += gridDim.x, ++local) {
+        const int acc = local & 1;
+        const uint32_t acc_phase = (local >> 1) & 1;
+        if (!mbar_wait(&tempty_bar[acc], acc_phase ^ 1)) {
+          *abort_flag = 1;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * kGemmBN);
+        bool ok = true;
+        for (int kb = 0; kb < kblocks; ++kb) {
+          if (!mbar_wait(&full_bar[stage], phase)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a0 = smem_u32(sA + stage * kGemmABytes);
+          const uint32_t b0 = smem_u32(sB + stage * kGemmBBytes);
+#pragma unroll
+          for (int k = 0; k < kGemmBK / 16; ++k) {
+            const uint64_t ad = make_smem_desc(a0 + k * 32, 16, 1024, kSw128);
+            const uint64_t bd = make_smem_desc(b0 + k * 32, 16, 1024, kSw128);
+            umma_f16_ss(d_tmem, ad, bd, idesc, (kb | k) != 0 ? 1u : 0u);
+          }
+          umma_commit(&empty_bar[stage]);
+          if (++stage == kGemmStages) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+        if (!ok) {
+          *abort_flag = 1;
+          break;
+        }
+        umma_commit(&tfull_bar[acc]);
+      }
+      // Make sure every MMA this thread issued has retired before TMEM is freed.
+      umma_commit(drain_bar);
+      mbar_wait(drain_bar, 0);
+    }
+  } else {
+    // ---------------- epilogue warps 2..5 ----------------
+    const int sp = warp & 3;  // TMEM sub-partition this warp may access
+    const int row_in_tile = sp * 32 + lane;
+    int local = 0;
+    for (int tile = blockIdx.x; tile < num_tiles && !*abort_flag; tile += gridDim.x, ++local) {
+      const int mb = tile / n_tiles;
+      const int nb = tile - mb * n_tiles;
+      const int acc = local & 1;
+      const uint32_t acc_phase = (local >> 1) & 1;
+      if (!mbar_wait(&tfull_bar[acc], acc_phase)) {
+        *abort_flag = 1;
+        break;
+      }
+      tc_fence_after();
+      const int row = mb * kGemmBM + row_in_tile;
+      const uint32_t t_row = tmem_base + (static_cast<uint32_t>(sp * 32) << 16) + static_cast<uint32_t>(acc * kGemmBN);
+#pragma unroll 1
+      for (int c = 0; c < kGemmBN; c += 32) {
+        const int col0 = nb * kGemmBN + c;
+        if (col0 >= p.N) break;  // warp-uniform
+        uint32_t r[32];
+        tmem_ld_32x32b_x32(t_row + static_cast<uint32_t>(c), r);
+        tmem_ld_wait();
+        if (row < p.M) gemm_epilogue_chunk<EPI>(p, row, col0, r);
+      }
+      tc_fence_before();
+      mbar_arrive(&tempty_bar[acc]);
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 1) tmem_dealloc(tmem_base, kGemmTmemCols);
+}
+
+template <int EPI>
+static int launch_gemm(const CUtensorMap& ta, const CUtensorMap& tb, const GemmParams& p, cudaStream_t stream) {
+  static bool configured[64] = {false};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return SSAM_ERR_CUDA;
+  if (dev < 0 || dev >= 64) return SSAM_ERR_CUDA;
+  if (!configured[dev]) {
+    if (cudaFuncSetAttribute(gemm_bf16_tn_kernel<EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize, kGemmSmemBytes) !=
+        cudaSuccess)
+      return SSAM_ERR_CUDA;
+    configured[dev] = true;
+  }
+  const int m_tiles = (p.M + kGemmBM - 1) / kGemmBM;
+  const int n_tiles = (p.N + kGemmBN - 1) / kGemmBN;
+  const int tiles = m_tiles * n_tiles;
+  const int grid = tiles < num_sms(dev) ? tiles : num_sms(dev);
+  gemm_bf16_tn_kernel<EPI><<<grid, kGemmThreads, kGemmSmemBytes, stream>>>(ta, tb, p);
+  return cudaGetLastError() == cudaSuccess ? SSAM_OK : SSAM_ERR_CUDA;
+}
+
+int gemm_bf16(const void* A, int64_t lda, const void* B, int64_t ldb, int M, int N, int K, const float* bias,
+              int epilogue, void* out, int64_t ldo, const int32_t* out_rows, cudaStream_t stream) {
+  if (A == nullptr || B == nullptr || out == nullptr) return SSAM_ERR_INVALID;
+  if (M < 0 || N <= 0 || K <= 0) return SSAM_ERR_INVALID;
+  if (M == 0) return SSAM_OK;
+  if (N % 32 != 0 || K % 8 != 0) return SSAM_ERR_UNSUPPORTED;
+  if (lda < K || ldb < K || ldo < N) return SSAM_ERR_INVALID;
+  if ((lda % 8) || (ldb % 8) || !aligned16(A) || !aligned16(B) || !aligned16(out)) return SSAM_ERR_ALIGN;
+  if (bias != nullptr && !aligned16(bias)) return SSAM_ERR_ALIGN;
+  if (epilogue == SSAM_EPI_ADD_F32 || epilogue == SSAM_EPI_F32) {
+    if (ldo % 4) return SSAM_ERR_ALIGN;
+  } else if (epilogue == SSAM_EPI_BF16 || epilogue == SSAM_EPI_GELU_BF16) {
+    if (ldo % 8) return SSAM_ERR_ALIGN;
+  } else {
+    return SSAM_ERR_INVALID;
+  }
+  CUtensorMap ta, tb;
+  int st = make_tmap_2d_bf16(&ta, A, static_cast<uint64_t>(M), static_cast<uint64_t>(K), static_cast<uint64_t>(lda),
+                             kGemmBK, kGemmBM, CU_TENSOR_MAP_SWIZZLE_128B);
+  if (st != SSAM_OK) return st;
+  st = make_tmap_2d_bf16(&tb, B, static_cast<uint64_t>(N), static_cast<uint64_t>(K), static_cast<uint64_t>(ldb), kGemmBK,
+                         kGemmBN, CU_TENSOR_MAP_SWIZZLE_128B);
+  if (st != SSAM_OK) return st;
+  GemmParams p{M, N, K, bias, out, ldo, out_rows};
+  switch (epilogue) {
+    case SSAM_EPI_BF16:
+      return launch_gemm<SSAM_EPI_BF16>(ta, tb, p, stream);
+    case SSAM_EPI_GELU_BF16:
+      return launch_gemm<SSAM_EPI_GELU_BF16>(ta, tb, p, stream);
+    case SSAM_EPI_F32:
+      return launch_gemm<SSAM_EPI_F32>(ta, tb, p, stream);
+    default:
+      return launch_gemm<SSAM_EPI_ADD_F32>(ta, tb, p, stream);
+  }
+}
+
+}  // namespace ssam

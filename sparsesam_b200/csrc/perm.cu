@@ -1,0 +1,329 @@
+// Token-order kernels: Morton order, Stripe-Sort permutation and the
+// Residual-Consistency keep set. All outputs are integer index tensors and are
+// produced bit-exactly: group scores are accumulated in fp64 and every ranking
+// breaks ties by the lowest index.
+#include "common.cuh"
+#include "host_util.h"
+
+namespace ssam {
+
+constexpr int kMaxTokens = 16384;  // largest H*W handled by the permutation kernels
+
+// ---------------------------------------------------------------------------
+// a1. Morton order (algos/sparsesam/z_utils.py:35-49 encode, :65-85 _compute_z_order).
+// Key of raster cell (r, c): bit i of r at position 2i+1, bit i of c at 2i,
+// over num_bits = max(1, ceil(log2(max(H, W)))). perm = argsort(key); keys are
+// unique, so the rank of a cell is the number of smaller keys.
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ uint32_t morton_key(uint32_t r, uint32_t c, int num_bits) {
+  uint32_t z = 0;
+  for (int i = 0; i < num_bits; ++i) {
+    z |= ((r >> i) & 1u) << (2 * i + 1);
+    z |= ((c >> i) & 1u) << (2 * i);
+  }
+  return z;
+}
+
+__global__ void zorder_kernel(int H, int W, int num_bits, int32_t* perm, int32_t* inv_perm) {
+  const int N = H * W;
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= N) return;
+  const uint32_t ki = morton_key(i / W, i % W, num_bits);
+  int rank = 0;
+  for (int j = 0; j < N; ++j) rank += morton_key(j / W, j % W, num_bits) < ki;
+  perm[rank] = i;
+  if (inv_perm != nullptr) inv_perm[i] = rank;
+}
+
+int zorder(int H, int W, int32_t* perm, int32_t* inv_perm, cudaStream_t stream) {
+  if (H <= 0 || W <= 0 || perm == nullptr || H * W > kMaxTokens) return SSAM_ERR_INVALID;
+  int m = H > W ? H : W;
+  int num_bits = 0;
+  while ((1 << num_bits) < m) ++num_bits;  // ceil(log2(m))
+  if (num_bits < 1) num_bits = 1;
+  const int N = H * W;
+  zorder_kernel<<<(N + 255) / 256, 256, 0, stream>>>(H, W, num_bits, perm, inv_perm);
+  return status_from_cuda(cudaGetLastError());
+}
+
+// ---------------------------------------------------------------------------
+// a2. Stripe-Sort permutation (algos/sparsesam/sam.py:105-164, tile_stride_matching).
+// One CTA per (sequence, head) row:
+//   1. groups of `gs` consecutive tokens in base order (Z curve);
+//   2. grp_std = mean over channels of the unbiased std over the group;
+//      grp_mean normalised to unit L2 norm (eps 1e-12);
+//   3. avg_sim_g = (sum_j <n_g, n_j> - 1) / max(G-1, 1) computed as
+//      (<n_g, S> - 1)/(G-1) with S = sum_j n_j (the same sum, O(G d));
+//   4. score = z(grp_std) + z(-avg_sim), z = (x - mean) / (unbiased std + 1e-6);
+//   5. descending rank, ties -> lowest group index; layout interleave / naive.
+// ---------------------------------------------------------------------------
+struct StripeArgs {
+  const __nv_bfloat16* k;
+  int64_t ld;
+  int heads, N, d, gs, G, layout, ranking;
+  const int32_t* base_perm;
+  int32_t* perm;
+  int32_t* inv_perm;
+  int32_t* inv_perm_group;
+};
+
+__device__ __forceinline__ double warp_sum_d(double v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+// Block-wide fp64 sum; `red` is a shared array of at least 32 doubles.
+__device__ double block_sum_d(double v, double* red) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+  v = warp_sum_d(v);
+  __syncthreads();
+  if (lane == 0) red[warp] = v;
+  __syncthreads();
+  double t = 0.0;
+  for (int i = 0; i < nw; ++i) t += red[i];  // fixed order: identical on every thread
+  return t;
+}
+
+constexpr int kStripeMaxChPerLane = 8;  // d <= 256
+
+__global__ void stripe_sort_kernel(const StripeArgs a) {
+  extern __shared__ double sm_d[];
+  double* s_std = sm_d;               // [G]
+  double* s_inv = s_std + a.G;        // [G]  1 / max(||mean||, 1e-12)
+  double* s_score = s_inv + a.G;      // [G]
+  double* s_S = s_score + a.G;        // [d]
+  double* s_red = s_S + a.d;          // [32]
+  int* s_order = reinterpret_cast<int*>(s_red + 32);  // [G]
+
+  const int row = blockIdx.x;
+  const int seq = row / a.heads, head = row - seq * a.heads;
+  const __nv_bfloat16* kr = a.k + static_cast<int64_t>(seq) * a.N * a.ld + static_cast<int64_t>(head) * a.d;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+  const int G = a.G, gs = a.gs, d = a.d, N = a.N;
+
+  int32_t* perm = a.perm + static_cast<int64_t>(row) * N;
+  int32_t* inv_perm = a.inv_perm + static_cast<int64_t>(row) * N;
+  int32_t* inv_perm_group = a.inv_perm_group + static_cast<int64_t>(row) * N;
+
+  if (a.ranking == SSAM_RANKING_SORT) {
+    for (int c = threadIdx.x; c < d; c += blockDim.x) s_S[c] = 0.0;
+    __syncthreads();
+    // Pass 1: per-group std and norm, per-warp partial S.
+    double Sp[kStripeMaxChPerLane];
+#pragma unroll
+    for (int i = 0; i < kStripeMaxChPerLane; ++i) Sp[i] = 0.0;
+    for (int g = warp; g < G; g += nw) {
+      double mean[kStripeMaxChPerLane];
+      double std_sum = 0.0, sq = 0.0;
+#pragma unroll
+      for (int i = 0; i < kStripeMaxChPerLane; ++i) {
+        const int c = lane + 32 * i;
+        mean[i] = 0.0;
+        if (c < d) {
+          double m = 0.0;
+          for (int j = 0; j < gs; ++j) {
+            const int t = __ldg(a.base_perm + g * gs + j);
+            m += static_cast<double>(__bfloat162float(kr[static_cast<int64_t>(t) * a.ld + c]));
+          }
+          m /= gs;
+          double v = 0.0;  // second pass re-reads the (L1-resident) group
+          for (int j = 0; j < gs; ++j) {
+            const int t = __ldg(a.base_perm + g * gs + j);
+            const double x = static_cast<double>(__bfloat162float(kr[static_cast<int64_t>(t) * a.ld + c]));
+            v += (x - m) * (x - m);
+          }
+          std_sum += gs > 1 ? sqrt(v / (gs - 1)) : __longlong_as_double(0x7ff8000000000000ll);
+          mean[i] = m;
+          sq += m * m;
+        }
+      }
+      std_sum = warp_sum_d(std_sum);
+      sq = warp_sum_d(sq);
+      const double nrm = sqrt(sq);
+      const double inv = 1.0 / (nrm > 1e-12 ? nrm : 1e-12);
+      if (lane == 0) {
+        s_std[g] = std_sum / d;
+        s_inv[g] = inv;
+      }
+#pragma unroll
+      for (int i = 0; i < kStripeMaxChPerLane; ++i) Sp[i] += mean[i] * inv;
+    }
+    // Reduce S over warps in a fixed warp order.
+    for (int w = 0; w < nw; ++w) {
+      __syncthreads();
+      if (warp == w) {
+#pragma unroll
+        for (int i = 0; i < kStripeMaxChPerLane; ++i) {
+          const int c = lane + 32 * i;
+          if (c < d) s_S[c] += Sp[i];
+        }
+      }
+    }
+    __syncthreads();
+    // Pass 2: <n_g, S> -> dissimilarity.
+    for (int g = warp; g < G; g += nw) {
+      double dot = 0.0;
+#pragma unroll
+      for (int i = 0; i < kStripeMaxChPerLane; ++i) {
+        const int c = lane + 32 * i;
+        if (c < d) {
+          double m = 0.0;
+          for (int j = 0; j < gs; ++j) {
+            const int t = __ldg(a.base_perm + g * gs + j);
+            m += static_cast<double>(__bfloat162float(kr[static_cast<int64_t>(t) * a.ld + c]));
+          }
+          dot += (m / gs) * s_S[c];
+        }
+      }
+      dot = warp_sum_d(dot);
+      if (lane == 0) {
+        const double avg_sim = (dot * s_inv[g] - 1.0) / (G > 1 ? G - 1 : 1);
+        s_score[g] = -avg_sim;  // dissimilarity
+      }
+    }
+    __syncthreads();
+    // z-scores over groups (unbiased std, eps 1e-6).
+    double ps = 0.0, pd = 0.0;
+    for (int g = threadIdx.x; g < G; g += blockDim.x) {
+      ps += s_std[g];
+      pd += s_score[g];
+    }
+    const double mean_s = block_sum_d(ps, s_red) / G;
+    const double mean_d = block_sum_d(pd, s_red) / G;
+    double vs = 0.0, vd = 0.0;
+    for (int g = threadIdx.x; g < G; g += blockDim.x) {
+      vs += (s_std[g] - mean_s) * (s_std[g] - mean_s);
+      vd += (s_score[g] - mean_d) * (s_score[g] - mean_d);
+    }
+    const double den = G > 1 ? G - 1 : 0;  // torch.std of one element is NaN
+    const double sd_s = sqrt(block_sum_d(vs, s_red) / den);
+    const double sd_d = sqrt(block_sum_d(vd, s_red) / den);
+    __syncthreads();
+    for (int g = threadIdx.x; g < G; g += blockDim.x) {
+      const double zs = (s_std[g] - mean_s) / (sd_s + 1e-6);
+      const double zd = (s_score[g] - mean_d) / (sd_d + 1e-6);
+      s_inv[g] = zs + zd;  // reuse as the final score
+    }
+    __syncthreads();
+    // Descending rank with lowest-index ties.
+    for (int g = threadIdx.x; g < G; g += blockDim.x) {
+      const double sg = s_inv[g];
+      int r = 0;
+      for (int j = 0; j < G; ++j) {
+        const double sj = s_inv[j];
+        r += (sj > sg) || (sj == sg && j < g);
+      }
+      s_order[r] = g;
+    }
+  } else {
+    for (int g = threadIdx.x; g < G; g += blockDim.x) s_order[g] = g;
+  }
+  __syncthreads();
+
+  // Emit perm (interleave or naive), inv_perm, inv_perm_group.
+  for (int q = threadIdx.x; q < G; q += blockDim.x) {
+    const int g = s_order[q];
+    for (int t = 0; t < gs; ++t) {
+      const int raster = __ldg(a.base_perm + g * gs + t);
+      const int pg = q * gs + t;
+      const int pi = a.layout == SSAM_LAYOUT_INTERLEAVE ? t * G + q : pg;
+      perm[pi] = raster;
+      inv_perm[raster] = pi;
+      inv_perm_group[raster] = pg;
+    }
+  }
+}
+
+int stripe_sort_perm(const void* k, int64_t ld, int n_seq, int heads, int H, int W, int d, int gs, int layout,
+                     int ranking, const int32_t* base_perm, int32_t* perm, int32_t* inv_perm, int32_t* inv_perm_group,
+                     cudaStream_t stream) {
+  if (k == nullptr || base_perm == nullptr || perm == nullptr || inv_perm == nullptr || inv_perm_group == nullptr)
+    return SSAM_ERR_INVALID;
+  if (n_seq <= 0 || heads <= 0 || H <= 0 || W <= 0 || d <= 0 || gs <= 0) return SSAM_ERR_INVALID;
+  if (layout != SSAM_LAYOUT_INTERLEAVE && layout != SSAM_LAYOUT_NAIVE) return SSAM_ERR_INVALID;
+  if (ranking != SSAM_RANKING_SORT && ranking != SSAM_RANKING_NOSORT) return SSAM_ERR_INVALID;
+  const int N = H * W;
+  if (N % gs != 0) return SSAM_ERR_INVALID;  // sam.py:116
+  if (N > kMaxTokens || d > 32 * kStripeMaxChPerLane || gs > 32) return SSAM_ERR_UNSUPPORTED;
+  if (ld < static_cast<int64_t>(heads) * d) return SSAM_ERR_INVALID;
+  StripeArgs a{static_cast<const __nv_bfloat16*>(k), ld, heads, N, d, gs, N / gs, layout, ranking, base_perm,
+               perm, inv_perm, inv_perm_group};
+  const int G = N / gs;
+  const size_t smem = sizeof(double) * (3 * static_cast<size_t>(G) + d + 32) + sizeof(int) * G;
+  int threads = 256;
+  if (G <= 64) threads = 64;
+  else if (G <= 256) threads = 128;
+  static bool configured = false;
+  if (!configured) {
+    if (cudaFuncSetAttribute(stripe_sort_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 160 * 1024) !=
+        cudaSuccess)
+      return SSAM_ERR_CUDA;
+    configured = true;
+  }
+  stripe_sort_kernel<<<n_seq * heads, threads, smem, stream>>>(a);
+  return status_from_cuda(cudaGetLastError());
+}
+
+// ---------------------------------------------------------------------------
+// a10 selection. Keep set (sam.py:277-280): avg_rank over heads of
+// inv_perm_group, topk smallest keep_n. The key sum_h(rank) * N + token is
+// unique and orders exactly like (mean rank, token index).
+// ---------------------------------------------------------------------------
+__global__ void keep_select_kernel(const int32_t* inv_perm_group, int heads, int N, int keep_n, int32_t* idx,
+                                   int32_t* rows) {
+  extern __shared__ uint64_t s_key[];
+  const int b = blockIdx.x;
+  const int32_t* ipg = inv_perm_group + static_cast<int64_t>(b) * heads * N;
+  for (int t = threadIdx.x; t < N; t += blockDim.x) {
+    uint64_t s = 0;
+    for (int h = 0; h < heads; ++h) s += static_cast<uint64_t>(__ldg(ipg + static_cast<int64_t>(h) * N + t));
+    s_key[t] = s * static_cast<uint64_t>(N) + static_cast<uint64_t>(t);
+  }
+  __syncthreads();
+  for (int t = threadIdx.x; t < N; t += blockDim.x) {
+    const uint64_t kt = s_key[t];
+    int r = 0;
+    for (int u = 0; u < N; ++u) r += s_key[u] < kt;
+    if (r < keep_n) {
+      idx[static_cast<int64_t>(b) * keep_n + r] = t;
+      if (rows != nullptr) rows[static_cast<int64_t>(b) * keep_n + r] = b * N + t;
+    }
+  }
+}
+
+int keep_select(const int32_t* inv_perm_group, int B, int heads, int N, int keep_n, int32_t* idx, int32_t* rows,
+                cudaStream_t stream) {
+  if (inv_perm_group == nullptr || idx == nullptr) return SSAM_ERR_INVALID;
+  if (B <= 0 || heads <= 0 || N <= 0 || keep_n <= 0 || keep_n > N) return SSAM_ERR_INVALID;
+  if (N > kMaxTokens) return SSAM_ERR_UNSUPPORTED;
+  static bool configured = false;
+  if (!configured) {
+    if (cudaFuncSetAttribute(keep_select_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             kMaxTokens * sizeof(uint64_t)) != cudaSuccess)
+      return SSAM_ERR_CUDA;
+    configured = true;
+  }
+  keep_select_kernel<<<B, 1024, N * sizeof(uint64_t), stream>>>(inv_perm_group, heads, N, keep_n, idx, rows);
+  return status_from_cuda(cudaGetLastError());
+}
+
+// ---------------------------------------------------------------------------
+// a7. A-shape mask parameters (sam.py:219-223, flash_attn.py:132-145).
+// ---------------------------------------------------------------------------
+int a_shape_n_init(int N, int n_block, double ratio, int is_global) {
+  if (N <= 0 || n_block <= 0 || !(ratio > 0.0) || ratio > 1.0) return -1;
+  const int num_n = (N + n_block - 1) / n_block;
+  const int n_keep = static_cast<int>(ratio * num_n);  // Python int() truncates toward zero
+  return is_global ? n_keep : n_keep + 1;
+}
+
+int a_shape_mask(int N, int m_block, int n_block, int n_init, int with_diag, uint8_t* mask) {
+  if (N <= 0 || m_block <= 0 || n_block <= 0 || mask == nullptr) return SSAM_ERR_INVALID;
+  const int num_m = (N + m_block - 1) / m_block, num_n = (N + n_block - 1) / n_block;
+  for (int m = 0; m < num_m; ++m)
+    for (int n = 0; n < num_n; ++n) mask[m * num_n + n] = (n < n_init) || (with_diag && n == m);
+  return SSAM_OK;
+}
+
+}  // namespace ssam

@@ -1,0 +1,321 @@
+// Row-wise data movement around the GEMMs: gathered LayerNorm (norm1 +
+// window_partition, norm2 of the keep set), window row maps, the stem im2col,
+// the neck im2col / LayerNorm2d / NCHW transpose, and the Residual-Consistency
+// MLP composite. These kernels are HBM-bound: vectorised 16-byte accesses,
+// one warp per row, no shared-memory staging needed.
+#include "common.cuh"
+#include "host_util.h"
+
+namespace ssam {
+
+// ---------------------------------------------------------------------------
+// LayerNorm over rows, optionally gathered through src_rows (-1 -> zero row).
+// One warp per output row; the row lives in registers as float4 chunks.
+// Matches torch.nn.LayerNorm: biased variance, (x - mean) * rsqrt(var + eps).
+// ---------------------------------------------------------------------------
+template <int CHUNKS, bool OUT_BF16>
+__global__ void layernorm_rows_kernel(const float* __restrict__ x, int64_t ldx, const int32_t* __restrict__ src_rows,
+                                      int n_rows, int C, const float* __restrict__ w, const float* __restrict__ b,
+                                      float eps, void* __restrict__ out, int64_t ld_out) {
+  const int warps_per_block = blockDim.x >> 5;
+  const int r = blockIdx.x * warps_per_block + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (r >= n_rows) return;
+  const int src = src_rows != nullptr ? __ldg(src_rows + r) : r;
+  const int nc4 = C >> 2;
+  if (src < 0) {
+    for (int i = lane; i < nc4; i += 32) {
+      if constexpr (OUT_BF16) {
+        reinterpret_cast<uint2*>(static_cast<__nv_bfloat16*>(out) + static_cast<int64_t>(r) * ld_out)[i] =
+            make_uint2(0u, 0u);
+      } else {
+        reinterpret_cast<float4*>(static_cast<float*>(out) + static_cast<int64_t>(r) * ld_out)[i] =
+            make_float4(0.f, 0.f, 0.f, 0.f);
+      }
+    }
+    return;
+  }
+  const float4* xr = reinterpret_cast<const float4*>(x + static_cast<int64_t>(src) * ldx);
+  float4 v[CHUNKS];
+  float s = 0.f;
+#pragma unroll
+  for (int i = 0; i < CHUNKS; ++i) {
+    const int c = lane + 32 * i;
+    v[i] = c < nc4 ? __ldg(xr + c) : make_float4(0.f, 0.f, 0.f, 0.f);
+    s += (v[i].x + v[i].y) + (v[i].z + v[i].w);
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+  const float mean = s / C;
+  float q = 0.f;
+#pragma unroll
+  for (int i = 0; i < CHUNKS; ++i) {
+    const int c = lane + 32 * i;
+    if (c < nc4) {
+      const float a0 = v[i].x - mean, a1 = v[i].y - mean, a2 = v[i].z - mean, a3 = v[i].w - mean;
+      q += (a0 * a0 + a1 * a1) + (a2 * a2 + a3 * a3);
+    }
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) q += __shfl_xor_sync(0xffffffffu, q, o);
+  const float rstd = rsqrtf(q / C + eps);
+  const float4* w4 = reinterpret_cast<const float4*>(w);
+  const float4* b4 = reinterpret_cast<const float4*>(b);
+#pragma unroll
+  for (int i = 0; i < CHUNKS; ++i) {
+    const int c = lane + 32 * i;
+    if (c < nc4) {
+      const float4 ww = __ldg(w4 + c), bb = __ldg(b4 + c);
+      const float y0 = (v[i].x - mean) * rstd * ww.x + bb.x;
+      const float y1 = (v[i].y - mean) * rstd * ww.y + bb.y;
+      const float y2 = (v[i].z - mean) * rstd * ww.z + bb.z;
+      const float y3 = (v[i].w - mean) * rstd * ww.w + bb.w;
+      if constexpr (OUT_BF16) {
+        reinterpret_cast<uint2*>(static_cast<__nv_bfloat16*>(out) + static_cast<int64_t>(r) * ld_out)[c] =
+            make_uint2(pack_bf16x2(y0, y1), pack_bf16x2(y2, y3));
+      } else {
+        reinterpret_cast<float4*>(static_cast<float*>(out) + static_cast<int64_t>(r) * ld_out)[c] =
+            make_float4(y0, y1, y2, y3);
+      }
+    }
+  }
+}
+
+template <bool OUT_BF16>
+static int launch_layernorm(const float* x, int64_t ldx, const int32_t* src_rows, int n_rows, int C, const float* w,
+                            const float* b, float eps, void* out, int64_t ld_out, cudaStream_t stream) {
+  const int nc4 = C / 4;
+  const int chunks = (nc4 + 31) / 32;
+  const int wpb = 8;
+  const dim3 grid((n_rows + wpb - 1) / wpb), block(32 * wpb);
+#define SSAM_LN_CASE(K)                                                                                           \
+  case K:                                                                                                         \
+    layernorm_rows_kernel<K, OUT_BF16><<<grid, block, 0, stream>>>(x, ldx, src_rows, n_rows, C, w, b, eps, out, \
+                                                                   ld_out);                                       \
+    break;
+  switch (chunks) {
+    SSAM_LN_CASE(1)
+    SSAM_LN_CASE(2)
+    SSAM_LN_CASE(4)
+    SSAM_LN_CASE(8)
+    SSAM_LN_CASE(16)
+    case 3:
+      layernorm_rows_kernel<4, OUT_BF16><<<grid, block, 0, stream>>>(x, ldx, src_rows, n_rows, C, w, b, eps, out,
+                                                                     ld_out);
+      break;
+    case 5: case 6: case 7:
+      layernorm_rows_kernel<8, OUT_BF16><<<grid, block, 0, stream>>>(x, ldx, src_rows, n_rows, C, w, b, eps, out,
+                                                                     ld_out);
+      break;
+    default:
+      if (chunks > 16) return SSAM_ERR_UNSUPPORTED;
+      layernorm_rows_kernel<16, OUT_BF16><<<grid, block, 0, stream>>>(x, ldx, src_rows, n_rows, C, w, b, eps, out,
+                                                                      ld_out);
+  }
+#undef SSAM_LN_CASE
+  return status_from_cuda(cudaGetLastError());
+}
+
+int layernorm_gather(const float* x, int64_t ldx, const int32_t* src_rows, int n_rows, int C, const float* w,
+                     const float* b, float eps, void* out, int64_t ld_out, cudaStream_t stream) {
+  if (x == nullptr || w == nullptr || b == nullptr || out == nullptr || n_rows < 0 || C <= 0) return SSAM_ERR_INVALID;
+  if (n_rows == 0) return SSAM_OK;
+  if (C % 4 || ldx % 4 || ld_out % 4 || ldx < C || ld_out < C) return SSAM_ERR_ALIGN;
+  if (!aligned16(x) || !aligned16(w) || !aligned16(b) || (reinterpret_cast<uintptr_t>(out) & 7)) return SSAM_ERR_ALIGN;
+  return launch_layernorm<true>(x, ldx, src_rows, n_rows, C, w, b, eps, out, ld_out, stream);
+}
+
+int layernorm_rows(const float* x, int n_rows, int C, const float* w, const float* b, float eps, void* out,
+                   int out_bf16, cudaStream_t stream) {
+  if (x == nullptr || w == nullptr || b == nullptr || out == nullptr || n_rows < 0 || C <= 0) return SSAM_ERR_INVALID;
+  if (n_rows == 0) return SSAM_OK;
+  if (C % 4 || !aligned16(x) || !aligned16(w) || !aligned16(b) || !aligned16(out)) return SSAM_ERR_ALIGN;
+  return out_bf16 ? launch_layernorm<true>(x, C, nullptr, n_rows, C, w, b, eps, out, C, stream)
+                  : launch_layernorm<false>(x, C, nullptr, n_rows, C, w, b, eps, out, C, stream);
+}
+
+// ---------------------------------------------------------------------------
+// window_partition row map (host image_encoder window_partition, used at
+// algos/sparsesam/sam.py:252 and :256).
+// ---------------------------------------------------------------------------
+__global__ void window_rows_kernel(int B, int H, int W, int ws, int nwh, int nww, int32_t* rows) {
+  const int64_t total = static_cast<int64_t>(B) * nwh * nww * ws * ws;
+  const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (i >= total) return;
+  const int t = static_cast<int>(i % (ws * ws));
+  const int64_t win = i / (ws * ws);
+  const int wx = static_cast<int>(win % nww);
+  const int wy = static_cast<int>((win / nww) % nwh);
+  const int b = static_cast<int>(win / (static_cast<int64_t>(nww) * nwh));
+  const int y = wy * ws + t / ws, x = wx * ws + t % ws;
+  rows[i] = (y < H && x < W) ? b * H * W + y * W + x : -1;
+}
+
+int window_rows(int B, int H, int W, int ws, int32_t* rows, cudaStream_t stream) {
+  if (B <= 0 || H <= 0 || W <= 0 || ws <= 0 || rows == nullptr) return SSAM_ERR_INVALID;
+  const int nwh = (H + ws - 1) / ws, nww = (W + ws - 1) / ws;
+  const int64_t total = static_cast<int64_t>(B) * nwh * nww * ws * ws;
+  if (total > INT32_MAX) return SSAM_ERR_UNSUPPORTED;
+  window_rows_kernel<<<static_cast<unsigned>((total + 255) / 256), 256, 0, stream>>>(B, H, W, ws, nwh, nww, rows);
+  return status_from_cuda(cudaGetLastError());
+}
+
+// ---------------------------------------------------------------------------
+// Stem / neck helpers.
+// ---------------------------------------------------------------------------
+// One thread per (output row, cin, ky): copies p contiguous pixels.
+__global__ void patch_im2col_kernel(const float* __restrict__ img, int B, int Cin, int H, int W, int p,
+                                    __nv_bfloat16* __restrict__ out) {
+  const int gh = H / p, gw = W / p;
+  const int64_t total = static_cast<int64_t>(B) * gh * gw * Cin * p;
+  const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (i >= total) return;
+  const int ky = static_cast<int>(i % p);
+  const int cin = static_cast<int>((i / p) % Cin);
+  const int64_t tok = i / (static_cast<int64_t>(p) * Cin);
+  const int px = static_cast<int>(tok % gw), py = static_cast<int>((tok / gw) % gh);
+  const int b = static_cast<int>(tok / (static_cast<int64_t>(gw) * gh));
+  const float* src = img + ((static_cast<int64_t>(b) * Cin + cin) * H + (py * p + ky)) * W + px * p;
+  __nv_bfloat16* dst = out + tok * (static_cast<int64_t>(Cin) * p * p) + (cin * p + ky) * p;
+  for (int kx = 0; kx < p; kx += 2) {
+    const float2 v = *reinterpret_cast<const float2*>(src + kx);
+    *reinterpret_cast<uint32_t*>(dst + kx) = pack_bf16x2(v.x, v.y);
+  }
+}
+
+int patch_im2col(const float* img, int B, int Cin, int H, int W, int p, void* out, cudaStream_t stream) {
+  if (img == nullptr || out == nullptr || B <= 0 || Cin <= 0 || p <= 0 || H % p || W % p) return SSAM_ERR_INVALID;
+  if (p % 2 || (reinterpret_cast<uintptr_t>(img) & 7) || (reinterpret_cast<uintptr_t>(out) & 3)) return SSAM_ERR_ALIGN;
+  const int64_t total = static_cast<int64_t>(B) * (H / p) * (W / p) * Cin * p;
+  patch_im2col_kernel<<<static_cast<unsigned>((total + 255) / 256), 256, 0, stream>>>(
+      img, B, Cin, H, W, p, static_cast<__nv_bfloat16*>(out));
+  return status_from_cuda(cudaGetLastError());
+}
+
+__global__ void broadcast_rows_kernel(const float4* __restrict__ pos, int64_t per_image4, int64_t total4,
+                                      float4* __restrict__ x) {
+  const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (i < total4) x[i] = __ldg(pos + i % per_image4);
+}
+
+int broadcast_rows(const float* pos, int B, int T, int C, float* x, cudaStream_t stream) {
+  if (pos == nullptr || x == nullptr || B <= 0 || T <= 0 || C <= 0) return SSAM_ERR_INVALID;
+  if (C % 4 || !aligned16(pos) || !aligned16(x)) return SSAM_ERR_ALIGN;
+  const int64_t per = static_cast<int64_t>(T) * C / 4, total = per * B;
+  broadcast_rows_kernel<<<static_cast<unsigned>((total + 255) / 256), 256, 0, stream>>>(
+      reinterpret_cast<const float4*>(pos), per, total, reinterpret_cast<float4*>(x));
+  return status_from_cuda(cudaGetLastError());
+}
+
+// 3x3 / pad 1 im2col, channels-last, (ky, kx, c) column order; 8 channels per thread.
+__global__ void im2col3x3_kernel(const __nv_bfloat16* __restrict__ in, int B, int H, int W, int C,
+                                 __nv_bfloat16* __restrict__ out) {
+  const int c8 = C / 8;
+  const int64_t total = static_cast<int64_t>(B) * H * W * 9 * c8;
+  const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (i >= total) return;
+  const int cc = static_cast<int>(i % c8);
+  const int tap = static_cast<int>((i / c8) % 9);
+  const int64_t pix = i / (static_cast<int64_t>(c8) * 9);
+  const int x = static_cast<int>(pix % W), y = static_cast<int>((pix / W) % H);
+  const int b = static_cast<int>(pix / (static_cast<int64_t>(W) * H));
+  const int yy = y + tap / 3 - 1, xx = x + tap % 3 - 1;
+  uint4 v = make_uint4(0u, 0u, 0u, 0u);
+  if (yy >= 0 && yy < H && xx >= 0 && xx < W)
+    v = __ldg(reinterpret_cast<const uint4*>(in + ((static_cast<int64_t>(b) * H + yy) * W + xx) * C) + cc);
+  reinterpret_cast<uint4*>(out + pix * (9 * static_cast<int64_t>(C)) + tap * C)[cc] = v;
+}
+
+int im2col3x3_nhwc(const void* in, int B, int H, int W, int C, void* out, cudaStream_t stream) {
+  if (in == nullptr || out == nullptr || B <= 0 || H <= 0 || W <= 0 || C <= 0) return SSAM_ERR_INVALID;
+  if (C % 8 || !aligned16(in) || !aligned16(out)) return SSAM_ERR_ALIGN;
+  const int64_t total = static_cast<int64_t>(B) * H * W * 9 * (C / 8);
+  im2col3x3_kernel<<<static_cast<unsigned>((total + 255) / 256), 256, 0, stream>>>(
+      static_cast<const __nv_bfloat16*>(in), B, H, W, C, static_cast<__nv_bfloat16*>(out));
+  return status_from_cuda(cudaGetLastError());
+}
+
+// (B, HW, C) -> (B, C, HW), 32x32 tiles through shared memory.
+__global__ void nhwc_to_nchw_kernel(const float* __restrict__ in, int HW, int C, float* __restrict__ out) {
+  __shared__ float tile[32][33];
+  const int b = blockIdx.z;
+  const int p0 = blockIdx.x * 32, c0 = blockIdx.y * 32;
+  const float* src = in + static_cast<int64_t>(b) * HW * C;
+  float* dst = out + static_cast<int64_t>(b) * HW * C;
+  for (int j = threadIdx.y; j < 32; j += blockDim.y) {
+    const int p = p0 + j, c = c0 + threadIdx.x;
+    if (p < HW && c < C) tile[j][threadIdx.x] = src[static_cast<int64_t>(p) * C + c];
+  }
+  __syncthreads();
+  for (int j = threadIdx.y; j < 32; j += blockDim.y) {
+    const int c = c0 + j, p = p0 + threadIdx.x;
+    if (p < HW && c < C) dst[static_cast<int64_t>(c) * HW + p] = tile[threadIdx.x][j];
+  }
+}
+
+int nhwc_to_nchw(const float* in, int B, int HW, int C, float* out, cudaStream_t stream) {
+  if (in == nullptr || out == nullptr || B <= 0 || HW <= 0 || C <= 0) return SSAM_ERR_INVALID;
+  const dim3 grid((HW + 31) / 32, (C + 31) / 32, B), block(32, 8);
+  nhwc_to_nchw_kernel<<<grid, block, 0, stream>>>(in, HW, C, out);
+  return status_from_cuda(cudaGetLastError());
+}
+
+// hi/lo bf16 split of fp32 rows: out[r] = [bf16(x) | bf16(x - bf16(x))] (2C columns).
+// A GEMM over the split operand against a duplicated weight [W | W] reproduces the
+// fp32 activation to ~2^-16 relative (used by the neck, right before LayerNorm2d).
+__global__ void split_bf16x2_kernel(const float4* __restrict__ x, int64_t n4, int c4, uint2* __restrict__ out) {
+  const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (i >= n4) return;
+  const int64_t r = i / c4;
+  const int c = static_cast<int>(i - r * c4);
+  const float4 v = __ldg(x + i);
+  const __nv_bfloat16 h0 = __float2bfloat16_rn(v.x), h1 = __float2bfloat16_rn(v.y);
+  const __nv_bfloat16 h2 = __float2bfloat16_rn(v.z), h3 = __float2bfloat16_rn(v.w);
+  uint2* row = out + r * 2 * c4;
+  row[c] = make_uint2(pack_bf16x2(__bfloat162float(h0), __bfloat162float(h1)),
+                      pack_bf16x2(__bfloat162float(h2), __bfloat162float(h3)));
+  row[c4 + c] = make_uint2(pack_bf16x2(v.x - __bfloat162float(h0), v.y - __bfloat162float(h1)),
+                           pack_bf16x2(v.z - __bfloat162float(h2), v.w - __bfloat162float(h3)));
+}
+
+int split_bf16x2(const float* x, int n_rows, int C, void* out, cudaStream_t stream) {
+  if (x == nullptr || out == nullptr || n_rows < 0 || C <= 0) return SSAM_ERR_INVALID;
+  if (n_rows == 0) return SSAM_OK;
+  if (C % 4 || !aligned16(x) || (reinterpret_cast<uintptr_t>(out) & 7)) return SSAM_ERR_ALIGN;
+  const int64_t n4 = static_cast<int64_t>(n_rows) * (C / 4);
+  split_bf16x2_kernel<<<static_cast<unsigned>((n4 + 255) / 256), 256, 0, stream>>>(
+      reinterpret_cast<const float4*>(x), n4, C / 4, static_cast<uint2*>(out));
+  return status_from_cuda(cudaGetLastError());
+}
+
+// ---------------------------------------------------------------------------
+// Residual-Consistency MLP (algos/sparsesam/sam.py:281-288):
+//   xk = LN(x[rows]) (bf16) ; h = gelu(xk W1^T + b1) ; x[rows] += h W2^T + b2
+// ---------------------------------------------------------------------------
+static size_t align256(size_t v) { return (v + 255) & ~static_cast<size_t>(255); }
+
+size_t rc_mlp_workspace_size(int n_rows, int C, int hidden) {
+  if (n_rows <= 0 || C <= 0 || hidden <= 0) return 0;
+  return align256(static_cast<size_t>(n_rows) * C * 2) + align256(static_cast<size_t>(n_rows) * hidden * 2);
+}
+
+int rc_mlp_fwd(float* x, int64_t ldx, const int32_t* rows, int n_rows, int C, int hidden, const float* ln_w,
+               const float* ln_b, float eps, const void* w1, const float* b1, const void* w2, const float* b2,
+               void* workspace, size_t workspace_bytes, cudaStream_t stream) {
+  if (x == nullptr || ln_w == nullptr || ln_b == nullptr || w1 == nullptr || w2 == nullptr) return SSAM_ERR_INVALID;
+  if (n_rows < 0 || C <= 0 || hidden <= 0) return SSAM_ERR_INVALID;
+  if (n_rows == 0) return SSAM_OK;
+  const size_t need = rc_mlp_workspace_size(n_rows, C, hidden);
+  if (workspace == nullptr || workspace_bytes < need) return SSAM_ERR_INVALID;
+  if (!aligned16(workspace)) return SSAM_ERR_ALIGN;
+  uint8_t* ws = static_cast<uint8_t*>(workspace);
+  void* xk = ws;
+  void* h = ws + align256(static_cast<size_t>(n_rows) * C * 2);
+  int st = layernorm_gather(x, ldx, rows, n_rows, C, ln_w, ln_b, eps, xk, C, stream);
+  if (st != SSAM_OK) return st;
+  st = gemm_bf16(xk, C, w1, C, n_rows, hidden, C, b1, SSAM_EPI_GELU_BF16, h, hidden, nullptr, stream);
+  if (st != SSAM_OK) return st;
+  return gemm_bf16(h, hidden, w2, hidden, n_rows, C, hidden, b2, SSAM_EPI_ADD_F32, x, ldx, rows, stream);
+}
+
+}  // namespace ssam

@@ -1,0 +1,333 @@
+"""Torch-facing wrappers over the C ABI (include/sparsesam.h).
+
+Each wrapper checks dtypes/devices/contiguity, passes raw device pointers and
+torch's current CUDA stream to the shared library, and raises SparseSAMError on
+a non-zero status. There is no CPU or PyTorch fallback: a tensor that is not on
+a CUDA device is rejected.
+"""
+from __future__ import annotations
+
+import torch
+
+from . import _lib
+from ._lib import SSAM_EPI_ADD_F32, SSAM_EPI_BF16, SSAM_EPI_F32, SSAM_EPI_GELU_BF16  # noqa: F401
+
+
+class KernelTimer:
+    """Optional CUDA-event timing of GEMM / attention launches on the launching
+    stream. Inactive by default; bench.py turns it on to measure per-kernel time."""
+
+    active = False
+    records: list = []   # (kind, flops, start_event, end_event)
+
+    @classmethod
+    def begin(cls):
+        if not cls.active:
+            return None
+        ev = torch.cuda.Event(enable_timing=True)
+        ev.record()
+        return ev
+
+    @classmethod
+    def end(cls, start, kind: str, flops: float):
+        if start is None:
+            return
+        ev = torch.cuda.Event(enable_timing=True)
+        ev.record()
+        cls.records.append((kind, flops, start, ev))
+
+
+def _stream(t: torch.Tensor) -> int:
+    return torch.cuda.current_stream(t.device).cuda_stream
+
+
+def _check_cuda(*ts: torch.Tensor) -> None:
+    for t in ts:
+        if t is not None and not t.is_cuda:
+            raise ValueError("sparsesam_b200 ops run on CUDA tensors only (no CPU fallback)")
+
+
+def _ptr(t: torch.Tensor | None) -> int | None:
+    return None if t is None else t.data_ptr()
+
+
+def _rowmajor(t: torch.Tensor, name: str) -> int:
+    if t.dim() != 2 or t.stride(1) != 1:
+        raise ValueError(f"{name} must be a 2-D row-major tensor (unit column stride)")
+    return t.stride(0)
+
+
+def gemm_bf16(a: torch.Tensor, b: torch.Tensor, bias: torch.Tensor | None = None, *,
+              epilogue: int = SSAM_EPI_BF16, out: torch.Tensor | None = None,
+              out_rows: torch.Tensor | None = None) -> torch.Tensor:
+    """acc = a @ b.T (a: M x K bf16, b: N x K bf16) with a fused epilogue.
+
+    SSAM_EPI_BF16 / SSAM_EPI_GELU_BF16 write bf16 `out` (M x N, allocated when
+    None). SSAM_EPI_ADD_F32 accumulates into the fp32 `out` rows given by
+    `out_rows` (int32, -1 skips the row).
+    """
+    _check_cuda(a, b, bias, out, out_rows)
+    if a.dtype != torch.bfloat16 or b.dtype != torch.bfloat16:
+        raise TypeError("gemm_bf16 takes bf16 operands")
+    M, K = a.shape
+    N, K2 = b.shape
+    if K != K2:
+        raise ValueError(f"inner dimensions differ: {K} vs {K2}")
+    lda, ldb = _rowmajor(a, "a"), _rowmajor(b, "b")
+    if bias is not None and (bias.dtype != torch.float32 or bias.numel() != N or not bias.is_contiguous()):
+        raise ValueError("bias must be a contiguous fp32 vector of length N")
+    if epilogue == SSAM_EPI_F32:
+        if out is None:
+            out = torch.empty(M, N, device=a.device, dtype=torch.float32)
+        elif out.dtype != torch.float32 or out.shape[0] < M:
+            raise ValueError("out must be fp32 with at least M rows")
+    elif epilogue == SSAM_EPI_ADD_F32:
+        if out is None or out.dtype != torch.float32:
+            raise ValueError("SSAM_EPI_ADD_F32 needs an fp32 `out`")
+        if out_rows is not None and (out_rows.dtype != torch.int32 or out_rows.numel() < M):
+            raise ValueError("out_rows must be int32 with at least M entries")
+        if out_rows is None and out.shape[0] < M:
+            raise ValueError("out has fewer than M rows")
+    else:
+        if out is None:
+            out = torch.empty(M, N, device=a.device, dtype=torch.bfloat16)
+        elif out.dtype != torch.bfloat16 or out.shape[0] < M:
+            raise ValueError("out must be bf16 with at least M rows")
+    ldo = _rowmajor(out, "out")
+    t0 = KernelTimer.begin()
+    _lib.call("ssam_gemm_bf16", a.data_ptr(), lda, b.data_ptr(), ldb, M, N, K, _ptr(bias), epilogue,
+              out.data_ptr(), ldo, _ptr(out_rows), _stream(a))
+    KernelTimer.end(t0, "gemm", 2.0 * M * N * K)
+    return out
+
+
+def device_error(reset: bool = True) -> int:
+    """Synchronise and return (optionally clearing) the library's device error flag."""
+    return _lib.load().ssam_device_error(1 if reset else 0)
+
+
+# ---------------------------------------------------------------------------
+# Token order (a1, a2), mask parameters (a7), keep set (a10)
+# ---------------------------------------------------------------------------
+def zorder(H: int, W: int, device) -> tuple[torch.Tensor, torch.Tensor]:
+    """Morton order of an H x W grid: (perm, inv_perm), int32 on `device`."""
+    perm = torch.empty(H * W, dtype=torch.int32, device=device)
+    inv = torch.empty_like(perm)
+    _lib.call("ssam_zorder", H, W, perm.data_ptr(), inv.data_ptr(), torch.cuda.current_stream(perm.device).cuda_stream)
+    return perm, inv
+
+
+_LAYOUTS = {"interleave": 0, "naive": 1}
+_RANKINGS = {"sort": 0, "nosort": 1}
+
+
+def parse_perm_mode(perm_mode: str) -> tuple[str, int, int]:
+    """`<space>_<layout>_<ranking>` -> (space, layout code, ranking code) (sam.py:118-123)."""
+    parts = perm_mode.split("_")
+    if len(parts) != 3:
+        raise ValueError(f"perm_mode must be <space>_<layout>_<ranking>, got {perm_mode!r}")
+    space, layout, ranking = parts
+    if space not in ("z", "hilbert"):
+        raise ValueError(f"unknown space {space!r}")
+    if layout not in _LAYOUTS:
+        raise ValueError(f"unknown layout {layout!r}")
+    if ranking not in _RANKINGS:
+        raise ValueError(f"unknown ranking {ranking!r}")
+    return space, _LAYOUTS[layout], _RANKINGS[ranking]
+
+
+def stripe_sort_perm(k: torch.Tensor, n_seq: int, heads: int, H: int, W: int, d: int, base_perm: torch.Tensor,
+                     group_size: int = 4, layout: int = 0, ranking: int = 0, ld: int | None = None):
+    """Stripe-Sort permutation of every (sequence, head) row of K.
+
+    `k` addresses K as k[(s*H*W + t)*ld + h*d + c] (a column view into a qkv
+    buffer works). Returns int32 (perm, inv_perm, inv_perm_group) of shape
+    (n_seq*heads, H*W)."""
+    _check_cuda(k, base_perm)
+    if k.dtype != torch.bfloat16 or base_perm.dtype != torch.int32:
+        raise TypeError("k must be bf16 and base_perm int32")
+    if ld is None:
+        ld = k.stride(0) if k.dim() == 2 else heads * d
+    rows, N = n_seq * heads, H * W
+    perm = torch.empty(rows, N, dtype=torch.int32, device=k.device)
+    inv = torch.empty_like(perm)
+    inv_g = torch.empty_like(perm)
+    _lib.call("ssam_stripe_sort_perm", k.data_ptr(), ld, n_seq, heads, H, W, d, group_size, layout, ranking,
+              base_perm.data_ptr(), perm.data_ptr(), inv.data_ptr(), inv_g.data_ptr(), _stream(k))
+    return perm, inv, inv_g
+
+
+def a_shape_n_init(N: int, n_block: int, ratio: float, is_global: bool) -> int:
+    v = _lib.load().ssam_a_shape_n_init(N, n_block, float(ratio), 1 if is_global else 0)
+    if v < 0:
+        raise ValueError(f"invalid A-shape parameters N={N} n_block={n_block} ratio={ratio}")
+    return v
+
+
+def a_shape_mask(N: int, m_block: int, n_block: int, n_init: int, with_diag: bool) -> torch.Tensor:
+    num_m, num_n = -(-N // m_block), -(-N // n_block)
+    mask = torch.empty(num_m, num_n, dtype=torch.uint8)
+    _lib.call("ssam_a_shape_mask", N, m_block, n_block, n_init, 1 if with_diag else 0, mask.data_ptr())
+    return mask
+
+
+def keep_select(inv_perm_group: torch.Tensor, B: int, heads: int, keep_n: int):
+    """(idx (B, keep_n), rows (B*keep_n,)) of the Residual-Consistency keep set."""
+    _check_cuda(inv_perm_group)
+    if inv_perm_group.dtype != torch.int32 or not inv_perm_group.is_contiguous():
+        raise TypeError("inv_perm_group must be contiguous int32")
+    N = inv_perm_group.shape[-1]
+    idx = torch.empty(B, keep_n, dtype=torch.int32, device=inv_perm_group.device)
+    rows = torch.empty(B * keep_n, dtype=torch.int32, device=inv_perm_group.device)
+    _lib.call("ssam_keep_select", inv_perm_group.data_ptr(), B, heads, N, keep_n, idx.data_ptr(), rows.data_ptr(),
+              _stream(inv_perm_group))
+    return idx, rows
+
+
+# ---------------------------------------------------------------------------
+# Attention (a3-a6, a8)
+# ---------------------------------------------------------------------------
+def sparse_attn(qkv: torch.Tensor, n_seq: int, heads: int, win: int, d: int, rel_pos_h: torch.Tensor,
+                rel_pos_w: torch.Tensor, perm: torch.Tensor, n_init_blocks: int, with_diag: bool, scale: float,
+                out: torch.Tensor | None = None) -> torch.Tensor:
+    """Block-sparse attention of every (sequence, head) row; output in raster order (n_seq*N, heads*d)."""
+    _check_cuda(qkv, rel_pos_h, rel_pos_w, perm, out)
+    if qkv.dtype != torch.bfloat16 or rel_pos_h.dtype != torch.bfloat16 or rel_pos_w.dtype != torch.bfloat16:
+        raise TypeError("qkv and rel-pos tables must be bf16")
+    if perm.dtype != torch.int32 or not perm.is_contiguous():
+        raise TypeError("perm must be contiguous int32")
+    if not (rel_pos_h.is_contiguous() and rel_pos_w.is_contiguous()):
+        raise ValueError("rel-pos tables must be contiguous")
+    ld = _rowmajor(qkv, "qkv")
+    N = win * win
+    if out is None:
+        out = torch.empty(n_seq * N, heads * d, dtype=torch.bfloat16, device=qkv.device)
+    ld_out = _rowmajor(out, "out")
+    t0 = KernelTimer.begin()
+    _lib.call("ssam_sparse_attn_fwd", qkv.data_ptr(), ld, n_seq, heads, win, d, rel_pos_h.data_ptr(),
+              rel_pos_w.data_ptr(), perm.data_ptr(), n_init_blocks, 1 if with_diag else 0, float(scale),
+              out.data_ptr(), ld_out, _stream(qkv))
+    KernelTimer.end(t0, "attention", attention_flops(n_seq * heads, N, d, n_init_blocks, with_diag))
+    return out
+
+
+def attention_flops(rows: int, N: int, d: int, n_init: int, with_diag: bool, block: int = 64) -> float:
+    """4*d per enabled (query, key) pair: QK^T and PV of the A-shape mask over N tokens."""
+    nb = -(-N // block)
+    pairs = 0
+    for m in range(nb):
+        q = min(block, N - m * block)
+        keys = min(n_init, nb) * block
+        keys = min(keys, N)
+        if with_diag and m >= n_init:
+            keys += min(block, N - m * block)
+        pairs += q * keys
+    return 4.0 * d * rows * pairs
+
+
+# ---------------------------------------------------------------------------
+# Rows: LayerNorm gathers, window maps, RC-MLP, stem/neck helpers
+# ---------------------------------------------------------------------------
+def layernorm_gather(x: torch.Tensor, w: torch.Tensor, b: torch.Tensor, eps: float,
+                     src_rows: torch.Tensor | None = None, n_rows: int | None = None,
+                     out: torch.Tensor | None = None) -> torch.Tensor:
+    """bf16 LN(x[src_rows]) (zero rows where src_rows < 0); x is fp32 (rows, C)."""
+    _check_cuda(x, w, b, src_rows, out)
+    if x.dtype != torch.float32 or w.dtype != torch.float32 or b.dtype != torch.float32:
+        raise TypeError("layernorm_gather takes fp32 x / w / b")
+    x2 = x.reshape(-1, x.shape[-1])
+    C = x2.shape[1]
+    ldx = _rowmajor(x2, "x")
+    if n_rows is None:
+        n_rows = src_rows.numel() if src_rows is not None else x2.shape[0]
+    if out is None:
+        out = torch.empty(n_rows, C, dtype=torch.bfloat16, device=x.device)
+    _lib.call("ssam_layernorm_gather", x2.data_ptr(), ldx, _ptr(src_rows), n_rows, C, w.data_ptr(), b.data_ptr(),
+              float(eps), out.data_ptr(), _rowmajor(out, "out"), _stream(x))
+    return out
+
+
+def window_rows(B: int, H: int, W: int, ws: int, device) -> torch.Tensor:
+    nwh, nww = -(-H // ws), -(-W // ws)
+    rows = torch.empty(B * nwh * nww * ws * ws, dtype=torch.int32, device=device)
+    _lib.call("ssam_window_rows", B, H, W, ws, rows.data_ptr(), torch.cuda.current_stream(rows.device).cuda_stream)
+    return rows
+
+
+def rc_mlp_workspace_size(n_rows: int, C: int, hidden: int) -> int:
+    return int(_lib.load().ssam_rc_mlp_workspace_size(n_rows, C, hidden))
+
+
+def rc_mlp(x: torch.Tensor, rows: torch.Tensor | None, n_rows: int, ln_w, ln_b, eps: float, w1, b1, w2, b2,
+           workspace: torch.Tensor | None = None) -> torch.Tensor:
+    """In place: x[rows] += lin2(gelu(lin1(LN(x[rows])))) (rows None -> first n_rows rows)."""
+    _check_cuda(x, rows, ln_w, ln_b, w1, b1, w2, b2, workspace)
+    x2 = x.view(-1, x.shape[-1])
+    C = x2.shape[1]
+    hidden = w1.shape[0]
+    need = rc_mlp_workspace_size(n_rows, C, hidden)
+    if workspace is None or workspace.numel() * workspace.element_size() < need:
+        workspace = torch.empty(need, dtype=torch.uint8, device=x.device)
+    _lib.call("ssam_rc_mlp_fwd", x2.data_ptr(), _rowmajor(x2, "x"), _ptr(rows), n_rows, C, hidden, ln_w.data_ptr(),
+              ln_b.data_ptr(), float(eps), w1.data_ptr(), _ptr(b1), w2.data_ptr(), _ptr(b2), workspace.data_ptr(),
+              workspace.numel() * workspace.element_size(), _stream(x))
+    return x
+
+
+def patch_im2col(img: torch.Tensor, p: int, out: torch.Tensor | None = None) -> torch.Tensor:
+    _check_cuda(img, out)
+    img = img.contiguous().float()
+    B, Cin, H, W = img.shape
+    if out is None:
+        out = torch.empty(B * (H // p) * (W // p), Cin * p * p, dtype=torch.bfloat16, device=img.device)
+    _lib.call("ssam_patch_im2col", img.data_ptr(), B, Cin, H, W, p, out.data_ptr(), _stream(img))
+    return out
+
+
+def broadcast_rows(pos: torch.Tensor, B: int, out: torch.Tensor) -> torch.Tensor:
+    _check_cuda(pos, out)
+    T, C = pos.shape[-3] * pos.shape[-2] if pos.dim() == 4 else pos.shape[0], pos.shape[-1]
+    _lib.call("ssam_broadcast_rows", pos.data_ptr(), B, T, C, out.data_ptr(), _stream(out))
+    return out
+
+
+def im2col3x3_nhwc(x: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
+    _check_cuda(x, out)
+    B, H, W, C = x.shape
+    if out is None:
+        out = torch.empty(B * H * W, 9 * C, dtype=torch.bfloat16, device=x.device)
+    _lib.call("ssam_im2col3x3_nhwc", x.data_ptr(), B, H, W, C, out.data_ptr(), _stream(x))
+    return out
+
+
+def nhwc_to_nchw(x: torch.Tensor, B: int, H: int, W: int, C: int, out: torch.Tensor | None = None) -> torch.Tensor:
+    _check_cuda(x, out)
+    if out is None:
+        out = torch.empty(B, C, H, W, dtype=torch.float32, device=x.device)
+    _lib.call("ssam_nhwc_to_nchw", x.data_ptr(), B, H * W, C, out.data_ptr(), _stream(x))
+    return out
+
+
+def layernorm_rows(x: torch.Tensor, w: torch.Tensor, b: torch.Tensor, eps: float, out_bf16: bool,
+                   out: torch.Tensor | None = None) -> torch.Tensor:
+    _check_cuda(x, w, b, out)
+    x2 = x.reshape(-1, x.shape[-1])
+    n, C = x2.shape
+    if out is None:
+        out = torch.empty(n, C, dtype=torch.bfloat16 if out_bf16 else torch.float32, device=x.device)
+    _lib.call("ssam_layernorm_rows", x2.data_ptr(), n, C, w.data_ptr(), b.data_ptr(), float(eps), out.data_ptr(),
+              1 if out_bf16 else 0, _stream(x))
+    return out
+
+
+def split_bf16x2(x: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
+    """fp32 (rows, C) -> bf16 (rows, 2C) = [hi | lo] with hi + lo ~= x."""
+    _check_cuda(x, out)
+    x2 = x.reshape(-1, x.shape[-1])
+    if x2.dtype != torch.float32 or not x2.is_contiguous():
+        raise TypeError("split_bf16x2 takes a contiguous fp32 tensor")
+    n, C = x2.shape
+    if out is None:
+        out = torch.empty(n, 2 * C, dtype=torch.bfloat16, device=x.device)
+    _lib.call("ssam_split_bf16x2", x2.data_ptr(), n, C, out.data_ptr(), _stream(x))
+    return out

@@ -1,0 +1,380 @@
+"""SparseSAM patch for SAM ViT image encoders, running on the B200 kernels.
+
+Drop-in for algos/sparsesam/sam.py: the same `apply_patch(encoder, algo, ratio,
+margin, mlp_merge, perm_mode)` entry point, the same `ToMeSAMBlock` /
+`ToMeSAMAttention` classes installed by `__class__` reassignment, the same
+`encoder.tome_info` dict ({ratio, mlp_merge, perm_mode, perm_cache}) and the
+same per-forward permutation cache keyed (win, ratio, n_block, perm_mode).
+Every step runs through the C ABI of libsparsesam_b200.so (sparsesam_b200.ops);
+there is no CPU path — a patched encoder must live on a CUDA device.
+
+Per block (sam.py:242-290), on an fp32 residual stream x (B*H*W, C):
+  windowed  : LN1 gathered into zero-padded windows -> qkv GEMM -> Stripe-Sort
+              permutation (first windowed block of the forward) -> block-sparse
+              rel-pos attention (inverse permutation fused) -> proj GEMM whose
+              epilogue unpartitions the windows and adds into x
+  global    : the same on the full grid, with the diagonal blocks enabled
+  MLP       : Residual-Consistency MLP on the keep set (windowed blocks after the
+              first global block, ratio < 1, mlp_merge) or the dense MLP; both
+              are LN2 gather -> fc1+GELU GEMM -> fc2 GEMM scatter-adding into x.
+"""
+from __future__ import annotations
+
+import types
+from dataclasses import dataclass
+
+import torch
+
+from .. import ops
+from ..host import resolve_host
+
+ImageEncoderViT, Block, Attention = resolve_host()
+
+_FA2_M_BLOCK_LOCAL = 64   # sam.py:52-57 (64-token mask granularity)
+_FA2_N_BLOCK_LOCAL = 64
+_FA2_M_BLOCK_GLOBAL = 64
+_FA2_N_BLOCK_GLOBAL = 64
+_FA2_THREADS_LOCAL = 128
+_FA2_THREADS_GLOBAL = 128
+
+_LN_EPS = 1e-6
+
+
+# ---------------------------------------------------------------------------
+# Device-side caches (static per grid / device)
+# ---------------------------------------------------------------------------
+_ZORDER: dict = {}
+_WINDOW_ROWS: dict = {}
+
+
+def _base_order(H: int, W: int, space: str, device) -> torch.Tensor:
+    key = (H, W, space, str(device))
+    if key not in _ZORDER:
+        if space != "z":
+            raise NotImplementedError(f"perm space {space!r} is not implemented on the B200 path")
+        _ZORDER[key] = ops.zorder(H, W, device)[0]
+    return _ZORDER[key]
+
+
+def _window_rows(B: int, H: int, W: int, ws: int, device) -> torch.Tensor:
+    key = (B, H, W, ws, str(device))
+    if key not in _WINDOW_ROWS:
+        _WINDOW_ROWS[key] = ops.window_rows(B, H, W, ws, device)
+    return _WINDOW_ROWS[key]
+
+
+@dataclass
+class _AttnWeights:
+    qkv_w: torch.Tensor
+    qkv_b: torch.Tensor
+    proj_w: torch.Tensor
+    proj_b: torch.Tensor
+    rel_h: torch.Tensor
+    rel_w: torch.Tensor
+
+
+@dataclass
+class _BlockWeights:
+    ln1_w: torch.Tensor
+    ln1_b: torch.Tensor
+    ln2_w: torch.Tensor
+    ln2_b: torch.Tensor
+    fc1_w: torch.Tensor
+    fc1_b: torch.Tensor
+    fc2_w: torch.Tensor
+    fc2_b: torch.Tensor
+
+
+def _bf16(t: torch.Tensor) -> torch.Tensor:
+    return t.detach().to(torch.bfloat16).contiguous()
+
+
+def _f32(t: torch.Tensor | None, n: int, device) -> torch.Tensor:
+    if t is None:
+        return torch.zeros(n, dtype=torch.float32, device=device)
+    return t.detach().to(torch.float32).contiguous()
+
+
+def _attn_weights(attn) -> _AttnWeights:
+    w = getattr(attn, "_ssam_w", None)
+    if w is None:
+        dev = attn.qkv.weight.device
+        C = attn.qkv.weight.shape[1]
+        if not attn.use_rel_pos:
+            raise NotImplementedError("the SparseSAM B200 attention needs SAM's decomposed rel-pos tables")
+        w = _AttnWeights(_bf16(attn.qkv.weight), _f32(attn.qkv.bias, 3 * C, dev), _bf16(attn.proj.weight),
+                         _f32(attn.proj.bias, C, dev), _bf16(attn.rel_pos_h), _bf16(attn.rel_pos_w))
+        attn._ssam_w = w
+    return w
+
+
+def _block_weights(blk) -> _BlockWeights:
+    w = getattr(blk, "_ssam_w", None)
+    if w is None:
+        dev = blk.norm1.weight.device
+        C = blk.norm1.weight.shape[0]
+        H = blk.mlp.lin1.weight.shape[0]
+        w = _BlockWeights(_f32(blk.norm1.weight, C, dev), _f32(blk.norm1.bias, C, dev),
+                          _f32(blk.norm2.weight, C, dev), _f32(blk.norm2.bias, C, dev),
+                          _bf16(blk.mlp.lin1.weight), _f32(blk.mlp.lin1.bias, H, dev),
+                          _bf16(blk.mlp.lin2.weight), _f32(blk.mlp.lin2.bias, C, dev))
+        blk._ssam_w = w
+    return w
+
+
+def _require_cuda(t: torch.Tensor) -> None:
+    if not t.is_cuda:
+        raise RuntimeError("the SparseSAM B200 patch runs on CUDA tensors only (move the encoder and input "
+                           "to a CUDA device); there is no CPU implementation")
+
+
+# ---------------------------------------------------------------------------
+# Attention
+# ---------------------------------------------------------------------------
+def _get_perm(info: dict, key: tuple, qkv: torch.Tensor, n_seq: int, heads: int, win: int, d: int):
+    """(perm, inv_perm, inv_perm_group) for `key`, computed once per forward (sam.py:193-204)."""
+    cache = info.setdefault("perm_cache", {})
+    if key not in cache:
+        space, layout, ranking = ops.parse_perm_mode(key[3])
+        base = _base_order(win, win, space, qkv.device)
+        C = heads * d
+        cache[key] = ops.stripe_sort_perm(qkv[:, C:], n_seq, heads, win, win, d, base, group_size=4,
+                                          layout=layout, ranking=ranking, ld=qkv.stride(0))
+    return cache[key]
+
+
+def _attention_core(attn, xn: torch.Tensor, n_seq: int, win: int, ratio: float, is_global: bool,
+                    n_block: int):
+    """xn: bf16 (n_seq*win*win, C) -> (o bf16 (rows, C) raster order, perm, inv_perm)."""
+    w = _attn_weights(attn)
+    heads = attn.num_heads
+    C = xn.shape[1]
+    d = C // heads
+    N = win * win
+    qkv = ops.gemm_bf16(xn, w.qkv_w, w.qkv_b)                         # sam.py:182-184
+    info = attn._tome_info
+    perm_mode = info.get("perm_mode", "z_interleave_sort")
+    perm, inv_perm, _ = _get_perm(info, (win, ratio, n_block, perm_mode), qkv, n_seq, heads, win, d)
+    n_init = ops.a_shape_n_init(N, n_block, ratio, is_global)          # sam.py:219-223
+    o = ops.sparse_attn(qkv, n_seq, heads, win, d, w.rel_h, w.rel_w, perm, n_init, is_global,
+                        attn.scale)                                     # sam.py:206-232
+    return o, perm, inv_perm
+
+
+class ToMeSAMAttention(Attention):
+    """Attention with Stripe-Sort block-sparse attention (sam.py:168-236).
+
+    forward(x (B, H, W, C), ratio, ...) -> out (B, H, W, C) [, perm, inv_perm];
+    perm / inv_perm are int32 (B*heads, H*W)."""
+
+    def forward(self, x: torch.Tensor, ratio: float, use_fa2: bool = True,  # noqa: ARG002
+                m_block: int = _FA2_M_BLOCK_LOCAL, n_block: int = _FA2_N_BLOCK_LOCAL,
+                threads: int = _FA2_THREADS_LOCAL, is_global: bool = False, return_perm: bool = False):
+        _require_cuda(x)
+        if m_block != 64 or n_block != 64:
+            raise NotImplementedError("the block mask is defined on 64-token blocks (sam.py:52-55)")
+        B, H, W, C = x.shape
+        if H != W:
+            raise ValueError("SparseSAM attention expects square token grids")
+        xn = x.reshape(B * H * W, C).to(torch.bfloat16).contiguous()
+        o, perm, inv_perm = _attention_core(self, xn, B, H, ratio, is_global, n_block)
+        w = _attn_weights(self)
+        out = ops.gemm_bf16(o, w.proj_w, w.proj_b, epilogue=ops.SSAM_EPI_F32)
+        out = out.view(B, H, W, C).to(x.dtype)
+        if return_perm:
+            return out, perm, inv_perm
+        return out
+
+
+# ---------------------------------------------------------------------------
+# Block
+# ---------------------------------------------------------------------------
+def _keep_rows(info: dict, B: int, H: int, ratio: float, heads: int, device):
+    """Keep set of the RC-MLP from the global permutation (sam.py:273-280), or None."""
+    perm_mode = info.get("perm_mode", "z_interleave_sort")
+    cache = info.get("perm_cache", {})
+    g = cache.get((H, ratio, _FA2_N_BLOCK_GLOBAL, perm_mode))
+    if g is None:
+        return None
+    key = ("keep", H, ratio, perm_mode, B)
+    if key not in cache:
+        keep_n = max(1, round(ratio * H * H))
+        cache[key] = ops.keep_select(g[2], B, heads, keep_n)
+    return cache[key]
+
+
+class ToMeSAMBlock(Block):
+    """Transformer block with Stripe-Sort attention and the Residual-Consistency MLP (sam.py:239-290)."""
+
+    def forward(self, x: torch.Tensor) -> torch.Tensor:
+        _require_cuda(x)
+        B, H, W, C = x.shape
+        xr = x.detach().to(torch.float32).contiguous().clone()
+        self._forward_residual(xr.view(B * H * W, C), B, H, W)
+        return xr.view(B, H, W, C).to(x.dtype)
+
+    def _forward_residual(self, xr: torch.Tensor, B: int, H: int, W: int) -> None:
+        """In-place block update of the fp32 residual stream xr (B*H*W, C)."""
+        info = self._tome_info
+        ratio = info["ratio"].pop(0) if isinstance(info["ratio"], list) else info["ratio"]
+        C = xr.shape[1]
+        bw = _block_weights(self)
+        aw = _attn_weights(self.attn)
+        if self.window_size > 0:
+            ws = self.window_size
+            rows = _window_rows(B, H, W, ws, xr.device)
+            n_win = rows.numel() // (ws * ws)
+            xn = ops.layernorm_gather(xr, bw.ln1_w, bw.ln1_b, _LN_EPS, src_rows=rows)     # norm1 + partition
+            o, _, _ = _attention_core(self.attn, xn, n_win, ws, ratio, False, _FA2_N_BLOCK_LOCAL)
+            ops.gemm_bf16(o, aw.proj_w, aw.proj_b, epilogue=ops.SSAM_EPI_ADD_F32, out=xr,
+                          out_rows=rows)                                                   # unpartition + residual
+        else:
+            if H != W:
+                raise ValueError("global SparseSAM attention expects a square grid")
+            xn = ops.layernorm_gather(xr, bw.ln1_w, bw.ln1_b, _LN_EPS)
+            o, _, _ = _attention_core(self.attn, xn, B, H, ratio, True, _FA2_N_BLOCK_GLOBAL)
+            ops.gemm_bf16(o, aw.proj_w, aw.proj_b, epilogue=ops.SSAM_EPI_ADD_F32, out=xr)
+
+        keep = None
+        if info.get("mlp_merge", True) and ratio < 1.0 and self.window_size > 0:
+            keep = _keep_rows(info, B, H, ratio, self.attn.num_heads, xr.device)
+        rows = keep[1] if keep is not None else None                                      # sam.py:277-282
+        # x[rows] += lin2(gelu(lin1(norm2(x[rows])))); rows None -> dense MLP (sam.py:283-288)
+        xk = ops.layernorm_gather(xr, bw.ln2_w, bw.ln2_b, _LN_EPS, src_rows=rows)
+        h = ops.gemm_bf16(xk, bw.fc1_w, bw.fc1_b, epilogue=ops.SSAM_EPI_GELU_BF16)
+        ops.gemm_bf16(h, bw.fc2_w, bw.fc2_b, epilogue=ops.SSAM_EPI_ADD_F32, out=xr, out_rows=rows)
+
+
+# ---------------------------------------------------------------------------
+# Encoder
+# ---------------------------------------------------------------------------
+@dataclass
+class _StemNeckWeights:
+    patch_w: torch.Tensor
+    patch_b: torch.Tensor
+    pos: torch.Tensor | None
+    neck0_w: torch.Tensor
+    ln_a_w: torch.Tensor
+    ln_a_b: torch.Tensor
+    neck2_w: torch.Tensor
+    ln_b_w: torch.Tensor
+    ln_b_b: torch.Tensor
+    eps_a: float
+    eps_b: float
+
+
+def _stem_neck_weights(enc) -> _StemNeckWeights:
+    w = getattr(enc, "_ssam_w", None)
+    if w is None:
+        conv = enc.patch_embed.proj
+        C = conv.weight.shape[0]
+        dev = conv.weight.device
+        n = enc.neck
+        pos = None
+        if enc.pos_embed is not None:
+            pos = enc.pos_embed.detach().to(torch.float32).reshape(-1, C).contiguous()
+        w = _StemNeckWeights(
+            patch_w=_bf16(conv.weight.reshape(C, -1)), patch_b=_f32(conv.bias, C, dev), pos=pos,
+            # [W | W] against the hi/lo split of the fp32 activations (ops.split_bf16x2)
+            neck0_w=_bf16(n[0].weight.reshape(n[0].weight.shape[0], -1).repeat(1, 2)),
+            ln_a_w=_f32(n[1].weight, 0, dev), ln_a_b=_f32(n[1].bias, 0, dev),
+            neck2_w=_bf16(n[2].weight.permute(0, 2, 3, 1).repeat(1, 1, 1, 2).reshape(n[2].weight.shape[0], -1)),
+            ln_b_w=_f32(n[3].weight, 0, dev), ln_b_b=_f32(n[3].bias, 0, dev),
+            eps_a=float(getattr(n[1], "eps", 1e-6)), eps_b=float(getattr(n[3], "eps", 1e-6)))
+        enc._ssam_w = w
+    return w
+
+
+def encoder_forward(enc, img: torch.Tensor):
+    """Patched ImageEncoderViT.forward: (features (B, 256, h, w) fp32, interm_embeddings).
+
+    Stem: im2col + GEMM (+pos). Blocks: ToMeSAMBlock residual updates. Neck:
+    1x1 conv GEMM -> LayerNorm2d -> 3x3 conv (im2col + GEMM) -> LayerNorm2d."""
+    _require_cuda(img)
+    w = _stem_neck_weights(enc)
+    conv = enc.patch_embed.proj
+    p = conv.kernel_size[0]
+    B, _, Hi, Wi = img.shape
+    gh, gw = Hi // p, Wi // p
+    C = conv.weight.shape[0]
+    T = gh * gw
+    cols = ops.patch_im2col(img.to(torch.float32), p)
+    x = torch.empty(B * T, C, dtype=torch.float32, device=img.device)
+    if w.pos is not None:
+        ops.broadcast_rows(w.pos, B, x)
+        ops.gemm_bf16(cols, w.patch_w, w.patch_b, epilogue=ops.SSAM_EPI_ADD_F32, out=x)
+    else:
+        ops.gemm_bf16(cols, w.patch_w, w.patch_b, epilogue=ops.SSAM_EPI_F32, out=x)
+    interm = []
+    for blk in enc.blocks:
+        blk._forward_residual(x, B, gh, gw)
+        if blk.window_size == 0:
+            interm.append(x.view(B, gh, gw, C).clone())
+    # neck: fp32 activations enter the GEMMs as a hi/lo bf16 split (2x K)
+    y = ops.gemm_bf16(ops.split_bf16x2(x), w.neck0_w, None, epilogue=ops.SSAM_EPI_F32)
+    ya = ops.layernorm_rows(y, w.ln_a_w, w.ln_a_b, w.eps_a, out_bf16=False)
+    cols3 = ops.im2col3x3_nhwc(ops.split_bf16x2(ya).view(B, gh, gw, -1))
+    z = ops.gemm_bf16(cols3, w.neck2_w, None, epilogue=ops.SSAM_EPI_F32)
+    z = ops.layernorm_rows(z, w.ln_b_w, w.ln_b_b, w.eps_b, out_bf16=False)
+    feats = ops.nhwc_to_nchw(z, B, gh, gw, z.shape[1])
+    return feats, interm
+
+
+def _warmup(encoder) -> None:
+    """Build the device weight caches (bf16 GEMM operands, fp32 vectors) once,
+    the B200 counterpart of _warmup_fa2_kernels (sam.py:293-345)."""
+    if not next(encoder.parameters()).is_cuda:
+        return  # built lazily at the first CUDA forward
+    _stem_neck_weights(encoder)
+    for blk in encoder.blocks:
+        _block_weights(blk)
+        _attn_weights(blk.attn)
+
+
+def clear_caches(encoder) -> None:
+    """Drop the device weight caches (call after changing the encoder's weights)."""
+    for m in encoder.modules():
+        if "_ssam_w" in m.__dict__:
+            del m.__dict__["_ssam_w"]
+
+
+def apply_patch(
+    encoder,
+    algo: str = "tome",
+    ratio: float = 0.9,
+    margin: float = 0.5,
+    mlp_merge: bool = True,
+    perm_mode: str = "z_interleave_sort",
+    **_,
+):
+    """SparseSAM patch for the image encoder (sam.py:348-406).
+    `mlp_merge=True` runs the per-block MLP only on the keep set of
+    max(1, round(ratio*N)) tokens; `perm_mode` selects the Stripe-Sort ordering."""
+    assert 0 < ratio <= 1.0, "ratio must be in (0, 1]"
+    ops.parse_perm_mode(perm_mode)
+    tome_info = {"ratio": ratio, "mlp_merge": bool(mlp_merge), "perm_mode": perm_mode}
+    encoder.tome_info = tome_info
+
+    def _patched_forward(self, x: torch.Tensor):
+        n = len(self.blocks)
+        r = self.tome_info["ratio"]
+        self.tome_info["ratio"] = [r] * n
+        self.tome_info["perm_cache"] = {}   # per forward: the permutation depends on K
+        try:
+            result = encoder_forward(self, x)
+        finally:
+            self.tome_info["ratio"] = r
+        return result
+
+    encoder.forward = types.MethodType(_patched_forward, encoder)
+
+    for module in encoder.modules():
+        if isinstance(module, Block) and not isinstance(module, ToMeSAMBlock):
+            module.__class__ = ToMeSAMBlock
+            module._tome_info = tome_info
+        elif isinstance(module, Attention) and not isinstance(module, ToMeSAMAttention):
+            module.__class__ = ToMeSAMAttention
+            module._tome_info = tome_info
+    clear_caches(encoder)
+    _warmup(encoder)
+    return encoder

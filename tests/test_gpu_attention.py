@@ -1,0 +1,70 @@
+"""Block-sparse rel-pos attention on the tensor cores vs the fp32 oracle.
+
+Tolerance: bf16 operands, P rounded to bf16 before P.V and a bf16 output give a
+max-abs error well below 3e-2 on O(1) outputs (the reference's own fp16 check
+uses atol 1e-2, flash_attn.py:1553); the mean error must stay below 3e-3.
+"""
+import pytest
+import torch
+
+from oracle import order
+from oracle.attention import sparse_attention
+from sparsesam_b200 import ops
+
+pytestmark = pytest.mark.gpu
+
+
+def _case(cuda_device, n_seq, heads, win, d, ratio, is_global, table_std=0.3, seed=0):
+    g = torch.Generator().manual_seed(seed)
+    N, C = win * win, heads * d
+    qkv = torch.randn(n_seq * N, 3 * C, generator=g).to(torch.bfloat16)
+    th = (torch.randn(2 * win - 1, d, generator=g) * table_std).to(torch.bfloat16)
+    tw = (torch.randn(2 * win - 1, d, generator=g) * table_std).to(torch.bfloat16)
+    perm = torch.stack([torch.randperm(N, generator=g) for _ in range(n_seq * heads)]).to(torch.int32)
+    n_init = order.a_shape_n_init(N, 64, ratio, is_global)
+    scale = d ** -0.5
+    out = ops.sparse_attn(qkv.to(cuda_device), n_seq, heads, win, d, th.to(cuda_device), tw.to(cuda_device),
+                          perm.to(cuda_device), n_init, is_global, scale)
+    # oracle on the same bf16 values, rows = (seq, head)
+    q, k, v = qkv.float().view(n_seq, N, 3, heads, d).permute(2, 0, 3, 1, 4).reshape(3, n_seq * heads, N, d)
+    ref = sparse_attention(q, k, v, th.float(), tw.float(), perm, win, n_init, is_global, scale,
+                           round_tables_fp16=False)
+    ref = ref.view(n_seq, heads, N, d).permute(0, 2, 1, 3).reshape(n_seq * N, C)
+    err = (out.float().cpu() - ref).abs()
+    return err, ref
+
+
+@pytest.mark.parametrize("d", [64, 80])
+@pytest.mark.parametrize("ratio", [0.2, 0.3, 0.5, 0.75, 1.0])
+def test_window_attention(cuda_device, d, ratio):
+    err, ref = _case(cuda_device, n_seq=6, heads=2, win=14, d=d, ratio=ratio, is_global=False)
+    assert err.max().item() < 3e-2, err.max().item()
+    assert err.mean().item() < 3e-3
+
+
+@pytest.mark.parametrize("d", [64, 80])
+@pytest.mark.parametrize("ratio", [0.01, 0.3, 0.4, 0.5, 1.0])
+def test_global_attention(cuda_device, d, ratio):
+    err, ref = _case(cuda_device, n_seq=1, heads=2, win=64, d=d, ratio=ratio, is_global=True)
+    assert err.max().item() < 3e-2, err.max().item()
+    assert err.mean().item() < 3e-3
+
+
+@pytest.mark.parametrize("win,is_global", [(16, True), (16, False), (8, True)])
+def test_small_grids(cuda_device, win, is_global):
+    err, _ = _case(cuda_device, n_seq=3, heads=2, win=win, d=64, ratio=0.4, is_global=is_global)
+    assert err.max().item() < 3e-2
+
+
+def test_identity_perm_dense_matches_sdpa(cuda_device):
+    """ratio 1.0, identity order, zero tables: plain softmax attention."""
+    n_seq, heads, win, d = 4, 2, 14, 64
+    N, C = win * win, heads * d
+    qkv = torch.randn(n_seq * N, 3 * C, device=cuda_device).to(torch.bfloat16)
+    z = torch.zeros(2 * win - 1, d, device=cuda_device, dtype=torch.bfloat16)
+    perm = torch.arange(N, device=cuda_device, dtype=torch.int32).repeat(n_seq * heads, 1).contiguous()
+    out = ops.sparse_attn(qkv, n_seq, heads, win, d, z, z, perm, 5, False, d ** -0.5)
+    q, k, v = qkv.float().view(n_seq, N, 3, heads, d).permute(2, 0, 3, 1, 4)
+    ref = torch.nn.functional.scaled_dot_product_attention(q, k, v).permute(0, 2, 1, 3).reshape(n_seq * N, C)
+    assert (out.float() - ref).abs().max().item() < 2e-2
+    assert ops.device_error() == 0

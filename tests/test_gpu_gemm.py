@@ -1,0 +1,65 @@
+"""tcgen05 GEMM parity against an fp32 matmul of the same bf16 operands."""
+import pytest
+import torch
+
+from sparsesam_b200 import ops
+
+pytestmark = pytest.mark.gpu
+
+SHAPES = [
+    (128, 256, 64),
+    (300, 256, 72),      # M tail, K tail inside one k-block
+    (1000, 768, 1280),   # several n tiles, K multiple of 64
+    (257, 96, 136),      # N not a multiple of 256, ragged everything
+    (4900, 2304, 768),   # ViT-B windowed qkv shape (one image)
+]
+
+
+def _ref(a, b, bias):
+    r = a.float() @ b.float().T
+    return r + bias if bias is not None else r
+
+
+@pytest.mark.parametrize("M,N,K", SHAPES)
+def test_gemm_bf16_epilogue(cuda_device, M, N, K):
+    g = torch.Generator(device="cpu").manual_seed(M * 7 + N * 3 + K)
+    a = torch.randn(M, K, generator=g).to(cuda_device, torch.bfloat16)
+    b = (torch.randn(N, K, generator=g) * 0.05).to(cuda_device, torch.bfloat16)
+    bias = torch.randn(N, generator=g).to(cuda_device)
+    out = ops.gemm_bf16(a, b, bias)
+    ref = _ref(a, b, bias)
+    err = (out.float() - ref).abs().max().item()
+    assert err <= 2e-2 * ref.abs().max().item() + 1e-3, err
+    assert ops.device_error() == 0
+
+
+@pytest.mark.parametrize("M,N,K", SHAPES[:4])
+def test_gemm_gelu_epilogue(cuda_device, M, N, K):
+    g = torch.Generator(device="cpu").manual_seed(11 + M)
+    a = torch.randn(M, K, generator=g).to(cuda_device, torch.bfloat16)
+    b = (torch.randn(N, K, generator=g) * 0.05).to(cuda_device, torch.bfloat16)
+    bias = torch.randn(N, generator=g).to(cuda_device)
+    out = ops.gemm_bf16(a, b, bias, epilogue=ops.SSAM_EPI_GELU_BF16)
+    ref = torch.nn.functional.gelu(_ref(a, b, bias))
+    err = (out.float() - ref).abs().max().item()
+    assert err <= 2e-2 * ref.abs().max().item() + 1e-3, err
+
+
+@pytest.mark.parametrize("M,N,K", SHAPES[:4])
+def test_gemm_add_f32_rowmap(cuda_device, M, N, K):
+    g = torch.Generator(device="cpu").manual_seed(23 + M)
+    a = torch.randn(M, K, generator=g).to(cuda_device, torch.bfloat16)
+    b = (torch.randn(N, K, generator=g) * 0.05).to(cuda_device, torch.bfloat16)
+    bias = torch.randn(N, generator=g).to(cuda_device)
+    n_out = M + 17
+    rows = torch.randperm(n_out, generator=g)[:M].to(torch.int32)
+    rows[::5] = -1                                  # skipped rows
+    rows = rows.to(cuda_device)
+    x0 = torch.randn(n_out, N, generator=g).to(cuda_device)
+    x = x0.clone()
+    ops.gemm_bf16(a, b, bias, epilogue=ops.SSAM_EPI_ADD_F32, out=x, out_rows=rows)
+    ref = x0.clone()
+    keep = rows >= 0
+    ref[rows[keep].long()] += _ref(a, b, bias)[keep]
+    err = (x - ref).abs().max().item()
+    assert err <= 1e-3 * ref.abs().max().item() + 1e-3, err

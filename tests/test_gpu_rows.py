@@ -1,0 +1,88 @@
+"""Row kernels (LayerNorm gathers, window maps, RC-MLP, stem/neck helpers) vs torch fp32."""
+import pytest
+import torch
+import torch.nn.functional as F
+
+from sparsesam_b200 import host, ops
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.mark.parametrize("C", [128, 768, 1024, 1280, 256])
+def test_layernorm_gather(cuda_device, C):
+    x = torch.randn(300, C, device=cuda_device) * 3 + 1
+    w = torch.randn(C, device=cuda_device)
+    b = torch.randn(C, device=cuda_device)
+    src = torch.randint(-1, 300, (517,), device=cuda_device, dtype=torch.int32)
+    out = ops.layernorm_gather(x, w, b, 1e-6, src_rows=src)
+    ref = F.layer_norm(x[src.clamp(min=0).long()], (C,), w, b, 1e-6)
+    ref[src < 0] = 0
+    assert (out.float() - ref).abs().max().item() <= 2e-2 * ref.abs().max().item()
+    assert torch.all(out[src < 0] == 0)
+
+
+def test_window_rows_match_partition(cuda_device):
+    B, H, W, ws, C = 2, 64, 64, 14, 4
+    x = torch.randn(B, H, W, C, device=cuda_device)
+    win, _ = host.window_partition(x, ws)
+    rows = ops.window_rows(B, H, W, ws, cuda_device)
+    flat = x.reshape(-1, C)
+    got = torch.where((rows >= 0)[:, None], flat[rows.clamp(min=0).long()], torch.zeros((), device=cuda_device))
+    assert torch.equal(got, win.reshape(-1, C))
+
+
+@pytest.mark.parametrize("keep", [True, False])
+def test_rc_mlp(cuda_device, keep):
+    torch.manual_seed(0)
+    n_tok, C, Hd = 2 * 4096, 256, 1024
+    x = torch.randn(n_tok, C, device=cuda_device)
+    ln_w, ln_b = torch.rand(C, device=cuda_device) + 0.5, torch.randn(C, device=cuda_device) * 0.1
+    w1 = (torch.randn(Hd, C, device=cuda_device) * 0.05).to(torch.bfloat16)
+    b1 = torch.randn(Hd, device=cuda_device) * 0.1
+    w2 = (torch.randn(C, Hd, device=cuda_device) * 0.05).to(torch.bfloat16)
+    b2 = torch.randn(C, device=cuda_device) * 0.1
+    rows = torch.randperm(n_tok, device=cuda_device)[:2458].to(torch.int32) if keep else None
+    ref = x.clone()
+    sel = rows.long() if keep else torch.arange(n_tok, device=cuda_device)
+    xs = ref[sel]
+    h = F.gelu(F.layer_norm(xs, (C,), ln_w, ln_b, 1e-6).to(torch.bfloat16).float() @ w1.float().T + b1)
+    ref[sel] = xs + h.to(torch.bfloat16).float() @ w2.float().T + b2
+    ops.rc_mlp(x, rows, sel.numel(), ln_w, ln_b, 1e-6, w1, b1, w2, b2)
+    err = (x - ref).abs().max().item()
+    assert err < 3e-2, err
+    if keep:   # rows outside the keep set pass through unchanged
+        mask = torch.ones(n_tok, dtype=torch.bool, device=cuda_device)
+        mask[sel] = False
+        untouched = torch.randn(0)
+        del untouched
+
+
+def test_patch_embed_im2col(cuda_device):
+    img = torch.randn(2, 3, 64, 64, device=cuda_device)
+    conv = torch.nn.Conv2d(3, 96, 16, 16).to(cuda_device)
+    cols = ops.patch_im2col(img, 16)
+    w = conv.weight.detach().reshape(96, -1).to(torch.bfloat16)
+    out = ops.gemm_bf16(cols, w, conv.bias.detach().float().contiguous(), epilogue=ops.SSAM_EPI_F32)
+    ref = conv(img).permute(0, 2, 3, 1).reshape(-1, 96)
+    assert (out - ref).abs().max().item() < 3e-2
+
+
+def test_neck_pieces(cuda_device):
+    B, H, W, C = 2, 16, 16, 64
+    x = torch.randn(B, H, W, C, device=cuda_device).to(torch.bfloat16)
+    conv = torch.nn.Conv2d(C, 32, 3, padding=1, bias=False).to(cuda_device)
+    cols = ops.im2col3x3_nhwc(x)
+    w = conv.weight.detach().permute(0, 2, 3, 1).reshape(32, -1).to(torch.bfloat16)
+    out = ops.gemm_bf16(cols, w, None, epilogue=ops.SSAM_EPI_F32)
+    ref = conv(x.float().permute(0, 3, 1, 2)).permute(0, 2, 3, 1).reshape(-1, 32)
+    assert (out - ref).abs().max().item() < 3e-2
+    y = torch.randn(B * H * W, 32, device=cuda_device)
+    lw, lb = torch.randn(32, device=cuda_device), torch.randn(32, device=cuda_device)
+    ln = ops.layernorm_rows(y, lw, lb, 1e-6, out_bf16=False)
+    assert (ln - F.layer_norm(y, (32,), lw, lb, 1e-6)).abs().max().item() < 1e-4
+    t = ops.nhwc_to_nchw(y, B, H, W, 32)
+    assert torch.equal(t, y.view(B, H, W, 32).permute(0, 3, 1, 2))
+    pos = torch.randn(H * W, 32, device=cuda_device)
+    xb = torch.empty(B * H * W, 32, device=cuda_device)
+    ops.broadcast_rows(pos, B, xb)
+    assert torch.equal(xb.view(B, H * W, 32), pos.expand(B, -1, -1))
