@@ -11,14 +11,20 @@
 // and the result of permuted row p is written to raster token perm[p]
 // (the inverse permutation and the head merge are fused into the store).
 //
-// One CTA = 128 permuted queries of one row, 4 warps, thread i owns query row i:
-//   prologue : gather Q rows by perm (cp.async, UMMA SW128/SW32 layout), load the
-//              rel-pos tables, P_H = Q Th^T and P_W = Q Tw^T on the tensor cores,
-//              and scatter the per-row bias windows into shared memory;
-//   per key block (64 keys, double-buffered cp.async gathers):
-//              S = Q K^T (UMMA -> TMEM), row softmax from TMEM in registers
-//              (online max/sum, exp2), P -> shared memory (bf16), O_blk = P V
-//              (UMMA, V as an MN-major operand), O = alpha*O + O_blk in registers.
+// Persistent, warp-specialised CTA (one per SM), 192 threads:
+//   warps 0-3  softmax warpgroup: thread i owns query row i of the current
+//              128-query tile; extracts its rel-pos bias windows, runs the online
+//              softmax out of TMEM, writes P (bf16) and does the epilogue;
+//   warp 4     loader: cp.async gathers of the permuted Q / K / V rows (64-key
+//              blocks, 3 stages) and the rel-pos tables, signalled through
+//              mbarriers (cp.async.mbarrier.arrive);
+//   warp 5     UMMA issuer: P_H = Q Th^T and P_W = Q Tw^T for the next tile,
+//              S(j+1) = Q K^T issued ahead of softmax(j) into a second TMEM
+//              buffer, O += P V accumulated in TMEM (V as an MN-major operand).
+// O is rescaled lazily: only when a row maximum grows by more than 2^8 is the
+// TMEM row read, scaled and written back; otherwise the stale maximum is kept
+// (probabilities stay below 2^8 and the final 1/l normalisation is consistent).
+// Every wait is bounded; on timeout the CTA raises SSAM_ERR_TIMEOUT and unwinds.
 #include <cuda_fp16.h>
 
 #include "common.cuh"
@@ -26,16 +32,21 @@
 
 namespace ssam {
 
-constexpr int kAttnThreads = 128;
-constexpr int kAttnBM = 128;    // queries per CTA
-constexpr int kAttnBN = 64;     // keys per block (the reference's 64-token mask granularity)
-constexpr int kAttnTmemCols = 256;
+constexpr int kAttnBM = 128;  // queries per tile
+constexpr int kAttnBN = 64;   // keys per block (the reference's 64-token mask granularity)
+constexpr int kAttnStages = 3;
+constexpr int kAttnThreads = 192;
+constexpr int kAttnTmemCols = 512;
+constexpr float kRescaleThreshold = 8.0f;  // log2 units
 
 __device__ __forceinline__ void cp_async16(uint32_t dst, const void* src, uint32_t src_bytes) {
   asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "r"(src_bytes) : "memory");
 }
-__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
-__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_group 0;" ::: "memory"); }
+__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
+// Arrive on `bar` once every cp.async issued so far by this thread has landed.
+__device__ __forceinline__ void cp_async_arrive_noinc(uint64_t* bar) {
+  asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
 
 __device__ __forceinline__ float fast_exp2(float x) {
   float y;
@@ -43,9 +54,19 @@ __device__ __forceinline__ float fast_exp2(float x) {
   return y;
 }
 
-// Shared-memory geometry of a D-wide operand tile with R rows: the first 64
-// channels in a 128B-swizzled region (R x 128 B), channels 64..79 (D == 80) in a
-// 32B-swizzled region (R x 32 B) right after it.
+__device__ __forceinline__ void tmem_st_32x32b_x16(uint32_t taddr, const uint32_t (&r)[16]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], "
+      "{%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, %16};" ::"r"(taddr),
+      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]), "r"(r[9]),
+      "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15])
+      : "memory");
+}
+__device__ __forceinline__ void tmem_st_wait() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
+
+// Shared-memory geometry of a D-wide operand tile with R rows: channels 0..63 in
+// a 128B-swizzled region (R x 128 B), channels 64..79 (D == 80) in a 32B-swizzled
+// region (R x 32 B) right after it.
 template <int D>
 struct TileGeom {
   static constexpr int kChunks = D / 8;  // 16-byte chunks per row
@@ -53,7 +74,6 @@ struct TileGeom {
   static __host__ __device__ constexpr int bytes(int rows) { return rows * 128 + (kTail ? rows * 32 : 0); }
 };
 
-// Destination of 16-byte chunk c of row r inside a TileGeom region.
 template <int D>
 __device__ __forceinline__ uint32_t tile_chunk_addr(uint32_t base, int rows, int r, int c) {
   if (c < 8) return base + r * 128 + ((c ^ (r & 7)) << 4);
@@ -67,6 +87,62 @@ __device__ __forceinline__ uint64_t kmajor_desc(uint32_t base, int rows, int ks)
   return make_smem_desc(base + rows * 128, 16, 256, kSw32);
 }
 
+__host__ __device__ constexpr int align1k(int v) { return (v + 1023) & ~1023; }
+
+// Instruction descriptor for kind::f16 with fp16 A/B (formats 0), fp32 accumulator.
+__host__ __device__ constexpr uint32_t make_idesc_f16(uint32_t M, uint32_t N) {
+  return (1u << 4) | ((N >> 3) << 17) | ((M >> 4) << 24);
+}
+
+// Two specialisations: SMALL for windowed grids (win <= 16, 32-row tables) and
+// the global 64x64 grid. SMALL tiles have one or two key blocks, so they get a
+// deeper S pipeline and double-buffered O / P_H / A_bias to remove tile bubbles.
+template <int D, bool SMALL>
+struct AttnCfg {
+  static constexpr int kS = SMALL ? 3 : 2;        // S buffers in TMEM (QK^T lookahead)
+  static constexpr int kO = SMALL ? 2 : 1;        // O accumulators in TMEM
+  static constexpr int kPH = SMALL ? 2 : 1;       // P_H/P_W TMEM buffers
+  static constexpr int kAB = SMALL ? 2 : 1;       // A_bias shared-memory buffers
+  static constexpr int kStages = SMALL ? 3 : 2;   // K / V / one-hot stages
+  static constexpr int kBW = SMALL ? 16 : 64;     // bias columns per table (>= win)
+  static constexpr int kNT = SMALL ? 32 : 128;    // table rows padded to the MMA N
+  static constexpr int kTmO = kS * kAttnBN;       // TMEM column of O[0]
+  static constexpr int kTmPH = SMALL ? kTmO + kO * D : 256;
+  static constexpr int kOHBytes = 2 * kAttnBN * kBW * 2;  // one-hot H | W regions per stage
+  static constexpr int kABBytes = 2 * kAttnBM * kBW * 2;  // A_bias H | W regions
+  static_assert(kTmPH + kPH * 2 * kNT <= kAttnTmemCols, "TMEM plan exceeds 512 columns");
+};
+
+// Byte offset of element (row r, column k) of a K-major fp16 bias operand region
+// (128B swizzle for 64-wide rows, 32B swizzle for 16-wide rows).
+template <bool SMALL>
+__device__ __forceinline__ uint32_t bias_off(int r, int k) {
+  if constexpr (SMALL) return r * 32 + ((((k >> 3) ^ ((r >> 2) & 1))) << 4) + (k & 7) * 2;
+  return r * 128 + ((((k >> 3) ^ (r & 7))) << 4) + (k & 7) * 2;
+}
+
+// Shared-memory plan (bytes from a 1 KB-aligned base).
+template <int D, bool SMALL>
+struct AttnLayout {
+  using C = AttnCfg<D, SMALL>;
+  using TG = TileGeom<D>;
+  static constexpr int kStage = 2 * TG::bytes(kAttnBN) + C::kOHBytes;  // K | V | one-hot
+  int th, tw, q, kv, p, ab, kinfo, tok, bars, total;
+  __host__ __device__ AttnLayout(int win) {
+    th = 0;
+    tw = align1k(th + TG::bytes(C::kNT));
+    q = align1k(tw + TG::bytes(C::kNT));               // [2] x bytes(128)
+    kv = q + 2 * TG::bytes(kAttnBM);                   // [stages] x kStage
+    p = kv + C::kStages * kStage;                      // [2] x 128 x 128 B
+    ab = p + 2 * kAttnBM * 128;                        // [kAB] x kABBytes
+    kinfo = ab + C::kAB * C::kABBytes;                 // int [stages][64]
+    tok = kinfo + C::kStages * kAttnBN * 4;            // int [2][128]
+    bars = (tok + 2 * kAttnBM * 4 + 7) & ~7;           // mbarriers
+    total = bars + 32 * 8 + 16 + 1024;                 // + alignment slack
+    (void)win;
+  }
+};
+
 struct AttnParams {
   const __nv_bfloat16* qkv;
   int64_t ld_qkv;
@@ -76,351 +152,584 @@ struct AttnParams {
   const int32_t* perm;
   int n_init, with_diag;
   float scale_log2;  // scale * log2(e)
+  float inv_scale;   // 1 / scale
   __nv_bfloat16* out;
   int64_t ld_out;
-  int nt;  // table rows padded to the MMA N (32 or 128)
+  int n_tiles;  // 128-query tiles per row
+  int total_tiles;
 };
 
-template <int D>
-struct AttnSmem {
-  static constexpr int kQ = 0;
-  static constexpr int kQBytes = TileGeom<D>::bytes(kAttnBM);
-  static constexpr int kKVBytes = TileGeom<D>::bytes(kAttnBN);
-  static constexpr int kK0 = kQ + kQBytes;           // K[2], V[2] (tables alias this region)
-  static constexpr int kV0 = kK0 + 2 * kKVBytes;
-  static constexpr int kP = kV0 + 2 * kKVBytes;      // 128 x 64 bf16, SW128
-  static constexpr int kBias = kP + kAttnBM * 128;   // biasH[win][128], biasW[win][128] fp16
-  static_assert(2 * TileGeom<D>::bytes(128) <= 4 * kKVBytes, "rel-pos tables must fit in the K/V region");
-  static_assert(kK0 % 1024 == 0 && kKVBytes % 1024 == 0 && kP % 1024 == 0, "UMMA regions need 1 KB alignment");
-  static __host__ __device__ constexpr int bias_bytes(int win) { return 2 * win * kAttnBM * 2; }
-  static __host__ __device__ constexpr int kinfo_off(int win) { return kBias + bias_bytes(win); }
-  static __host__ __device__ constexpr int total(int win) {
-    return kinfo_off(win) + 2 * kAttnBN * 4 /*kinfo[2][64]*/ + kAttnBM * 4 /*tok*/ + 64 /*bar+tmem*/ + 1024;
-  }
-};
-
-template <int D>
-__global__ void __launch_bounds__(kAttnThreads, 2) sparse_attn_kernel(const AttnParams a) {
-  using SM = AttnSmem<D>;
-  using TG = TileGeom<D>;
-  extern __shared__ uint8_t smem_raw[];
-  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  const uint32_t s_base = smem_u32(smem);
-  // Per-row bias windows, stored transposed ([j][row]) in fp16 like the
-  // reference's sRelH / sRelW (flash_attn.py:838-839).
-  __half* s_bias_h = reinterpret_cast<__half*>(smem + SM::kBias);
-  __half* s_bias_w = s_bias_h + a.win * kAttnBM;
-  int* s_kinfo = reinterpret_cast<int*>(smem + SM::kinfo_off(a.win));  // [2][64]
-  int* s_tok = s_kinfo + 2 * kAttnBN;                                  // [128]
-  uint64_t* bar = reinterpret_cast<uint64_t*>(s_tok + kAttnBM);
-  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(bar + 1);
-
-  const int tid = threadIdx.x;
-  const int warp = tid >> 5;
-  const int n_tiles = (a.N + kAttnBM - 1) / kAttnBM;
-  const int tile = blockIdx.x % n_tiles;
-  const int row = blockIdx.x / n_tiles;
-  const int seq = row / a.heads, head = row - seq * a.heads;
-  const int N = a.N, win = a.win;
-  const int32_t* perm = a.perm + static_cast<int64_t>(row) * N;
-  const __nv_bfloat16* q_base = a.qkv + static_cast<int64_t>(seq) * N * a.ld_qkv + head * D;
-  const __nv_bfloat16* k_base = q_base + a.C;
-  const __nv_bfloat16* v_base = q_base + 2 * a.C;
-  const int nblk = (N + kAttnBN - 1) / kAttnBN;
-
-  // Enabled key blocks of this tile: the keep bar, then the diagonal blocks.
-  const int nk = a.n_init < nblk ? a.n_init : nblk;
-  int n_diag = 0, diag0 = -1, diag1 = -1;
-  if (a.with_diag) {
-    for (int mb = 2 * tile; mb < 2 * tile + 2; ++mb) {
-      if (mb < nblk && mb >= nk) {
-        if (n_diag == 0) diag0 = mb; else diag1 = mb;
-        ++n_diag;
+// Key blocks of one tile: the keep bar [0, nk), then the diagonal blocks of the
+// two 64-query m-blocks of the tile that lie outside the bar.
+struct TileBlocks {
+  int nk, n, d0, d1;
+  __device__ TileBlocks() : nk(0), n(0), d0(-1), d1(-1) {}
+  __device__ TileBlocks(const AttnParams& a, int qtile) {
+    const int nblk = (a.N + kAttnBN - 1) / kAttnBN;
+    nk = a.n_init < nblk ? a.n_init : nblk;
+    n = nk;
+    d0 = d1 = -1;
+    if (a.with_diag) {
+      for (int mb = 2 * qtile; mb < 2 * qtile + 2; ++mb) {
+        if (mb < nblk && mb >= nk) {
+          if (n == nk) d0 = mb; else d1 = mb;
+          ++n;
+        }
       }
     }
   }
-  const int n_blocks = nk + n_diag;
-  auto block_at = [&](int i) { return i < nk ? i : (i == nk ? diag0 : diag1); };
+  __device__ int at(int i) const { return i < nk ? i : (i == nk ? d0 : d1); }
+};
+
+// Walks the flat (tile, key block) sequence of one persistent CTA.
+struct BlockCursor {
+  int tile, lt, j, g;
+  bool done;
+  TileBlocks tb;
+  __device__ void start(const AttnParams& a) {
+    tile = blockIdx.x;
+    lt = 0;
+    j = 0;
+    g = 0;
+    done = tile >= a.total_tiles;
+    if (!done) tb = TileBlocks(a, tile % a.n_tiles);
+  }
+  __device__ void advance(const AttnParams& a) {
+    ++j;
+    ++g;
+    if (j >= tb.n) {
+      j = 0;
+      ++lt;
+      tile += gridDim.x;
+      done = tile >= a.total_tiles;
+      if (!done) tb = TileBlocks(a, tile % a.n_tiles);
+    }
+  }
+};
+
+// mbarrier indices
+enum {
+  kBarTab = 0,
+  kBarQFull = 1,     // [2]
+  kBarQEmpty = 3,    // [2]
+  kBarKVFull = 5,    // [3]
+  kBarKVEmpty = 8,   // [3]
+  kBarPHFull = 11,   // [2]
+  kBarPHFree = 13,   // [2]
+  kBarABFull = 15,   // [2]
+  kBarSFull = 17,    // [3]
+  kBarSFree = 20,    // [3]
+  kBarPFull = 23,    // [2]
+  kBarODone = 25,    // [2]
+  kBarOFree = 27,    // [2]
+  kBarDrain = 29,
+  kNumBars = 30
+};
+
+template <int D, bool SMALL>
+__global__ void __launch_bounds__(kAttnThreads, 1) sparse_attn_kernel(const AttnParams a) {
+  using TG = TileGeom<D>;
+  using C = AttnCfg<D, SMALL>;
+  using LAY = AttnLayout<D, SMALL>;
+  const LAY L(a.win);
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const uint32_t sb = smem_u32(smem);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L.bars);
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(bars + kNumBars);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
+  int* s_kinfo = reinterpret_cast<int*>(smem + L.kinfo);
+  int* s_tok = reinterpret_cast<int*>(smem + L.tok);
+
+  const int tid = threadIdx.x;
+  const int warp = tid >> 5, lane = tid & 31;
+  const int N = a.N, win = a.win;
 
   if (tid == 0) {
-    mbar_init(bar, 1);
+    mbar_init(&bars[kBarTab], 64);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&bars[kBarQFull + i], 64);
+      mbar_init(&bars[kBarQEmpty + i], 1);
+      mbar_init(&bars[kBarPHFull + i], 1);
+      mbar_init(&bars[kBarPHFree + i], 128);
+      mbar_init(&bars[kBarABFull + i], 128);
+      mbar_init(&bars[kBarPFull + i], 128);
+      mbar_init(&bars[kBarODone + i], 1);
+      mbar_init(&bars[kBarOFree + i], 128);
+    }
+    for (int s = 0; s < 3; ++s) {
+      mbar_init(&bars[kBarKVFull + s], 64);
+      mbar_init(&bars[kBarKVEmpty + s], 1);
+      mbar_init(&bars[kBarSFull + s], 1);
+      mbar_init(&bars[kBarSFree + s], 128);
+    }
+    mbar_init(&bars[kBarDrain], 1);
+    *abort_flag = 0;
     fence_mbar_init();
   }
-  if (warp == 0) {
+  if (warp == 5) {
     tmem_alloc(tmem_holder, kAttnTmemCols);
     tmem_relinquish();
   }
-
-  // ---- prologue: Q rows (gathered by perm) and the two rel-pos tables ----
-  {
-    const int p = tile * kAttnBM + tid;
-    s_tok[tid] = p < N ? __ldg(perm + p) : -1;
-  }
-  __syncthreads();
-  const uint32_t sQ = s_base + SM::kQ;
-  for (int idx = tid; idx < kAttnBM * TG::kChunks; idx += kAttnThreads) {
-    const int r = idx / TG::kChunks, c = idx - r * TG::kChunks;
-    const int t = s_tok[r];
-    const void* src = t >= 0 ? static_cast<const void*>(q_base + static_cast<int64_t>(t) * a.ld_qkv + c * 8)
-                             : static_cast<const void*>(a.qkv);
-    cp_async16(tile_chunk_addr<D>(sQ, kAttnBM, r, c), src, t >= 0 ? 16u : 0u);
-  }
-  const uint32_t sTh = s_base + SM::kK0;
-  const uint32_t sTw = sTh + TG::bytes(kAttnBM);
-  const int trows = 2 * win - 1;
-  for (int idx = tid; idx < a.nt * TG::kChunks; idx += kAttnThreads) {
-    const int r = idx / TG::kChunks, c = idx - r * TG::kChunks;
-    const bool ok = r < trows;
-    cp_async16(tile_chunk_addr<D>(sTh, kAttnBM, r, c), ok ? static_cast<const void*>(a.th + r * D + c * 8) : a.th,
-               ok ? 16u : 0u);
-    cp_async16(tile_chunk_addr<D>(sTw, kAttnBM, r, c), ok ? static_cast<const void*>(a.tw + r * D + c * 8) : a.tw,
-               ok ? 16u : 0u);
-  }
-  cp_async_commit();
-  cp_async_wait_all();
-  fence_proxy_async_smem();
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_holder;
-  const uint32_t t_lane = tmem + (static_cast<uint32_t>(warp * 32) << 16);
-  uint32_t bar_phase = 0;
-  bool ok = true;
 
-  // P_H -> columns [0, nt), P_W -> columns [128, 128 + nt).
-  if (tid == 0) {
-    const uint32_t idesc_t = make_idesc_bf16(kAttnBM, a.nt, 0, 0);
-#pragma unroll
-    for (int ks = 0; ks < D / 16; ++ks) {
-      umma_f16_ss(tmem, kmajor_desc<D>(sQ, kAttnBM, ks), kmajor_desc<D>(sTh, kAttnBM, ks), idesc_t, ks > 0);
-      umma_f16_ss(tmem + 128, kmajor_desc<D>(sQ, kAttnBM, ks), kmajor_desc<D>(sTw, kAttnBM, ks), idesc_t, ks > 0);
+  auto wait_or_abort = [&](int bar, uint32_t parity) -> bool {
+    if (*abort_flag) return false;
+    if (!mbar_wait(&bars[bar], parity)) {
+      *abort_flag = 1;
+      return false;
     }
-    umma_commit(bar);
-  }
-  ok = mbar_wait(bar, bar_phase);
-  bar_phase ^= 1;
-  ok = __syncthreads_and(ok);
-  tc_fence_after();
-
-  const int my_tok = s_tok[tid];
-  const int qh = my_tok >= 0 ? my_tok / win : 0;
-  const int qw = my_tok >= 0 ? my_tok - qh * win : 0;
-  if (ok) {
-    // relH[i][j] = P_H[i][qh - j + win - 1]: column c holds j = qh + win - 1 - c.
-    for (int c0 = 0; c0 < a.nt; c0 += 32) {
-      uint32_t rh[32], rw[32];
-      tmem_ld_32x32b_x32(t_lane + c0, rh);
-      tmem_ld_32x32b_x32(t_lane + 128 + c0, rw);
-      tmem_ld_wait();
-#pragma unroll
-      for (int j = 0; j < 32; ++j) {
-        const int jh = qh + win - 1 - (c0 + j);
-        if (jh >= 0 && jh < win) s_bias_h[jh * kAttnBM + tid] = __float2half_rn(__uint_as_float(rh[j]));
-        const int jw = qw + win - 1 - (c0 + j);
-        if (jw >= 0 && jw < win) s_bias_w[jw * kAttnBM + tid] = __float2half_rn(__uint_as_float(rw[j]));
-      }
-    }
-  }
-  tc_fence_before();
-  __syncthreads();  // tables consumed: the K/V region is free; bias visible to all threads
-
-  // ---- main loop over enabled key blocks ----
-  auto load_kv = [&](int i, int buf) {
-    const int kb = block_at(i);
-    const uint32_t sK = s_base + SM::kK0 + buf * SM::kKVBytes;
-    const uint32_t sV = s_base + SM::kV0 + buf * SM::kKVBytes;
-    if (tid < kAttnBN) {
-      const int kp = kb * kAttnBN + tid;
-      int info = -1;
-      if (kp < N) {
-        const int t = __ldg(perm + kp);
-        const int kh = t / win;
-        info = kh | ((t - kh * win) << 16);
-      }
-      s_kinfo[buf * kAttnBN + tid] = info;
-    }
-    for (int idx = tid; idx < kAttnBN * TG::kChunks; idx += kAttnThreads) {
-      const int r = idx / TG::kChunks, c = idx - r * TG::kChunks;
-      const int kp = kb * kAttnBN + r;
-      const int t = kp < N ? __ldg(perm + kp) : -1;
-      const int64_t off = static_cast<int64_t>(t) * a.ld_qkv + c * 8;
-      cp_async16(tile_chunk_addr<D>(sK, kAttnBN, r, c), t >= 0 ? static_cast<const void*>(k_base + off) : a.qkv,
-                 t >= 0 ? 16u : 0u);
-      cp_async16(tile_chunk_addr<D>(sV, kAttnBN, r, c), t >= 0 ? static_cast<const void*>(v_base + off) : a.qkv,
-                 t >= 0 ? 16u : 0u);
-    }
-    cp_async_commit();
+    return true;
   };
+  auto tile_exists = [&](int lt_) { return static_cast<int>(blockIdx.x) + lt_ * static_cast<int>(gridDim.x) < a.total_tiles; };
 
-  float o[D];
+  if (warp == 4) {
+    // =========================== loader warp ===========================
+    // Lane-per-row copies: a lane moves whole rows (kChunks x 16 B), so every
+    // cp.async address is a row base plus a compile-time chunk offset. The
+    // permutation indices of the next key block are fetched one block ahead.
+    // Order: Q(0), then per tile t: Q(t+1), K/V(t, blocks) — the UMMA warp
+    // computes P_H(t+1) from Q(t+1) while tile t runs.
+    auto copy_row = [&](uint32_t region, int rows, int r, const __nv_bfloat16* src) {
+      const uint32_t bytes = src != nullptr ? 16u : 0u;
+      const uint8_t* s0 = reinterpret_cast<const uint8_t*>(src != nullptr ? src : a.qkv);
 #pragma unroll
-  for (int c = 0; c < D; ++c) o[c] = 0.f;
-  float m_run = -INFINITY, l_run = 0.f;
-  const int my_mb = 2 * tile + (tid >= 64 ? 1 : 0);
-  const float log2e = 1.4426950408889634f;
-  const uint32_t sP = s_base + SM::kP;
-  const uint32_t idesc_s = make_idesc_bf16(kAttnBM, kAttnBN, 0, 0);
-  const uint32_t idesc_o64 = make_idesc_bf16(kAttnBM, 64, 0, 1);
-  const uint32_t idesc_o16 = make_idesc_bf16(kAttnBM, 16, 0, 1);
+      for (int c = 0; c < TG::kChunks; ++c)
+        cp_async16(tile_chunk_addr<D>(region, rows, r, c), s0 + (src != nullptr ? c * 16 : 0), bytes);
+    };
+    // one-hot regions start at zero; kinfo starts at -1 (nothing to clear)
+    for (int s = 0; s < C::kStages; ++s) {
+      uint4* oh = reinterpret_cast<uint4*>(smem + L.kv + s * LAY::kStage + 2 * TG::bytes(kAttnBN));
+      for (int i = lane; i < C::kOHBytes / 16; i += 32) oh[i] = make_uint4(0u, 0u, 0u, 0u);
+      for (int r = lane; r < kAttnBN; r += 32) s_kinfo[s * kAttnBN + r] = -1;
+    }
+    __syncwarp();
+    // rel-pos tables, once per CTA
+    const uint32_t sTh = sb + L.th, sTw = sb + L.tw;
+    const int trows = 2 * win - 1;
+    for (int r = lane; r < C::kNT; r += 32) {
+      copy_row(sTh, C::kNT, r, r < trows ? a.th + r * D : nullptr);
+      copy_row(sTw, C::kNT, r, r < trows ? a.tw + r * D : nullptr);
+    }
+    mbar_arrive(&bars[kBarTab]);
+    cp_async_arrive_noinc(&bars[kBarTab]);
 
-  if (ok && n_blocks > 0) load_kv(0, 0);
-  for (int i = 0; i < n_blocks && ok; ++i) {
-    const int buf = i & 1;
-    const int kb = block_at(i);
+    auto load_q = [&](int lt_) -> bool {
+      const int tile = blockIdx.x + lt_ * gridDim.x;
+      const int row = tile / a.n_tiles, qtile = tile - row * a.n_tiles;
+      const int seq = row / a.heads, head = row - seq * a.heads;
+      const int32_t* perm = a.perm + static_cast<int64_t>(row) * N;
+      const __nv_bfloat16* q_base = a.qkv + static_cast<int64_t>(seq) * N * a.ld_qkv + head * D;
+      int qt[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const int p = qtile * kAttnBM + lane + 32 * i;
+        qt[i] = p < N ? __ldg(perm + p) : -1;
+      }
+      const int qb = lt_ & 1;
+      if (!wait_or_abort(kBarQEmpty + qb, ((lt_ >> 1) & 1) ^ 1)) return false;
+      const uint32_t sQ = sb + L.q + qb * TG::bytes(kAttnBM);
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const int r = lane + 32 * i;
+        s_tok[qb * kAttnBM + r] = qt[i];
+        copy_row(sQ, kAttnBM, r, qt[i] >= 0 ? q_base + static_cast<int64_t>(qt[i]) * a.ld_qkv : nullptr);
+      }
+      mbar_arrive(&bars[kBarQFull + qb]);
+      cp_async_arrive_noinc(&bars[kBarQFull + qb]);
+      return true;
+    };
+
+    int g = 0;
+    bool ok = tile_exists(0) ? load_q(0) : true;
+    for (int lt = 0; ok && tile_exists(lt) && !*abort_flag; ++lt) {
+      if (tile_exists(lt + 1) && !(ok = load_q(lt + 1))) break;
+      const int tile = blockIdx.x + lt * gridDim.x;
+      const int row = tile / a.n_tiles, qtile = tile - row * a.n_tiles;
+      const int seq = row / a.heads, head = row - seq * a.heads;
+      const int32_t* perm = a.perm + static_cast<int64_t>(row) * N;
+      const __nv_bfloat16* k_base = a.qkv + static_cast<int64_t>(seq) * N * a.ld_qkv + a.C + head * D;
+      const TileBlocks tb(a, qtile);
+      int nt0 = -1, nt1 = -1;
+      if (tb.n > 0) {
+        const int kp = tb.at(0) * kAttnBN + lane;
+        nt0 = kp < N ? __ldg(perm + kp) : -1;
+        nt1 = kp + 32 < N ? __ldg(perm + kp + 32) : -1;
+      }
+      for (int j = 0; j < tb.n; ++j, ++g) {
+        const int t0 = nt0, t1 = nt1;
+        if (j + 1 < tb.n) {  // prefetch the next block's tokens
+          const int kp = tb.at(j + 1) * kAttnBN + lane;
+          nt0 = kp < N ? __ldg(perm + kp) : -1;
+          nt1 = kp + 32 < N ? __ldg(perm + kp + 32) : -1;
+        }
+        const int stage = g % C::kStages;
+        if (!(ok = wait_or_abort(kBarKVEmpty + stage, ((g / C::kStages) & 1) ^ 1))) break;
+        int* kinfo = s_kinfo + stage * kAttnBN;
+        const uint32_t sK = sb + L.kv + stage * LAY::kStage;
+        const uint32_t sV = sK + TG::bytes(kAttnBN);
+        uint8_t* oh_h = smem + L.kv + stage * LAY::kStage + 2 * TG::bytes(kAttnBN);
+        uint8_t* oh_w = oh_h + kAttnBN * C::kBW * 2;
+#pragma unroll
+        for (int i = 0; i < 2; ++i) {
+          const int r = lane + 32 * i;
+          const int t = i == 0 ? t0 : t1;
+          int info = -1;
+          if (t >= 0) {
+            const int kh = t / win;
+            info = kh | ((t - kh * win) << 16);
+          }
+          const int old = kinfo[r];
+          if (old >= 0) {  // clear the previous one-hot entries of this row
+            *reinterpret_cast<uint16_t*>(oh_h + bias_off<SMALL>(r, old & 0xffff)) = 0;
+            *reinterpret_cast<uint16_t*>(oh_w + bias_off<SMALL>(r, old >> 16)) = 0;
+          }
+          if (info >= 0) {
+            *reinterpret_cast<uint16_t*>(oh_h + bias_off<SMALL>(r, info & 0xffff)) = 0x3C00;  // fp16 1.0
+            *reinterpret_cast<uint16_t*>(oh_w + bias_off<SMALL>(r, info >> 16)) = 0x3C00;
+          }
+          kinfo[r] = info;
+          const __nv_bfloat16* krow = t >= 0 ? k_base + static_cast<int64_t>(t) * a.ld_qkv : nullptr;
+          copy_row(sK, kAttnBN, r, krow);
+          copy_row(sV, kAttnBN, r, krow != nullptr ? krow + a.C : nullptr);
+        }
+        fence_proxy_async_smem();  // one-hot rows (generic stores) -> UMMA reads
+        mbar_arrive(&bars[kBarKVFull + stage]);
+        cp_async_arrive_noinc(&bars[kBarKVFull + stage]);
+      }
+    }
     cp_async_wait_all();
-    fence_proxy_async_smem();
-    __syncthreads();
-    if (i + 1 < n_blocks) load_kv(i + 1, buf ^ 1);
-    const uint32_t sK = s_base + SM::kK0 + buf * SM::kKVBytes;
-    const uint32_t sV = s_base + SM::kV0 + buf * SM::kKVBytes;
+  } else if (warp == 5) {
+    // =========================== UMMA issuer ===========================
+    if (lane == 0) {
+      const uint32_t sTh = sb + L.th, sTw = sb + L.tw;
+      const uint32_t idesc_t = make_idesc_bf16(kAttnBM, C::kNT, 0, 0);
+      const uint32_t idesc_s = make_idesc_bf16(kAttnBM, kAttnBN, 0, 0);
+      const uint32_t idesc_b = make_idesc_f16(kAttnBM, kAttnBN);
+      const uint32_t idesc_o64 = make_idesc_bf16(kAttnBM, 64, 0, 1);
+      const uint32_t idesc_o16 = make_idesc_bf16(kAttnBM, 16, 0, 1);
+      bool ok = wait_or_abort(kBarTab, 0);
+      fence_proxy_async_smem();
 
-    // S = Q K^T -> TMEM columns [0, 64)
-    if (tid == 0) {
-      tc_fence_after();
+      auto issue_ph = [&](int lt_) -> bool {  // P_H / P_W of tile lt_
+        const int qb = lt_ & 1, pb = lt_ % C::kPH;
+        if (!wait_or_abort(kBarQFull + qb, (lt_ >> 1) & 1)) return false;
+        if (!wait_or_abort(kBarPHFree + pb, ((lt_ / C::kPH) & 1) ^ 1)) return false;
+        tc_fence_after();
+        fence_proxy_async_smem();
+        const uint32_t sQ = sb + L.q + qb * TG::bytes(kAttnBM);
+        const uint32_t tPH = tmem + C::kTmPH + pb * 2 * C::kNT;
 #pragma unroll
-      for (int ks = 0; ks < D / 16; ++ks)
-        umma_f16_ss(tmem, kmajor_desc<D>(sQ, kAttnBM, ks), kmajor_desc<D>(sK, kAttnBN, ks), idesc_s, ks > 0);
-      umma_commit(bar);
-    }
-    ok = mbar_wait(bar, bar_phase);
-    bar_phase ^= 1;
-    ok = __syncthreads_and(ok);
-    if (!ok) break;
-    tc_fence_after();
-
-    uint32_t s[64];
-    {
-      uint32_t (&s0)[32] = *reinterpret_cast<uint32_t(*)[32]>(&s[0]);
-      uint32_t (&s1)[32] = *reinterpret_cast<uint32_t(*)[32]>(&s[32]);
-      tmem_ld_32x32b_x32(t_lane, s0);
-      tmem_ld_32x32b_x32(t_lane + 32, s1);
-      tmem_ld_wait();
-    }
-    const bool row_on = (kb < nk) || (kb == my_mb);
-    const int* kinfo = s_kinfo + buf * kAttnBN;
-    float mx = -INFINITY;
-#pragma unroll
-    for (int j = 0; j < 64; ++j) {
-      const int info = kinfo[j];
-      float x = -INFINITY;
-      if (row_on && info >= 0) {
-        const float bh = __half2float(s_bias_h[(info & 0xffff) * kAttnBM + tid]);
-        const float bw = __half2float(s_bias_w[(info >> 16) * kAttnBM + tid]);
-        x = __uint_as_float(s[j]) * a.scale_log2 + (bh + bw) * log2e;
-      }
-      s[j] = __float_as_uint(x);
-      mx = fmaxf(mx, x);
-    }
-    const float m_new = fmaxf(m_run, mx);
-    const float m_use = m_new == -INFINITY ? 0.f : m_new;
-    const float alpha = fast_exp2(m_run - m_use);
-    float sum = 0.f;
-    uint8_t* prow = smem + SM::kP + tid * 128;
-#pragma unroll
-    for (int c = 0; c < 8; ++c) {
-      float pv[8];
-#pragma unroll
-      for (int e = 0; e < 8; ++e) {
-        pv[e] = fast_exp2(__uint_as_float(s[c * 8 + e]) - m_use);
-        sum += pv[e];
-      }
-      uint4 w;
-      w.x = pack_bf16x2(pv[0], pv[1]);
-      w.y = pack_bf16x2(pv[2], pv[3]);
-      w.z = pack_bf16x2(pv[4], pv[5]);
-      w.w = pack_bf16x2(pv[6], pv[7]);
-      *reinterpret_cast<uint4*>(prow + ((c ^ (tid & 7)) << 4)) = w;
-    }
-    l_run = l_run * alpha + sum;
-    m_run = m_new;
-
-    // O_blk = P V -> TMEM columns [128, 128 + D)
-    fence_proxy_async_smem();
-    tc_fence_before();
-    __syncthreads();
-    if (tid == 0) {
-      tc_fence_after();
-#pragma unroll
-      for (int ks = 0; ks < kAttnBN / 16; ++ks) {
-        const uint64_t pd = make_smem_desc(sP + ks * 32, 16, 1024, kSw128);
-        umma_f16_ss(tmem + 128, pd, make_smem_desc(sV + ks * 2048, 8192, 1024, kSw128), idesc_o64, ks > 0);
-        if constexpr (TG::kTail)
-          umma_f16_ss(tmem + 192, pd, make_smem_desc(sV + kAttnBN * 128 + ks * 512, 4096, 256, kSw32), idesc_o16,
+        for (int ks = 0; ks < D / 16; ++ks) {
+          umma_f16_ss(tPH, kmajor_desc<D>(sQ, kAttnBM, ks), kmajor_desc<D>(sTh, C::kNT, ks), idesc_t, ks > 0);
+          umma_f16_ss(tPH + C::kNT, kmajor_desc<D>(sQ, kAttnBM, ks), kmajor_desc<D>(sTw, C::kNT, ks), idesc_t,
                       ks > 0);
+        }
+        umma_commit(&bars[kBarPHFull + pb]);
+        return true;
+      };
+      auto issue_qk = [&](const BlockCursor& c) -> bool {
+        if (c.j == 0) {
+          if constexpr (SMALL) {
+            if (tile_exists(c.lt + 1) && !issue_ph(c.lt + 1)) return false;
+          } else {
+            if (!issue_ph(c.lt)) return false;
+          }
+          if (!wait_or_abort(kBarABFull + c.lt % C::kAB, (c.lt / C::kAB) & 1)) return false;
+        }
+        const int st = c.g % C::kStages, sbuf = c.g % C::kS;
+        if (!wait_or_abort(kBarKVFull + st, (c.g / C::kStages) & 1)) return false;
+        if (!wait_or_abort(kBarSFree + sbuf, ((c.g / C::kS) & 1) ^ 1)) return false;
+        tc_fence_after();
+        fence_proxy_async_smem();
+        const uint32_t sQ = sb + L.q + (c.lt & 1) * TG::bytes(kAttnBM);
+        const uint32_t sK = sb + L.kv + st * LAY::kStage;
+        const uint32_t sOH = sK + 2 * TG::bytes(kAttnBN);
+        const uint32_t sAB = sb + L.ab + (c.lt % C::kAB) * C::kABBytes;
+        const uint32_t tS = tmem + sbuf * kAttnBN;
+#pragma unroll
+        for (int ks = 0; ks < D / 16; ++ks)
+          umma_f16_ss(tS, kmajor_desc<D>(sQ, kAttnBM, ks), kmajor_desc<D>(sK, kAttnBN, ks), idesc_s, ks > 0);
+        // + A_bias . onehot^T  (relH / scale at kh, relW / scale at kw)
+#pragma unroll
+        for (int part = 0; part < 2; ++part) {
+          const uint32_t ab = sAB + part * kAttnBM * C::kBW * 2;
+          const uint32_t oh = sOH + part * kAttnBN * C::kBW * 2;
+          if constexpr (SMALL) {
+            umma_f16_ss(tS, make_smem_desc(ab, 16, 256, kSw32), make_smem_desc(oh, 16, 256, kSw32), idesc_b, 1u);
+          } else {
+#pragma unroll
+            for (int ks = 0; ks < 4; ++ks)
+              umma_f16_ss(tS, make_smem_desc(ab + ks * 32, 16, 1024, kSw128),
+                          make_smem_desc(oh + ks * 32, 16, 1024, kSw128), idesc_b, 1u);
+          }
+        }
+        umma_commit(&bars[kBarSFull + sbuf]);
+        if (c.j == c.tb.n - 1) umma_commit(&bars[kBarQEmpty + (c.lt & 1)]);
+        return true;
+      };
+      auto issue_pv = [&](const BlockCursor& c) -> bool {
+        if (!wait_or_abort(kBarPFull + (c.g & 1), (c.g >> 1) & 1)) return false;
+        const int ob = c.lt % C::kO;
+        if (c.j == 0 && !wait_or_abort(kBarOFree + ob, ((c.lt / C::kO) & 1) ^ 1)) return false;
+        tc_fence_after();
+        fence_proxy_async_smem();
+        const int st = c.g % C::kStages;
+        const uint32_t sP = sb + L.p + (c.g & 1) * (kAttnBM * 128);
+        const uint32_t sV = sb + L.kv + st * LAY::kStage + TG::bytes(kAttnBN);
+        const uint32_t tO = tmem + C::kTmO + ob * D;
+#pragma unroll
+        for (int ks = 0; ks < kAttnBN / 16; ++ks) {
+          const uint64_t pd = make_smem_desc(sP + ks * 32, 16, 1024, kSw128);
+          const uint32_t acc = (c.j > 0 || ks > 0) ? 1u : 0u;
+          umma_f16_ss(tO, pd, make_smem_desc(sV + ks * 2048, 8192, 1024, kSw128), idesc_o64, acc);
+          if constexpr (TG::kTail)
+            umma_f16_ss(tO + 64, pd, make_smem_desc(sV + kAttnBN * 128 + ks * 512, 4096, 256, kSw32), idesc_o16, acc);
+        }
+        umma_commit(&bars[kBarODone + (c.g & 1)]);
+        umma_commit(&bars[kBarKVEmpty + st]);
+        return true;
+      };
+
+      if (ok && SMALL && tile_exists(0)) ok = issue_ph(0);
+      BlockCursor cq, cp;
+      cq.start(a);
+      cp.start(a);
+      while (ok && !cp.done) {
+        while (ok && !cq.done && cq.g < cp.g + C::kS) {
+          ok = issue_qk(cq);
+          cq.advance(a);
+        }
+        if (!ok) break;
+        ok = issue_pv(cp);
+        cp.advance(a);
       }
-      umma_commit(bar);
+      umma_commit(&bars[kBarDrain]);
+      mbar_wait(&bars[kBarDrain], 0);
     }
-    ok = mbar_wait(bar, bar_phase);
-    bar_phase ^= 1;
-    ok = __syncthreads_and(ok);
-    if (!ok) break;
-    tc_fence_after();
-    {
-      uint32_t r[32];
-      tmem_ld_32x32b_x32(t_lane + 128, r);
-      tmem_ld_wait();
-#pragma unroll
-      for (int c = 0; c < 32; ++c) o[c] = o[c] * alpha + __uint_as_float(r[c]);
-      tmem_ld_32x32b_x32(t_lane + 160, r);
-      tmem_ld_wait();
-#pragma unroll
-      for (int c = 0; c < 32; ++c) o[32 + c] = o[32 + c] * alpha + __uint_as_float(r[c]);
-      if constexpr (D > 64) {
-        uint32_t r16[16];
-        tmem_ld_32x32b_x16(t_lane + 192, r16);
+  } else {
+    // ======================== softmax warpgroup ========================
+    const uint32_t t_lane = tmem + (static_cast<uint32_t>(warp * 32) << 16);
+
+    // rel-pos bias of tile lt_ -> A_bias[lt_ % kAB] row tid (fp16, relH/scale at column j)
+    auto extract_bias = [&](int lt_, int& tok_out) -> bool {
+      const int qb = lt_ & 1, pb = lt_ % C::kPH;
+      if (!wait_or_abort(kBarQFull + qb, (lt_ >> 1) & 1)) return false;
+      const int t = s_tok[qb * kAttnBM + tid];
+      tok_out = t;
+      const int qh = t >= 0 ? t / win : 0;
+      const int qw = t >= 0 ? t - qh * win : 0;
+      if (!wait_or_abort(kBarPHFull + pb, (lt_ / C::kPH) & 1)) return false;
+      tc_fence_after();
+      uint8_t* ab_h = smem + L.ab + (lt_ % C::kAB) * C::kABBytes;
+      uint8_t* ab_w = ab_h + kAttnBM * C::kBW * 2;
+      const uint32_t tPH = t_lane + C::kTmPH + pb * 2 * C::kNT;
+      for (int c0 = 0; c0 < C::kNT; c0 += 32) {
+        uint32_t rh[32], rw[32];
+        tmem_ld_32x32b_x32(tPH + c0, rh);
+        tmem_ld_32x32b_x32(tPH + C::kNT + c0, rw);
         tmem_ld_wait();
 #pragma unroll
-        for (int c = 0; c < 16; ++c) o[64 + c] = o[64 + c] * alpha + __uint_as_float(r16[c]);
+        for (int j = 0; j < 32; ++j) {
+          const int jh = qh + win - 1 - (c0 + j);
+          if (jh >= 0 && jh < win)
+            *reinterpret_cast<__half*>(ab_h + bias_off<SMALL>(tid, jh)) =
+                __float2half_rn(__uint_as_float(rh[j]) * a.inv_scale);
+          const int jw = qw + win - 1 - (c0 + j);
+          if (jw >= 0 && jw < win)
+            *reinterpret_cast<__half*>(ab_w + bias_off<SMALL>(tid, jw)) =
+                __float2half_rn(__uint_as_float(rw[j]) * a.inv_scale);
+        }
       }
-    }
-    tc_fence_before();
-  }
-
-  // ---- epilogue: normalise and store at the raster position (inverse permutation) ----
-  if (ok && my_tok >= 0) {
-    const float inv_l = l_run > 0.f ? 1.f / l_run : 0.f;
-    uint4* dst = reinterpret_cast<uint4*>(a.out + (static_cast<int64_t>(seq) * N + my_tok) * a.ld_out + head * D);
+      for (int j = win; j < C::kBW; ++j) {  // padding columns must not hold NaN/Inf
+        *reinterpret_cast<__half*>(ab_h + bias_off<SMALL>(tid, j)) = __float2half_rn(0.f);
+        *reinterpret_cast<__half*>(ab_w + bias_off<SMALL>(tid, j)) = __float2half_rn(0.f);
+      }
+      fence_proxy_async_smem();
+      tc_fence_before();
+      mbar_arrive(&bars[kBarABFull + lt_ % C::kAB]);
+      mbar_arrive(&bars[kBarPHFree + pb]);
+      return true;
+    };
+    // O / l of tile lt_, stored at the raster token (inverse permutation and head merge)
+    auto epilogue = [&](int lt_, int g_last, int tok, float l) -> bool {
+      const int tile = blockIdx.x + lt_ * gridDim.x;
+      const int row = tile / a.n_tiles;
+      const int seq = row / a.heads, head = row - seq * a.heads;
+      if (g_last >= 0 && !wait_or_abort(kBarODone + (g_last & 1), (g_last >> 1) & 1)) return false;
+      tc_fence_after();
+      const float inv_l = l > 0.f ? 1.f / l : 0.f;
+      uint4* dst = tok >= 0 ? reinterpret_cast<uint4*>(a.out + (static_cast<int64_t>(seq) * N + tok) * a.ld_out +
+                                                       head * D)
+                            : nullptr;
+      const uint32_t tO = t_lane + C::kTmO + (lt_ % C::kO) * D;
 #pragma unroll
-    for (int c = 0; c < D / 8; ++c) {
-      uint4 w;
-      w.x = pack_bf16x2(o[8 * c + 0] * inv_l, o[8 * c + 1] * inv_l);
-      w.y = pack_bf16x2(o[8 * c + 2] * inv_l, o[8 * c + 3] * inv_l);
-      w.z = pack_bf16x2(o[8 * c + 4] * inv_l, o[8 * c + 5] * inv_l);
-      w.w = pack_bf16x2(o[8 * c + 6] * inv_l, o[8 * c + 7] * inv_l);
-      dst[c] = w;
+      for (int c0 = 0; c0 < D; c0 += 16) {
+        uint32_t r16[16];
+        tmem_ld_32x32b_x16(tO + c0, r16);
+        tmem_ld_wait();
+        if (dst != nullptr) {
+          float o[16];
+#pragma unroll
+          for (int e = 0; e < 16; ++e) o[e] = g_last >= 0 ? __uint_as_float(r16[e]) * inv_l : 0.f;
+          dst[c0 / 8] = make_uint4(pack_bf16x2(o[0], o[1]), pack_bf16x2(o[2], o[3]), pack_bf16x2(o[4], o[5]),
+                                   pack_bf16x2(o[6], o[7]));
+          dst[c0 / 8 + 1] = make_uint4(pack_bf16x2(o[8], o[9]), pack_bf16x2(o[10], o[11]),
+                                       pack_bf16x2(o[12], o[13]), pack_bf16x2(o[14], o[15]));
+        }
+      }
+      tc_fence_before();
+      mbar_arrive(&bars[kBarOFree + lt_ % C::kO]);
+      return true;
+    };
+
+    bool ok = true;
+    int tok_cur = -1, tok_next = -1;
+    if (tile_exists(0)) ok = extract_bias(0, tok_cur);
+    int pend_lt = -1, pend_g = -1, pend_tok = -1;  // deferred epilogue
+    float pend_l = 0.f;
+    int g = 0;
+    for (int lt = 0; ok && tile_exists(lt); ++lt) {
+      const int tile = blockIdx.x + lt * gridDim.x;
+      const int qtile = tile % a.n_tiles;
+      const TileBlocks tb(a, qtile);
+      const int my_mb = 2 * qtile + (tid >= 64 ? 1 : 0);
+      const uint32_t tO = t_lane + C::kTmO + (lt % C::kO) * D;
+      float m_run = -INFINITY, l_run = 0.f;
+      for (int j = 0; j < tb.n; ++j, ++g) {
+        const int st = g % C::kStages, sbuf = g % C::kS;
+        const int kb = tb.at(j);
+        if (!(ok = wait_or_abort(kBarKVFull + st, (g / C::kStages) & 1))) break;  // kinfo visibility
+        if (!(ok = wait_or_abort(kBarSFull + sbuf, (g / C::kS) & 1))) break;
+        tc_fence_after();
+        uint32_t s[64];
+        {
+          uint32_t (&s0)[32] = *reinterpret_cast<uint32_t(*)[32]>(&s[0]);
+          uint32_t (&s1)[32] = *reinterpret_cast<uint32_t(*)[32]>(&s[32]);
+          tmem_ld_32x32b_x32(t_lane + sbuf * kAttnBN, s0);
+          tmem_ld_32x32b_x32(t_lane + sbuf * kAttnBN + 32, s1);
+          tmem_ld_wait();
+        }
+        tc_fence_before();
+        mbar_arrive(&bars[kBarSFree + sbuf]);
+
+        const bool full = kb < tb.nk && (kb + 1) * kAttnBN <= N;
+        float mx = -INFINITY;
+        if (full) {
+#pragma unroll
+          for (int jj = 0; jj < 64; ++jj) {
+            const float x = __uint_as_float(s[jj]) * a.scale_log2;
+            s[jj] = __float_as_uint(x);
+            mx = fmaxf(mx, x);
+          }
+        } else {
+          const int* kinfo = s_kinfo + st * kAttnBN;
+          const bool row_on = (kb < tb.nk) || (kb == my_mb);
+#pragma unroll
+          for (int jj = 0; jj < 64; ++jj) {
+            const float x = (row_on && kinfo[jj] >= 0) ? __uint_as_float(s[jj]) * a.scale_log2 : -INFINITY;
+            s[jj] = __float_as_uint(x);
+            mx = fmaxf(mx, x);
+          }
+        }
+        const float m_new = fmaxf(m_run, mx);
+        float m_use = m_run;
+        bool rescale = false;
+        if (j == 0) {
+          m_use = m_new;
+        } else if (m_new > m_run + kRescaleThreshold) {
+          m_use = m_new;
+          rescale = true;
+        }
+        const float m_off = m_use == -INFINITY ? 0.f : m_use;
+        const float alpha = rescale ? fast_exp2(m_run - m_use) : 1.f;
+        float sum = 0.f;
+        uint32_t pk[32];
+#pragma unroll
+        for (int e = 0; e < 32; ++e) {
+          const float p0 = fast_exp2(__uint_as_float(s[2 * e]) - m_off);
+          const float p1 = fast_exp2(__uint_as_float(s[2 * e + 1]) - m_off);
+          sum += p0 + p1;
+          pk[e] = pack_bf16x2(p0, p1);
+        }
+        l_run = (j == 0 ? 0.f : l_run * alpha) + sum;
+        m_run = m_use;
+        // P buffer g&1 was last read by PV(g-2)
+        if (g >= 2 && !(ok = wait_or_abort(kBarODone + (g & 1), ((g >> 1) - 1) & 1))) break;
+        // tcgen05.ld/st are warp-collective (.sync.aligned): the O rescale runs on
+        // the whole warp when any of its rows needs it (the others scale by 1).
+        if (__any_sync(0xffffffffu, rescale)) {
+          if (!(ok = wait_or_abort(kBarODone + ((g - 1) & 1), ((g - 1) >> 1) & 1))) break;
+          tc_fence_after();
+#pragma unroll
+          for (int c0 = 0; c0 < D; c0 += 16) {
+            uint32_t r16[16];
+            tmem_ld_32x32b_x16(tO + c0, r16);
+            tmem_ld_wait();
+#pragma unroll
+            for (int e = 0; e < 16; ++e) r16[e] = __float_as_uint(__uint_as_float(r16[e]) * alpha);
+            tmem_st_32x32b_x16(tO + c0, r16);
+          }
+          tmem_st_wait();
+        }
+        uint8_t* prow = smem + L.p + (g & 1) * (kAttnBM * 128) + tid * 128;
+#pragma unroll
+        for (int c = 0; c < 8; ++c)
+          *reinterpret_cast<uint4*>(prow + ((c ^ (tid & 7)) << 4)) =
+              make_uint4(pk[4 * c], pk[4 * c + 1], pk[4 * c + 2], pk[4 * c + 3]);
+        fence_proxy_async_smem();
+        tc_fence_before();
+        mbar_arrive(&bars[kBarPFull + (g & 1)]);
+
+        if (SMALL && j == 0) {
+          // bias of the next tile and the previous tile's epilogue, off the critical path
+          if (tile_exists(lt + 1) && !(ok = extract_bias(lt + 1, tok_next))) break;
+          if (pend_lt >= 0 && !(ok = epilogue(pend_lt, pend_g, pend_tok, pend_l))) break;
+          pend_lt = -1;
+        }
+      }
+      if (!ok) break;
+      if constexpr (SMALL) {
+        pend_lt = lt;
+        pend_g = tb.n > 0 ? g - 1 : -1;
+        pend_tok = tok_cur;
+        pend_l = l_run;
+      } else {
+        if (tile_exists(lt + 1) && !(ok = extract_bias(lt + 1, tok_next))) break;
+        if (!(ok = epilogue(lt, tb.n > 0 ? g - 1 : -1, tok_cur, l_run))) break;
+      }
+      tok_cur = tok_next;
     }
+    if (ok && pend_lt >= 0) epilogue(pend_lt, pend_g, pend_tok, pend_l);
   }
 
-  // ---- teardown: drain copies and MMAs, free TMEM ----
-  cp_async_wait_all();
-  if (!ok && tid == 0) {
-    umma_commit(bar);
-    mbar_wait(bar, bar_phase);
-  }
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
-  if (warp == 0) tmem_dealloc(tmem, kAttnTmemCols);
+  if (warp == 5) tmem_dealloc(tmem, kAttnTmemCols);
 }
 
-template <int D>
-static int launch_attn(const AttnParams& p, int n_rows, cudaStream_t stream) {
-  using SM = AttnSmem<D>;
-  // At least 96 KB so that no more than two CTAs share an SM: two CTAs x 256
-  // TMEM columns fill the 512-column TMEM exactly.
-  const int smem = SM::total(p.win) > 96 * 1024 ? SM::total(p.win) : 96 * 1024;
+template <int D, bool SMALL>
+static int launch_attn(const AttnParams& p, cudaStream_t stream) {
+  const AttnLayout<D, SMALL> L(p.win);
   static bool configured[64] = {false};
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return SSAM_ERR_CUDA;
   if (!configured[dev]) {
-    if (cudaFuncSetAttribute(sparse_attn_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             SM::total(64) > 96 * 1024 ? SM::total(64) : 96 * 1024) != cudaSuccess)
+    if (cudaFuncSetAttribute(sparse_attn_kernel<D, SMALL>, cudaFuncAttributeMaxDynamicSharedMemorySize, L.total) !=
+        cudaSuccess)
       return SSAM_ERR_CUDA;
     configured[dev] = true;
   }
-  const int64_t grid = static_cast<int64_t>((p.N + kAttnBM - 1) / kAttnBM) * n_rows;
-  if (grid > INT32_MAX) return SSAM_ERR_UNSUPPORTED;
-  sparse_attn_kernel<D><<<static_cast<unsigned>(grid), kAttnThreads, smem, stream>>>(p);
+  // One persistent CTA per SM (the plan exceeds half the SM's shared memory),
+  // so its 512 TMEM columns are always available.
+  const int smem = L.total > 116 * 1024 ? L.total : 116 * 1024;
+  const int sms = num_sms(dev);
+  const int grid = p.total_tiles < sms ? p.total_tiles : sms;
+  sparse_attn_kernel<D, SMALL><<<grid, kAttnThreads, smem, stream>>>(p);
   return status_from_cuda(cudaGetLastError());
 }
 
@@ -432,6 +741,7 @@ int sparse_attn_fwd(const void* qkv, int64_t ld_qkv, int n_seq, int heads, int w
   if (n_seq <= 0 || heads <= 0 || win <= 0 || n_init_blocks < 0) return SSAM_ERR_INVALID;
   if (d != 64 && d != 80) return SSAM_ERR_UNSUPPORTED;
   if (win > 64) return SSAM_ERR_UNSUPPORTED;  // 2*win-1 table rows must fit one 128-wide MMA
+  if (!(scale > 0.f)) return SSAM_ERR_INVALID;
   const int C = heads * d;
   if (ld_qkv < 3 * C || ld_out < C) return SSAM_ERR_INVALID;
   if (ld_qkv % 8 || ld_out % 8 || !aligned16(qkv) || !aligned16(out) || !aligned16(rel_pos_h) ||
@@ -452,9 +762,14 @@ int sparse_attn_fwd(const void* qkv, int64_t ld_qkv, int n_seq, int heads, int w
   p.scale_log2 = scale * 1.4426950408889634f;
   p.out = static_cast<__nv_bfloat16*>(out);
   p.ld_out = ld_out;
-  p.nt = (2 * win - 1) <= 32 ? 32 : 128;
-  const int n_rows = n_seq * heads;
-  return d == 64 ? launch_attn<64>(p, n_rows, stream) : launch_attn<80>(p, n_rows, stream);
+  p.inv_scale = 1.0f / scale;
+  p.n_tiles = (p.N + kAttnBM - 1) / kAttnBM;
+  const int64_t total = static_cast<int64_t>(p.n_tiles) * n_seq * heads;
+  if (total > INT32_MAX) return SSAM_ERR_UNSUPPORTED;
+  p.total_tiles = static_cast<int>(total);
+  const bool small = win <= 16;  // 32-row tables, 16-wide bias operands
+  if (d == 64) return small ? launch_attn<64, true>(p, stream) : launch_attn<64, false>(p, stream);
+  return small ? launch_attn<80, true>(p, stream) : launch_attn<80, false>(p, stream);
 }
 
 }  // namespace ssam

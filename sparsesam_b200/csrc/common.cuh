@@ -28,6 +28,7 @@ __device__ __forceinline__ void set_device_error(int code) {
 // Upper bound on any spin-wait: about two seconds of GPU time.
 constexpr uint64_t kWaitTimeoutNs = 2000000000ull;
 constexpr uint32_t kWaitMaxIters = 0x7fffffffu;
+constexpr long long kWaitTimeoutCycles = 4000000000ll;  // ~2 s at 2 GHz (second, independent bound)
 
 __device__ __forceinline__ uint64_t globaltimer_ns() {
   uint64_t t;
@@ -83,9 +84,12 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
 __device__ __noinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
   if (mbar_try_wait(bar, parity)) return true;
   const uint64_t t0 = globaltimer_ns();
+  const long long c0 = clock64();
   for (uint32_t it = 0; it < kWaitMaxIters; ++it) {
     if (mbar_try_wait(bar, parity)) return true;
-    if ((it & 1023u) == 1023u && globaltimer_ns() - t0 > kWaitTimeoutNs) break;
+    if ((it & 255u) == 255u &&
+        (globaltimer_ns() - t0 > kWaitTimeoutNs || clock64() - c0 > kWaitTimeoutCycles))
+      break;
   }
   set_device_error(SSAM_ERR_TIMEOUT);
   return false;

@@ -2,12 +2,13 @@
 //
 //   acc[r, n] = sum_k A[r, k] * B[n, k]      A: M x K, B: N x K (both K-major)
 //
-// Roles per CTA (one CTA per SM, 192 threads):
+// Roles per CTA (one CTA per SM, 320 threads):
 //   warp 0      : TMA producer — 128x64 A tile + 256x64 B tile per stage (SW128).
 //   warp 1      : UMMA issuer  — tcgen05.mma M=128 N=256 K=16, fp32 accumulator
 //                 in TMEM, two accumulator buffers (2 x 256 columns).
-//   warps 2..5  : epilogue     — tcgen05.ld rows out of TMEM, fused bias /
-//                 GELU / fp32 residual add through an optional row map.
+//   warps 2..9  : epilogue     — tcgen05.ld rows out of TMEM (two warps per TMEM
+//                 sub-partition, each taking half of the 256 columns), fused
+//                 bias / GELU / fp32 residual add through an optional row map.
 // Every wait is bounded; on timeout the CTA records SSAM_ERR_TIMEOUT, drains the
 // copies and MMAs it issued, frees TMEM and returns.
 //
@@ -25,7 +26,8 @@ constexpr int kGemmStages = 4;
 constexpr int kGemmABytes = kGemmBM * kGemmBK * 2;  // 16 KB
 constexpr int kGemmBBytes = kGemmBN * kGemmBK * 2;  // 32 KB
 constexpr int kGemmStageBytes = kGemmABytes + kGemmBBytes;
-constexpr int kGemmThreads = 192;
+constexpr int kGemmThreads = 320;
+constexpr int kGemmEpiThreads = 256;
 constexpr int kGemmTmemCols = 512;
 constexpr int kGemmSmemBytes = kGemmStages * kGemmStageBytes + 1024 /*align slack*/ + 256 /*barriers*/;
 
@@ -118,7 +120,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(&tfull_bar[a], 1);
-      mbar_init(&tempty_bar[a], 128);
+      mbar_init(&tempty_bar[a], kGemmEpiThreads);
     }
     mbar_init(drain_bar, 1);
     *abort_flag = 0;
@@ -217,8 +219,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       mbar_wait(drain_bar, 0);
     }
   } else {
-    // ---------------- epilogue warps 2..5 ----------------
-    const int sp = warp & 3;  // TMEM sub-partition this warp may access
+    // ---------------- epilogue warps 2..9 ----------------
+    const int sp = warp & 3;                   // TMEM sub-partition this warp may access
+    const int half = (warp - 2) >> 2;          // which 128-column half of the tile
     const int row_in_tile = sp * 32 + lane;
     int local = 0;
     for (int tile = blockIdx.x; tile < num_tiles && !*abort_flag; tile += gridDim.x, ++local) {
@@ -234,7 +237,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       const int row = mb * kGemmBM + row_in_tile;
       const uint32_t t_row = tmem_base + (static_cast<uint32_t>(sp * 32) << 16) + static_cast<uint32_t>(acc * kGemmBN);
 #pragma unroll 1
-      for (int c = 0; c < kGemmBN; c += 32) {
+      for (int c = half * (kGemmBN / 2); c < (half + 1) * (kGemmBN / 2); c += 32) {
         const int col0 = nb * kGemmBN + c;
         if (col0 >= p.N) break;  // warp-uniform
         uint32_t r[32];
