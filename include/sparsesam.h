@@ -181,6 +181,26 @@ int ssam_nhwc_to_nchw(const float* in, int B, int HW, int C, float* out, void* s
 int ssam_layernorm_rows(const float* x, int n_rows, int C, const float* w, const float* b, float eps,
                         void* out, int out_bf16, void* stream);
 
+/* ---------------------------------------------------------------------------
+ * ssam_rc_mlp_fwd for callers that cannot allocate device memory at call time
+ * (a host with a fixed, pre-reserved device memory budget, or a foreign-language
+ * binding without a device allocator). Same arguments and result as
+ * ssam_rc_mlp_fwd, minus the workspace: the intermediates live in a 32 MiB
+ * scratch array inside the library that every device loading the library keeps
+ * until process exit. No counterpart in the reference (its MLP path allocates
+ * through PyTorch).
+ *   - Returns SSAM_ERR_UNSUPPORTED when ssam_rc_mlp_workspace_size(n_rows, C,
+ *     hidden) exceeds 32 MiB (about 2,600 rows at C = 1280, hidden = 5120).
+ *   - The first call on a device resolves the scratch address for that device;
+ *     make it before any CUDA stream capture starts.
+ *   - All calls share the one scratch array: calls that may overlap on the GPU
+ *     (different streams, or several host threads) race on it; serialise them.
+ *   - Allocates nothing (no cudaMalloc / cudaFree, no library allocator).
+ * ------------------------------------------------------------------------- */
+int ssam_rc_mlp_fwd_noalloc(float* x, int64_t ldx, const int32_t* rows, int n_rows, int C, int hidden,
+                            const float* ln_w, const float* ln_b, float eps, const void* w1, const float* b1,
+                            const void* w2, const float* b2, void* stream);
+
 /* hi/lo split of fp32 rows into bf16: out[r] = [bf16(x[r]) | bf16(x[r] - bf16(x[r]))]
  * (2*C columns). A GEMM of the split rows against [W | W] carries the fp32
  * activation into the tensor-core GEMM (used for the neck convolutions). */

@@ -45,6 +45,8 @@ SIGNATURES: dict[str, tuple] = {
     "ssam_nhwc_to_nchw": (c_int, [c_ptr, c_int, c_int, c_int, c_ptr, c_ptr]),
     "ssam_layernorm_rows": (c_int, [c_ptr, c_int, c_int, c_ptr, c_ptr, c_f32, c_ptr, c_int, c_ptr]),
     "ssam_split_bf16x2": (c_int, [c_ptr, c_int, c_int, c_ptr, c_ptr]),
+    "ssam_rc_mlp_fwd_noalloc": (c_int, [c_ptr, c_i64, c_ptr, c_int, c_int, c_int, c_ptr, c_ptr, c_f32, c_ptr, c_ptr,
+                                        c_ptr, c_ptr, c_ptr]),
 }
 
 SSAM_OK = 0
@@ -67,7 +69,7 @@ KERNELS_PER_CALL = {
     "ssam_zorder": 1, "ssam_stripe_sort_perm": 1, "ssam_sparse_attn_fwd": 1, "ssam_keep_select": 1,
     "ssam_layernorm_gather": 1, "ssam_window_rows": 1, "ssam_gemm_bf16": 1, "ssam_rc_mlp_fwd": 3,
     "ssam_patch_im2col": 1, "ssam_broadcast_rows": 1, "ssam_im2col3x3_nhwc": 1, "ssam_nhwc_to_nchw": 1,
-    "ssam_layernorm_rows": 1, "ssam_split_bf16x2": 1,
+    "ssam_layernorm_rows": 1, "ssam_split_bf16x2": 1, "ssam_rc_mlp_fwd_noalloc": 3,
 }
 launch_count = 0  # kernels enqueued through call() since import (read by bench.py)
 
