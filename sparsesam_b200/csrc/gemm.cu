@@ -256,6 +256,213 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   if (warp == 1) tmem_dealloc(tmem_base, kGemmTmemCols);
 }
 
+// ===========================================================================
+// 2-SM variant: a cluster of two CTAs computes a 256x256 tile with
+// tcgen05.mma.cta_group::2 (M=256, N=256, K=16). CTA r of the pair loads rows
+// [r*128, r*128+128) of the A tile and of the B tile (6 stages x 32 KB) and owns
+// accumulator rows [r*128, r*128+128) in its TMEM. Both CTAs' TMA loads
+// complete on the leader's (rank 0) full barrier; the leader's commits are
+// multicast to both CTAs' empty / tmem-full barriers; both CTAs' epilogue
+// threads release the accumulator on the leader's tmem-empty barrier.
+// Per SM this halves the B tile held in shared memory and the TMA traffic per
+// MMA compared with the 1-SM kernel.
+// ===========================================================================
+constexpr int kPairBM = 256;  // rows per CTA pair (128 per CTA)
+constexpr int kPairStages = 6;
+constexpr int kPairABytes = 128 * kGemmBK * 2;  // 16 KB
+constexpr int kPairBBytes = 128 * kGemmBK * 2;  // 16 KB (half of the 256-column B tile)
+constexpr int kPairStageBytes = kPairABytes + kPairBBytes;
+constexpr int kPairSmemBytes = kPairStages * kPairStageBytes + 1024 + 256;
+
+template <int EPI>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGemmThreads, 1)
+    gemm_bf16_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                          const GemmParams p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sA = smem;
+  uint8_t* sB = smem + kPairStages * kPairABytes;
+  uint64_t* full_bar = reinterpret_cast<uint64_t*>(smem + kPairStages * kPairStageBytes);
+  uint64_t* empty_bar = full_bar + kPairStages;
+  uint64_t* tfull_bar = empty_bar + kPairStages;  // [2]
+  uint64_t* tempty_bar = tfull_bar + 2;           // [2] (used on the leader)
+  uint64_t* drain_bar = tempty_bar + 2;           // [1]
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(drain_bar + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_ctarank();
+  const bool leader = rank == 0;
+  const int pair = blockIdx.x >> 1;
+  const int n_pairs = gridDim.x >> 1;
+  const int m_tiles = (p.M + kPairBM - 1) / kPairBM;
+  const int n_tiles = (p.N + kGemmBN - 1) / kGemmBN;
+  const int num_tiles = m_tiles * n_tiles;
+  const int kblocks = (p.K + kGemmBK - 1) / kGemmBK;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kPairStages; ++s) {
+      mbar_init(&full_bar[s], 1);
+      mbar_init(&empty_bar[s], 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&tfull_bar[a], 1);
+      mbar_init(&tempty_bar[a], 2 * kGemmEpiThreads / 32);  // one arrive per epilogue warp of both CTAs
+    }
+    mbar_init(drain_bar, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 1) {
+    tmem_alloc_pair(tmem_holder, kGemmTmemCols);
+    tmem_relinquish_pair();
+  }
+  tc_fence_before();
+  cluster_sync_all();  // barriers of both CTAs initialised before any cross-CTA use
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_holder;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      // ---------------- TMA producer (both CTAs) ----------------
+      tma_prefetch_desc(&tmA);
+      tma_prefetch_desc(&tmB);
+      int stage = 0;
+      uint32_t phase = 0;
+      uint32_t issued_mask = 0, issued_parity = 0;
+      for (int tile = pair; tile < num_tiles && !*abort_flag; tile += n_pairs) {
+        const int mb = tile / n_tiles;
+        const int nb = tile - mb * n_tiles;
+        for (int kb = 0; kb < kblocks; ++kb) {
+          if (!mbar_wait(&empty_bar[stage], phase ^ 1)) {
+            *abort_flag = 1;
+            break;
+          }
+          const uint32_t bar = mapa_shared(smem_u32(&full_bar[stage]), 0);
+          if (leader) mbar_arrive_expect_tx(&full_bar[stage], 2 * kPairStageBytes);
+          tma_load_2d_pair(sA + stage * kPairABytes, &tmA, bar, kb * kGemmBK, mb * kPairBM + rank * 128);
+          tma_load_2d_pair(sB + stage * kPairBBytes, &tmB, bar, kb * kGemmBK, nb * kGemmBN + rank * 128);
+          issued_mask |= 1u << stage;
+          issued_parity = (issued_parity & ~(1u << stage)) | (phase << stage);
+          if (++stage == kPairStages) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+      }
+      if (*abort_flag && leader) {
+        for (int s = 0; s < kPairStages; ++s)
+          if (issued_mask & (1u << s)) mbar_wait(&full_bar[s], (issued_parity >> s) & 1u);
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0 && leader) {
+      // ---------------- UMMA issuer (leader CTA) ----------------
+      const uint32_t idesc = make_idesc_bf16(kPairBM, kGemmBN, 0, 0);
+      int stage = 0;
+      uint32_t phase = 0;
+      int local = 0;
+      for (int tile = pair; tile < num_tiles && !*abort_flag; tile += n_pairs, ++local) {
+        const int acc = local & 1;
+        const uint32_t acc_phase = (local >> 1) & 1;
+        if (!mbar_wait(&tempty_bar[acc], acc_phase ^ 1)) {
+          *abort_flag = 1;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * kGemmBN);
+        bool ok = true;
+        for (int kb = 0; kb < kblocks; ++kb) {
+          if (!mbar_wait(&full_bar[stage], phase)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a0 = smem_u32(sA + stage * kPairABytes);
+          const uint32_t b0 = smem_u32(sB + stage * kPairBBytes);
+#pragma unroll
+          for (int k = 0; k < kGemmBK / 16; ++k) {
+            const uint64_t ad = make_smem_desc(a0 + k * 32, 16, 1024, kSw128);
+            const uint64_t bd = make_smem_desc(b0 + k * 32, 16, 1024, kSw128);
+            umma_f16_ss_pair(d_tmem, ad, bd, idesc, (kb | k) != 0 ? 1u : 0u);
+          }
+          umma_commit_pair(&empty_bar[stage], 0x3);
+          if (++stage == kPairStages) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+        if (!ok) {
+          *abort_flag = 1;
+          break;
+        }
+        umma_commit_pair(&tfull_bar[acc], 0x3);
+      }
+      umma_commit_pair(drain_bar, 0x1);
+      mbar_wait(drain_bar, 0);
+    }
+  } else {
+    // ---------------- epilogue warps 2..9 (both CTAs) ----------------
+    const int sp = warp & 3;
+    const int half = (warp - 2) >> 2;
+    const int row_in_tile = static_cast<int>(rank) * 128 + sp * 32 + lane;
+    const uint32_t tempty0 = mapa_shared(smem_u32(&tempty_bar[0]), 0);
+    const uint32_t tempty1 = mapa_shared(smem_u32(&tempty_bar[1]), 0);
+    int local = 0;
+    for (int tile = pair; tile < num_tiles && !*abort_flag; tile += n_pairs, ++local) {
+      const int mb = tile / n_tiles;
+      const int nb = tile - mb * n_tiles;
+      const int acc = local & 1;
+      const uint32_t acc_phase = (local >> 1) & 1;
+      if (!mbar_wait(&tfull_bar[acc], acc_phase)) {
+        *abort_flag = 1;
+        break;
+      }
+      tc_fence_after();
+      const int row = mb * kPairBM + row_in_tile;
+      const uint32_t t_row = tmem_base + (static_cast<uint32_t>(sp * 32) << 16) + static_cast<uint32_t>(acc * kGemmBN);
+#pragma unroll 1
+      for (int c = half * (kGemmBN / 2); c < (half + 1) * (kGemmBN / 2); c += 32) {
+        const int col0 = nb * kGemmBN + c;
+        if (col0 >= p.N) break;  // warp-uniform
+        uint32_t r[32];
+        tmem_ld_32x32b_x32(t_row + static_cast<uint32_t>(c), r);
+        tmem_ld_wait();
+        if (row < p.M) gemm_epilogue_chunk<EPI>(p, row, col0, r);
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive_cluster(acc ? tempty1 : tempty0);  // one release per warp
+    }
+  }
+
+  tc_fence_before();
+  cluster_sync_all();  // the leader's MMAs read the peer's shared memory until here
+  tc_fence_after();
+  if (warp == 1) tmem_dealloc_pair(tmem_base, kGemmTmemCols);
+}
+
+template <int EPI>
+static int launch_gemm_pair(const CUtensorMap& ta, const CUtensorMap& tb, const GemmParams& p, cudaStream_t stream) {
+  static bool configured[64] = {false};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return SSAM_ERR_CUDA;
+  if (!configured[dev]) {
+    if (cudaFuncSetAttribute(gemm_bf16_pair_kernel<EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             kPairSmemBytes) != cudaSuccess)
+      return SSAM_ERR_CUDA;
+    configured[dev] = true;
+  }
+  const int m_tiles = (p.M + kPairBM - 1) / kPairBM;
+  const int n_tiles = (p.N + kGemmBN - 1) / kGemmBN;
+  const int tiles = m_tiles * n_tiles;
+  const int max_pairs = num_sms(dev) / 2;
+  const int pairs = tiles < max_pairs ? tiles : max_pairs;
+  gemm_bf16_pair_kernel<EPI><<<2 * pairs, kGemmThreads, kPairSmemBytes, stream>>>(ta, tb, p);
+  return cudaGetLastError() == cudaSuccess ? SSAM_OK : SSAM_ERR_CUDA;
+}
+
 template <int EPI>
 static int launch_gemm(const CUtensorMap& ta, const CUtensorMap& tb, const GemmParams& p, cudaStream_t stream) {
   static bool configured[64] = {false};
@@ -300,6 +507,26 @@ int gemm_bf16(const void* A, int64_t lda, const void* B, int64_t ldb, int M, int
                          kGemmBN, CU_TENSOR_MAP_SWIZZLE_128B);
   if (st != SSAM_OK) return st;
   GemmParams p{M, N, K, bias, out, ldo, out_rows};
+  const int pair_tiles = ((M + kPairBM - 1) / kPairBM) * ((N + kGemmBN - 1) / kGemmBN);
+  if (M >= kPairBM && pair_tiles >= 64) {
+    // 2-SM kernel: 128-row boxes per CTA for both operands
+    st = make_tmap_2d_bf16(&ta, A, static_cast<uint64_t>(M), static_cast<uint64_t>(K), static_cast<uint64_t>(lda),
+                           kGemmBK, 128, CU_TENSOR_MAP_SWIZZLE_128B);
+    if (st != SSAM_OK) return st;
+    st = make_tmap_2d_bf16(&tb, B, static_cast<uint64_t>(N), static_cast<uint64_t>(K), static_cast<uint64_t>(ldb),
+                           kGemmBK, 128, CU_TENSOR_MAP_SWIZZLE_128B);
+    if (st != SSAM_OK) return st;
+    switch (epilogue) {
+      case SSAM_EPI_BF16:
+        return launch_gemm_pair<SSAM_EPI_BF16>(ta, tb, p, stream);
+      case SSAM_EPI_GELU_BF16:
+        return launch_gemm_pair<SSAM_EPI_GELU_BF16>(ta, tb, p, stream);
+      case SSAM_EPI_F32:
+        return launch_gemm_pair<SSAM_EPI_F32>(ta, tb, p, stream);
+      default:
+        return launch_gemm_pair<SSAM_EPI_ADD_F32>(ta, tb, p, stream);
+    }
+  }
   switch (epilogue) {
     case SSAM_EPI_BF16:
       return launch_gemm<SSAM_EPI_BF16>(ta, tb, p, stream);

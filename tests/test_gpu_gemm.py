@@ -11,7 +11,10 @@ SHAPES = [
     (300, 256, 72),      # M tail, K tail inside one k-block
     (1000, 768, 1280),   # several n tiles, K multiple of 64
     (257, 96, 136),      # N not a multiple of 256, ragged everything
-    (4900, 2304, 768),   # ViT-B windowed qkv shape (one image)
+    (4900, 2304, 768),   # ViT-B windowed qkv shape (one image): 2-SM path
+    (16384, 512, 128),   # 2-SM path, exact tiles
+    (20000, 1280, 320),  # 2-SM path, M tail inside a CTA pair
+    (16500, 768, 1280),  # 2-SM path, M tail in the second CTA of the last pair
 ]
 
 
@@ -33,7 +36,7 @@ def test_gemm_bf16_epilogue(cuda_device, M, N, K):
     assert ops.device_error() == 0
 
 
-@pytest.mark.parametrize("M,N,K", SHAPES[:4])
+@pytest.mark.parametrize("M,N,K", SHAPES)
 def test_gemm_gelu_epilogue(cuda_device, M, N, K):
     g = torch.Generator(device="cpu").manual_seed(11 + M)
     a = torch.randn(M, K, generator=g).to(cuda_device, torch.bfloat16)
@@ -45,7 +48,7 @@ def test_gemm_gelu_epilogue(cuda_device, M, N, K):
     assert err <= 2e-2 * ref.abs().max().item() + 1e-3, err
 
 
-@pytest.mark.parametrize("M,N,K", SHAPES[:4])
+@pytest.mark.parametrize("M,N,K", SHAPES)
 def test_gemm_add_f32_rowmap(cuda_device, M, N, K):
     g = torch.Generator(device="cpu").manual_seed(23 + M)
     a = torch.randn(M, K, generator=g).to(cuda_device, torch.bfloat16)
@@ -63,3 +66,19 @@ def test_gemm_add_f32_rowmap(cuda_device, M, N, K):
     ref[rows[keep].long()] += _ref(a, b, bias)[keep]
     err = (x - ref).abs().max().item()
     assert err <= 1e-3 * ref.abs().max().item() + 1e-3, err
+
+
+@pytest.mark.parametrize("M", [256, 20480])
+def test_gelu_epilogue_matches_exact_erf_gelu(cuda_device, M):
+    """acc = 0, bias sweeps [-9, 9]: the GELU epilogue must reproduce the exact
+    (erf) GELU of torch to within one bf16 ulp (its erf error is <= 1.5e-7)."""
+    N, K = 2048, 64
+    a = torch.zeros(M, K, device=cuda_device, dtype=torch.bfloat16)
+    b = torch.zeros(N, K, device=cuda_device, dtype=torch.bfloat16)
+    bias = torch.linspace(-9.0, 9.0, N, device=cuda_device)
+    out = ops.gemm_bf16(a, b, bias, epilogue=ops.SSAM_EPI_GELU_BF16)
+    exact = torch.nn.functional.gelu(bias.double()).float()
+    got = out.float()
+    # one bf16 ulp of the exact value (plus a tiny absolute floor near zero)
+    ulp = torch.clamp(exact.abs(), min=2.0 ** -126) * 2.0 ** -7
+    assert bool(((got - exact[None, :]).abs() <= ulp[None, :] + 1e-6).all())
