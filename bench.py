@@ -253,7 +253,9 @@ def run_ours(args) -> None:
 
     # dominant kernel: the GEMM (tcgen05); per-launch averages over the timed region
     g = [(fl, st.elapsed_time(en)) for kind, fl, st, en in ops.KernelTimer.records if kind == "gemm"]
-    a = [(fl, st.elapsed_time(en)) for kind, fl, st, en in ops.KernelTimer.records if kind == "attention"]
+    a = [(fl, st.elapsed_time(en)) for kind, fl, st, en in ops.KernelTimer.records if kind.startswith("attention")]
+    a_win = sum(st.elapsed_time(en) for kind, _, st, en in ops.KernelTimer.records if kind == "attention_window")
+    a_glb = sum(st.elapsed_time(en) for kind, _, st, en in ops.KernelTimer.records if kind == "attention_global")
     peaks = _peaks()
     g_tflops = sum(f for f, _ in g) / (sum(t for _, t in g) * 1e-3) / 1e12 if g else None
     a_tflops = sum(f for f, _ in a) / (sum(t for _, t in a) * 1e-3) / 1e12 if a else None
@@ -294,6 +296,8 @@ def run_ours(args) -> None:
                      "frac": (g_tflops / peaks["bf16_tflops_sustained"]) if g_tflops else None,
                      "traffic": traffic, "peak_source": peaks["source"] + " sustained bf16",
                      "gemm_ms_per_step": gemm_ms_step, "attention_ms_per_step": attn_ms_step,
+                     "attention_window_ms_per_step": a_win / args.steps,
+                     "attention_global_ms_per_step": a_glb / args.steps,
                      "attention_tflops": a_tflops},
         "clocks": clk,
     }

@@ -102,12 +102,15 @@ int ssam_a_shape_mask(int N, int m_block, int n_block, int n_init, int with_diag
  *   perm  : int32 [n_seq*heads, win*win] permutation of every row.
  *   out   : bf16 [n_seq*win*win, heads*d] in raster token order, leading dim ld_out.
  *   n_init_blocks / with_diag : A-shape mask over 64-token blocks.
+ *   workspace : ssam_sparse_attn_workspace_size() bytes (0 for windowed grids,
+ *               win <= 16; global grids keep the per-query bias there).
  * d must be 64 or 80.
  * ------------------------------------------------------------------------- */
+size_t ssam_sparse_attn_workspace_size(int n_seq, int heads, int win, int d);
 int ssam_sparse_attn_fwd(const void* qkv, int64_t ld_qkv, int n_seq, int heads, int win, int d,
                          const void* rel_pos_h, const void* rel_pos_w, const int32_t* perm,
                          int n_init_blocks, int with_diag, float scale, void* out, int64_t ld_out,
-                         void* stream);
+                         void* workspace, size_t workspace_bytes, void* stream);
 
 /* ---------------------------------------------------------------------------
  * a10 (selection). Keep set of the Residual-Consistency MLP.
@@ -205,6 +208,18 @@ int ssam_rc_mlp_fwd_noalloc(float* x, int64_t ldx, const int32_t* rows, int n_ro
  * (2*C columns). A GEMM of the split rows against [W | W] carries the fp32
  * activation into the tensor-core GEMM (used for the neck convolutions). */
 int ssam_split_bf16x2(const float* x, int n_rows, int C, void* out, void* stream);
+
+/* 3-term split of fp32 rows: out[r] = [hi | lo | hi] (3*C bf16 columns),
+ * hi = bf16(x), lo = bf16(x - hi). A GEMM of the split rows against
+ * [W_hi | W_hi | W_lo] (W_lo = bf16(W - W_hi)) carries both the fp32 activation
+ * and the fp32 weight into the tensor-core GEMM up to the lo*lo term (about
+ * 2^-16 relative); the neck convolutions use it. */
+int ssam_split_bf16x3(const float* x, int n_rows, int C, void* out, void* stream);
+
+/* Patch-embed im2col with the same 3-term split: rows of 3*Cin*p*p bf16 columns,
+ * [hi | lo | hi], each part in (cin, ky, kx) order; against [W_hi | W_hi | W_lo]
+ * the stem GEMM keeps fp32 accuracy. */
+int ssam_patch_im2col_split3(const float* img, int B, int Cin, int H, int W, int p, void* out, void* stream);
 
 #ifdef __cplusplus
 }

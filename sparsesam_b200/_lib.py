@@ -28,8 +28,9 @@ SIGNATURES: dict[str, tuple] = {
                                       c_ptr, c_ptr, c_ptr, c_ptr, c_ptr]),
     "ssam_a_shape_n_init": (c_int, [c_int, c_int, c_f64, c_int]),
     "ssam_a_shape_mask": (c_int, [c_int, c_int, c_int, c_int, c_int, c_ptr]),
+    "ssam_sparse_attn_workspace_size": (c_size, [c_int, c_int, c_int, c_int]),
     "ssam_sparse_attn_fwd": (c_int, [c_ptr, c_i64, c_int, c_int, c_int, c_int, c_ptr, c_ptr, c_ptr,
-                                     c_int, c_int, c_f32, c_ptr, c_i64, c_ptr]),
+                                     c_int, c_int, c_f32, c_ptr, c_i64, c_ptr, c_size, c_ptr]),
     "ssam_keep_select": (c_int, [c_ptr, c_int, c_int, c_int, c_int, c_ptr, c_ptr, c_ptr]),
     "ssam_layernorm_gather": (c_int, [c_ptr, c_i64, c_ptr, c_int, c_int, c_ptr, c_ptr, c_f32, c_ptr, c_i64,
                                       c_ptr]),
@@ -45,6 +46,8 @@ SIGNATURES: dict[str, tuple] = {
     "ssam_nhwc_to_nchw": (c_int, [c_ptr, c_int, c_int, c_int, c_ptr, c_ptr]),
     "ssam_layernorm_rows": (c_int, [c_ptr, c_int, c_int, c_ptr, c_ptr, c_f32, c_ptr, c_int, c_ptr]),
     "ssam_split_bf16x2": (c_int, [c_ptr, c_int, c_int, c_ptr, c_ptr]),
+    "ssam_split_bf16x3": (c_int, [c_ptr, c_int, c_int, c_ptr, c_ptr]),
+    "ssam_patch_im2col_split3": (c_int, [c_ptr, c_int, c_int, c_int, c_int, c_int, c_ptr, c_ptr]),
     "ssam_rc_mlp_fwd_noalloc": (c_int, [c_ptr, c_i64, c_ptr, c_int, c_int, c_int, c_ptr, c_ptr, c_f32, c_ptr, c_ptr,
                                         c_ptr, c_ptr, c_ptr]),
 }
@@ -70,6 +73,7 @@ KERNELS_PER_CALL = {
     "ssam_layernorm_gather": 1, "ssam_window_rows": 1, "ssam_gemm_bf16": 1, "ssam_rc_mlp_fwd": 3,
     "ssam_patch_im2col": 1, "ssam_broadcast_rows": 1, "ssam_im2col3x3_nhwc": 1, "ssam_nhwc_to_nchw": 1,
     "ssam_layernorm_rows": 1, "ssam_split_bf16x2": 1, "ssam_rc_mlp_fwd_noalloc": 3,
+    "ssam_split_bf16x3": 1, "ssam_patch_im2col_split3": 1,
 }
 launch_count = 0  # kernels enqueued through call() since import (read by bench.py)
 
@@ -116,12 +120,15 @@ def missing_symbols() -> list[str]:
     return [n for n in SIGNATURES if getattr(handle, n, None) is None]
 
 
-def call(name: str, *args) -> int:
-    """Invoke an entry point and raise SparseSAMError on a non-zero status."""
+def call(name: str, *args, launches: int | None = None) -> int:
+    """Invoke an entry point and raise SparseSAMError on a non-zero status.
+
+    ``launches`` overrides the entry's kernel count for calls whose count depends
+    on the arguments (the global-grid attention adds its bias pre-pass)."""
     global launch_count
     fn = getattr(load(), name)
     st = fn(*args)
-    launch_count += KERNELS_PER_CALL.get(name, 0)
+    launch_count += KERNELS_PER_CALL.get(name, 0) if launches is None else launches
     if st != SSAM_OK:
         msg = load().ssam_status_string(st).decode()
         raise SparseSAMError(name, st, msg)

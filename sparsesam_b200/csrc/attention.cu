@@ -11,31 +11,38 @@
 // and the result of permuted row p is written to raster token perm[p]
 // (the inverse permutation and the head merge are fused into the store).
 //
-// Persistent, warp-specialised CTA (one per SM), 192 threads:
+// Persistent, warp-specialised CTA (one per SM), 288 threads:
 //   warps 0-3  softmax warpgroup: thread i owns query row i of the current
-//              128-query tile; extracts its rel-pos bias windows, runs the online
-//              softmax out of TMEM, writes P (bf16) and does the epilogue;
-//   warp 4     loader: cp.async gathers of the permuted Q / K / V rows (64-key
-//              blocks, 3 stages) and the rel-pos tables, signalled through
-//              mbarriers (cp.async.mbarrier.arrive);
-//   warp 5     UMMA issuer: P_H = Q Th^T and P_W = Q Tw^T for the next tile,
-//              S(j+1) = Q K^T issued ahead of softmax(j) into a second TMEM
-//              buffer, O += P V accumulated in TMEM (V as an MN-major operand).
+//              128-query tile; runs the online softmax out of TMEM, writes P
+//              (bf16) back into the TMEM columns of its S block, places the
+//              rel-pos bias operand of the next tile in TMEM and does the
+//              deferred epilogue of the previous tile;
+//   warps 4-7  loaders: coalesced cp.async gathers of the permuted Q / K / V
+//              rows (eight lanes per 128-byte row segment) into 128-key stages,
+//              the one-hot key-position operand, and (global grids) the
+//              precomputed bias rows;
+//   warp 8     UMMA issuer: S = Q K^T + A_bias onehot^T (A_bias from TMEM),
+//              O += P V (P from TMEM, V as one N = D operand); for windowed
+//              grids also [P_H | P_W] = Q [Th ; Tw]^T of the next tile.
+// Every tcgen05.mma occupies the tensor pipe for about 100 cycles up to N = 128,
+// so the blocks are 128 keys wide and P.V is one MMA per 16 keys.
 // O is rescaled lazily: only when a row maximum grows by more than 2^8 is the
 // TMEM row read, scaled and written back; otherwise the stale maximum is kept
 // (probabilities stay below 2^8 and the final 1/l normalisation is consistent).
 // Every wait is bounded; on timeout the CTA raises SSAM_ERR_TIMEOUT and unwinds.
 #include <cuda_fp16.h>
 
+#include <type_traits>
+
 #include "common.cuh"
 #include "host_util.h"
 
 namespace ssam {
 
-constexpr int kAttnBM = 128;  // queries per tile
-constexpr int kAttnBN = 64;   // keys per block (the reference's 64-token mask granularity)
-constexpr int kAttnStages = 3;
-constexpr int kAttnThreads = 192;
+constexpr int kAttnBM = 128;   // queries per tile
+constexpr int kAttnBN = 128;   // keys per block
+constexpr int kMaskBlk = 64;   // the reference's mask granularity (64-token blocks)
+constexpr int kAttnThreads = 288;
 constexpr int kAttnTmemCols = 512;
 constexpr float kRescaleThreshold = 8.0f;  // log2 units
 
@@ -62,29 +69,51 @@ __device__ __forceinline__ void tmem_st_32x32b_x16(uint32_t taddr, const uint32_
       "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15])
       : "memory");
 }
+__device__ __forceinline__ void tmem_st_32x32b_x32(uint32_t taddr, const uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], "
+      "{%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, %16, "
+      "%17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31, %32};" ::"r"(taddr),
+      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]), "r"(r[9]),
+      "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15]), "r"(r[16]), "r"(r[17]), "r"(r[18]),
+      "r"(r[19]), "r"(r[20]), "r"(r[21]), "r"(r[22]), "r"(r[23]), "r"(r[24]), "r"(r[25]), "r"(r[26]), "r"(r[27]),
+      "r"(r[28]), "r"(r[29]), "r"(r[30]), "r"(r[31])
+      : "memory");
+}
 __device__ __forceinline__ void tmem_st_wait() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 
-// Shared-memory geometry of a D-wide operand tile with R rows: channels 0..63 in
-// a 128B-swizzled region (R x 128 B), channels 64..79 (D == 80) in a 32B-swizzled
-// region (R x 32 B) right after it.
+// D(tmem) (+)= A(tmem) * B(smem): A is K-major in TMEM (row m in lane m, two
+// 16-bit elements per 32-bit column), B described by a shared-memory descriptor.
+__device__ __forceinline__ void umma_f16_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc, uint32_t idesc,
+                                            uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}\n" ::"r"(d_tmem),
+      "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+// Shared-memory geometry of a D-wide operand tile with R rows, in 16-channel
+// chunks: chunk region k (channels 16k..16k+15) holds R rows of 32 bytes with the
+// 32-byte swizzle (16-byte half h of row r at h ^ ((r >> 2) & 1)). The same
+// bytes serve as a K-major operand (one region per 16-wide k-step) and, for V,
+// as an MN-major operand with N = D (regions are the N atoms, LBO = R * 32).
 template <int D>
 struct TileGeom {
   static constexpr int kChunks = D / 8;  // 16-byte chunks per row
-  static constexpr bool kTail = D > 64;
-  static __host__ __device__ constexpr int bytes(int rows) { return rows * 128 + (kTail ? rows * 32 : 0); }
+  static __host__ __device__ constexpr int bytes(int rows) { return rows * D * 2; }
 };
 
 template <int D>
 __device__ __forceinline__ uint32_t tile_chunk_addr(uint32_t base, int rows, int r, int c) {
-  if (c < 8) return base + r * 128 + ((c ^ (r & 7)) << 4);
-  return base + rows * 128 + r * 32 + (((c - 8) ^ ((r >> 2) & 1)) << 4);
+  return base + (c >> 1) * rows * 32 + r * 32 + ((((c & 1) ^ ((r >> 2) & 1))) << 4);
 }
 
 // K-major operand descriptor for k-step ks (16 channels) of a TileGeom region.
 template <int D>
 __device__ __forceinline__ uint64_t kmajor_desc(uint32_t base, int rows, int ks) {
-  if (ks < 4) return make_smem_desc(base + ks * 32, 16, 1024, kSw128);
-  return make_smem_desc(base + rows * 128, 16, 256, kSw32);
+  return make_smem_desc(base + ks * rows * 32, 16, 256, kSw32);
 }
 
 __host__ __device__ constexpr int align1k(int v) { return (v + 1023) & ~1023; }
@@ -94,27 +123,35 @@ __host__ __device__ constexpr uint32_t make_idesc_f16(uint32_t M, uint32_t N) {
   return (1u << 4) | ((N >> 3) << 17) | ((M >> 4) << 24);
 }
 
-// Two specialisations: SMALL for windowed grids (win <= 16, 32-row tables) and
-// the global 64x64 grid. SMALL tiles have one or two key blocks, so they get a
-// deeper S pipeline and double-buffered O / P_H / A_bias to remove tile bubbles.
+// Two specialisations.
+//   SMALL (windowed grids, win <= 16): the rel-pos bias of the next tile
+//   ([P_H | P_W] on the tensor cores + band extraction) is computed inside the
+//   kernel while the current tile runs.
+//   LARGE (the global grid): the bias of every query is computed once by
+//   relbias_kernel into a workspace (in permuted query order); a loader stages
+//   the rows of the next tile and the softmax warps move them into TMEM.
+// TMEM plan (512 columns): S[2] (128 fp32 columns each; P overwrites the first
+// 64 as bf16 pairs), O[kO] (D columns each), A_bias[2] (kBW columns each: relH
+// pairs then relW pairs), and for SMALL [P_H | P_W] (64 columns).
 template <int D, bool SMALL>
 struct AttnCfg {
-  static constexpr int kS = SMALL ? 3 : 2;        // S buffers in TMEM (QK^T lookahead)
-  static constexpr int kO = SMALL ? 2 : 1;        // O accumulators in TMEM
-  static constexpr int kPH = SMALL ? 2 : 1;       // P_H/P_W TMEM buffers
-  static constexpr int kAB = SMALL ? 2 : 1;       // A_bias shared-memory buffers
+  static constexpr int kS = 2;                    // S / P buffers in TMEM
   static constexpr int kStages = SMALL ? 3 : 2;   // K / V / one-hot stages
   static constexpr int kBW = SMALL ? 16 : 64;     // bias columns per table (>= win)
-  static constexpr int kNT = SMALL ? 32 : 128;    // table rows padded to the MMA N
+  static constexpr int kNT = 32;                  // rows per table (SMALL), stacked Th ; Tw
+  static constexpr int kABCols = kBW;             // 2 x kBW fp16 = kBW columns
+  static constexpr int kPHCols = SMALL ? 2 * kNT : 0;
   static constexpr int kTmO = kS * kAttnBN;       // TMEM column of O[0]
-  static constexpr int kTmPH = SMALL ? kTmO + kO * D : 256;
+  static constexpr int kO = (kTmO + 2 * D + 2 * kABCols + kPHCols <= kAttnTmemCols) ? 2 : 1;
+  static constexpr int kTmAB = kTmO + kO * D;     // TMEM column of A_bias[0]
+  static constexpr int kTmPH = kTmAB + 2 * kABCols;
   static constexpr int kOHBytes = 2 * kAttnBN * kBW * 2;  // one-hot H | W regions per stage
-  static constexpr int kABBytes = 2 * kAttnBM * kBW * 2;  // A_bias H | W regions
-  static_assert(kTmPH + kPH * 2 * kNT <= kAttnTmemCols, "TMEM plan exceeds 512 columns");
+  static constexpr int kABRow = 68;                       // SMALL bias scratch row (bytes, odd word stride)
+  static_assert(kTmPH + kPHCols <= kAttnTmemCols, "TMEM plan exceeds 512 columns");
 };
 
-// Byte offset of element (row r, column k) of a K-major fp16 bias operand region
-// (128B swizzle for 64-wide rows, 32B swizzle for 16-wide rows).
+// Byte offset of element (row r, column k) of a K-major fp16 one-hot operand
+// region (128B swizzle for 64-wide rows, 32B swizzle for 16-wide rows).
 template <bool SMALL>
 __device__ __forceinline__ uint32_t bias_off(int r, int k) {
   if constexpr (SMALL) return r * 32 + ((((k >> 3) ^ ((r >> 2) & 1))) << 4) + (k & 7) * 2;
@@ -127,19 +164,17 @@ struct AttnLayout {
   using C = AttnCfg<D, SMALL>;
   using TG = TileGeom<D>;
   static constexpr int kStage = 2 * TG::bytes(kAttnBN) + C::kOHBytes;  // K | V | one-hot
-  int th, tw, q, kv, p, ab, kinfo, tok, bars, total;
-  __host__ __device__ AttnLayout(int win) {
-    th = 0;
-    tw = align1k(th + TG::bytes(C::kNT));
-    q = align1k(tw + TG::bytes(C::kNT));               // [2] x bytes(128)
-    kv = q + 2 * TG::bytes(kAttnBM);                   // [stages] x kStage
-    p = kv + C::kStages * kStage;                      // [2] x 128 x 128 B
-    ab = p + 2 * kAttnBM * 128;                        // [kAB] x kABBytes
-    kinfo = ab + C::kAB * C::kABBytes;                 // int [stages][64]
-    tok = kinfo + C::kStages * kAttnBN * 4;            // int [2][128]
-    bars = (tok + 2 * kAttnBM * 4 + 7) & ~7;           // mbarriers
-    total = bars + 32 * 8 + 16 + 1024;                 // + alignment slack
-    (void)win;
+  static constexpr int kTables = SMALL ? TG::bytes(2 * C::kNT) : 0;
+  static constexpr int kABStage = SMALL ? kAttnBM * C::kABRow : kAttnBM * 256;  // scratch / staged bias rows
+  int tab, q, kv, ab, tok, bars, total;
+  __host__ __device__ AttnLayout() {
+    tab = 0;
+    q = align1k(tab + kTables);                   // [2] x bytes(128)
+    kv = align1k(q + 2 * TG::bytes(kAttnBM));     // [stages] x kStage
+    ab = align1k(kv + C::kStages * kStage);       // kABStage
+    tok = ab + kABStage;                          // int [2][128]
+    bars = (tok + 2 * kAttnBM * 4 + 7) & ~7;      // mbarriers
+    total = bars + 40 * 8 + 16 + 1024;            // + alignment slack
   }
 };
 
@@ -157,28 +192,24 @@ struct AttnParams {
   int64_t ld_out;
   int n_tiles;  // 128-query tiles per row
   int total_tiles;
+  __half* bias_ws;  // LARGE: [rows][n_tiles*128][128] fp16 = relH/scale | relW/scale
 };
 
-// Key blocks of one tile: the keep bar [0, nk), then the diagonal blocks of the
-// two 64-query m-blocks of the tile that lie outside the bar.
+// Key blocks of one tile. The mask enables 64-key block m for query m-block mb
+// when m < nk, or m == mb with the diagonal. Processed 128-key blocks: those
+// covering the keep bar [0, 64 nk), then block qtile (it holds the tile's two
+// diagonal 64-key blocks) when the bar does not reach it.
 struct TileBlocks {
-  int nk, n, d0, d1;
-  __device__ TileBlocks() : nk(0), n(0), d0(-1), d1(-1) {}
+  int nk, nkb, n, qt;
+  __device__ TileBlocks() : nk(0), nkb(0), n(0), qt(0) {}
   __device__ TileBlocks(const AttnParams& a, int qtile) {
-    const int nblk = (a.N + kAttnBN - 1) / kAttnBN;
+    const int nblk = (a.N + kMaskBlk - 1) / kMaskBlk;
     nk = a.n_init < nblk ? a.n_init : nblk;
-    n = nk;
-    d0 = d1 = -1;
-    if (a.with_diag) {
-      for (int mb = 2 * qtile; mb < 2 * qtile + 2; ++mb) {
-        if (mb < nblk && mb >= nk) {
-          if (n == nk) d0 = mb; else d1 = mb;
-          ++n;
-        }
-      }
-    }
+    nkb = (nk + 1) / 2;
+    qt = qtile;
+    n = nkb + ((a.with_diag && qtile >= nkb) ? 1 : 0);
   }
-  __device__ int at(int i) const { return i < nk ? i : (i == nk ? d0 : d1); }
+  __device__ int at(int i) const { return i < nkb ? i : qt; }
 };
 
 // Walks the flat (tile, key block) sequence of one persistent CTA.
@@ -208,22 +239,29 @@ struct BlockCursor {
 };
 
 // mbarrier indices
+// K (with its one-hot rows) and V of a stage are released separately: K once
+// QK^T of the block has completed, V once P.V has, so the K loads of block g+2
+// overlap the softmax of blocks g and g+1.
 enum {
   kBarTab = 0,
-  kBarQFull = 1,     // [2]
-  kBarQEmpty = 3,    // [2]
-  kBarKVFull = 5,    // [3]
-  kBarKVEmpty = 8,   // [3]
-  kBarPHFull = 11,   // [2]
-  kBarPHFree = 13,   // [2]
-  kBarABFull = 15,   // [2]
-  kBarSFull = 17,    // [3]
-  kBarSFree = 20,    // [3]
-  kBarPFull = 23,    // [2]
-  kBarODone = 25,    // [2]
-  kBarOFree = 27,    // [2]
-  kBarDrain = 29,
-  kNumBars = 30
+  kBarQFull = 1,     // [2]  loader lanes (cp.async)
+  kBarQEmpty = 3,    // [2]  UMMA commit after the tile's last QK^T
+  kBarKFull = 5,     // [3]  K loader lanes (cp.async)
+  kBarKEmpty = 8,    // [3]  UMMA commit after QK^T
+  kBarVFull = 11,    // [3]  V loader lanes (cp.async)
+  kBarVEmpty = 14,   // [3]  UMMA commit after P.V
+  kBarPHFull = 17,   //      UMMA commit (SMALL)
+  kBarPHFree = 18,   //      softmax (SMALL)
+  kBarABFull = 19,   // [2]  softmax: A_bias of the tile is in TMEM
+  kBarABSFull = 21,  //      LARGE: bias rows staged (cp.async)
+  kBarABSFree = 22,  //      LARGE: softmax copied the staged rows
+  kBarSFull = 23,    // [2]  UMMA commit after QK^T
+  kBarSFree = 25,    // [2]  UMMA commit after P.V (P lives in the S columns)
+  kBarPFull = 27,    // [2]  softmax
+  kBarODone = 29,    // [2]  UMMA commit after P.V
+  kBarOFree = 31,    // [2]  softmax epilogue
+  kBarDrain = 33,
+  kNumBars = 34
 };
 
 template <int D, bool SMALL>
@@ -231,14 +269,13 @@ __global__ void __launch_bounds__(kAttnThreads, 1) sparse_attn_kernel(const Attn
   using TG = TileGeom<D>;
   using C = AttnCfg<D, SMALL>;
   using LAY = AttnLayout<D, SMALL>;
-  const LAY L(a.win);
+  const LAY L;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const uint32_t sb = smem_u32(smem);
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L.bars);
   uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(bars + kNumBars);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
-  int* s_kinfo = reinterpret_cast<int*>(smem + L.kinfo);
   int* s_tok = reinterpret_cast<int*>(smem + L.tok);
 
   const int tid = threadIdx.x;
@@ -248,26 +285,30 @@ __global__ void __launch_bounds__(kAttnThreads, 1) sparse_attn_kernel(const Attn
   if (tid == 0) {
     mbar_init(&bars[kBarTab], 64);
     for (int i = 0; i < 2; ++i) {
-      mbar_init(&bars[kBarQFull + i], 64);
+      mbar_init(&bars[kBarQFull + i], 256);
       mbar_init(&bars[kBarQEmpty + i], 1);
-      mbar_init(&bars[kBarPHFull + i], 1);
-      mbar_init(&bars[kBarPHFree + i], 128);
       mbar_init(&bars[kBarABFull + i], 128);
+      mbar_init(&bars[kBarSFull + i], 1);
+      mbar_init(&bars[kBarSFree + i], 1);
       mbar_init(&bars[kBarPFull + i], 128);
       mbar_init(&bars[kBarODone + i], 1);
       mbar_init(&bars[kBarOFree + i], 128);
     }
-    for (int s = 0; s < 3; ++s) {
-      mbar_init(&bars[kBarKVFull + s], 64);
-      mbar_init(&bars[kBarKVEmpty + s], 1);
-      mbar_init(&bars[kBarSFull + s], 1);
-      mbar_init(&bars[kBarSFree + s], 128);
+    mbar_init(&bars[kBarPHFull], 1);
+    mbar_init(&bars[kBarPHFree], 128);
+    mbar_init(&bars[kBarABSFull], 128);
+    mbar_init(&bars[kBarABSFree], 128);
+    for (int s = 0; s < C::kStages; ++s) {
+      mbar_init(&bars[kBarKFull + s], 128);
+      mbar_init(&bars[kBarKEmpty + s], 1);
+      mbar_init(&bars[kBarVFull + s], 128);
+      mbar_init(&bars[kBarVEmpty + s], 1);
     }
     mbar_init(&bars[kBarDrain], 1);
     *abort_flag = 0;
     fence_mbar_init();
   }
-  if (warp == 5) {
+  if (warp == 8) {
     tmem_alloc(tmem_holder, kAttnTmemCols);
     tmem_relinquish();
   }
@@ -276,7 +317,10 @@ __global__ void __launch_bounds__(kAttnThreads, 1) sparse_attn_kernel(const Attn
   tc_fence_after();
   const uint32_t tmem = *tmem_holder;
 
+  // Fast path: one try_wait (usually the phase has completed); the abort flag is
+  // read only when the wait has to sleep.
   auto wait_or_abort = [&](int bar, uint32_t parity) -> bool {
+    if (mbar_try_wait(&bars[bar], parity)) return true;
     if (*abort_flag) return false;
     if (!mbar_wait(&bars[bar], parity)) {
       *abort_flag = 1;
@@ -286,149 +330,189 @@ __global__ void __launch_bounds__(kAttnThreads, 1) sparse_attn_kernel(const Attn
   };
   auto tile_exists = [&](int lt_) { return static_cast<int>(blockIdx.x) + lt_ * static_cast<int>(gridDim.x) < a.total_tiles; };
 
-  if (warp == 4) {
-    // =========================== loader warp ===========================
-    // Lane-per-row copies: a lane moves whole rows (kChunks x 16 B), so every
-    // cp.async address is a row base plus a compile-time chunk offset. The
-    // permutation indices of the next key block are fetched one block ahead.
-    // Order: Q(0), then per tile t: Q(t+1), K/V(t, blocks) — the UMMA warp
-    // computes P_H(t+1) from Q(t+1) while tile t runs.
-    auto copy_row = [&](uint32_t region, int rows, int r, const __nv_bfloat16* src) {
-      const uint32_t bytes = src != nullptr ? 16u : 0u;
-      const uint8_t* s0 = reinterpret_cast<const uint8_t*>(src != nullptr ? src : a.qkv);
+  if (warp >= 4 && warp < 8) {
+    // =========================== loader warps ===========================
+    // Warp 4 + h (h = 0, 1): K rows 64h..64h+63 of each block with their one-hot
+    // rows; warp 6 + h: the V rows. Warp 4 + w also copies Q rows
+    // 32w..32w+31 of each tile; warp 4 the rel-pos tables; warps 6-7 the staged
+    // bias rows (LARGE).
+    // Order: Q(0), then per tile t: Q(t+1), K/V(t, blocks). A copy instruction
+    // moves 16 bytes per lane with eight lanes on one 128-byte row segment (four
+    // rows per instruction), then the 32-byte tails (sixteen rows); lane l holds
+    // the tokens of rows l, l+32, ... and hands them out with shuffles. Rows of
+    // padded positions (token < 0) are zero-filled.
+    const int lw = warp - 4;
+    const int kv = lw >> 1, half = lw & 1;  // kv 0: K, 1: V
+    // NS x 32 rows starting at tile row r0, channel offset xcol of each token row.
+    auto copy_rows = [&](auto ns_tag, uint32_t region, int R, int r0, const int* tok, const __nv_bfloat16* base,
+                         int xcol) {
+      constexpr int NS = decltype(ns_tag)::value;
+      const int c = lane & 7;
 #pragma unroll
-      for (int c = 0; c < TG::kChunks; ++c)
-        cp_async16(tile_chunk_addr<D>(region, rows, r, c), s0 + (src != nullptr ? c * 16 : 0), bytes);
+      for (int i = 0; i < NS * 8; ++i) {  // 4 rows per instruction
+        const int rr = 4 * i + (lane >> 3);
+        const int t = __shfl_sync(0xffffffffu, tok[i >> 3], rr & 31);
+        const __nv_bfloat16* src = t >= 0 ? base + static_cast<int64_t>(t) * a.ld_qkv + xcol + c * 8 : a.qkv;
+        cp_async16(tile_chunk_addr<D>(region, R, r0 + rr, c), src, t >= 0 ? 16u : 0u);
+      }
+      if constexpr (D > 64) {
+        const int ct = 8 + (lane & 1);
+#pragma unroll
+        for (int i = 0; i < NS * 2; ++i) {  // 16 rows per instruction
+          const int rr = 16 * i + (lane >> 1);
+          const int t = __shfl_sync(0xffffffffu, tok[i >> 1], rr & 31);
+          const __nv_bfloat16* src = t >= 0 ? base + static_cast<int64_t>(t) * a.ld_qkv + xcol + ct * 8 : a.qkv;
+          cp_async16(tile_chunk_addr<D>(region, R, r0 + rr, ct), src, t >= 0 ? 16u : 0u);
+        }
+      }
     };
-    // one-hot regions start at zero; kinfo starts at -1 (nothing to clear)
-    for (int s = 0; s < C::kStages; ++s) {
-      uint4* oh = reinterpret_cast<uint4*>(smem + L.kv + s * LAY::kStage + 2 * TG::bytes(kAttnBN));
-      for (int i = lane; i < C::kOHBytes / 16; i += 32) oh[i] = make_uint4(0u, 0u, 0u, 0u);
-      for (int r = lane; r < kAttnBN; r += 32) s_kinfo[s * kAttnBN + r] = -1;
+    using One = std::integral_constant<int, 1>;
+    using Two = std::integral_constant<int, 2>;
+
+    // previous one-hot entries (kh | kw << 16, -1: none) of this K-loader lane's
+    // two rows in each stage
+    int oh_prev[C::kStages][2];
+#pragma unroll
+    for (int s2 = 0; s2 < C::kStages; ++s2) oh_prev[s2][0] = oh_prev[s2][1] = -1;
+    if (lw == 0) {
+      // one-hot regions start at zero
+      for (int s2 = 0; s2 < C::kStages; ++s2) {
+        uint4* oh = reinterpret_cast<uint4*>(smem + L.kv + s2 * LAY::kStage + 2 * TG::bytes(kAttnBN));
+        for (int i = lane; i < C::kOHBytes / 16; i += 32) oh[i] = make_uint4(0u, 0u, 0u, 0u);
+      }
+      if constexpr (SMALL) {  // [Th ; Tw] stacked, rows past 2win-1 zero
+        const int trows = 2 * win - 1;
+        for (int r = lane; r < 2 * C::kNT; r += 32) {
+          const int tr = r & (C::kNT - 1);
+          const __nv_bfloat16* src = (r < C::kNT ? a.th : a.tw) + tr * D;
+#pragma unroll
+          for (int c = 0; c < TG::kChunks; ++c)
+            cp_async16(tile_chunk_addr<D>(sb + L.tab, 2 * C::kNT, r, c), tr < trows ? src + c * 8 : a.th,
+                       tr < trows ? 16u : 0u);
+        }
+      }
+      __syncwarp();
+      mbar_arrive(&bars[kBarTab]);
+      cp_async_arrive_noinc(&bars[kBarTab]);
     }
-    __syncwarp();
-    // rel-pos tables, once per CTA
-    const uint32_t sTh = sb + L.th, sTw = sb + L.tw;
-    const int trows = 2 * win - 1;
-    for (int r = lane; r < C::kNT; r += 32) {
-      copy_row(sTh, C::kNT, r, r < trows ? a.th + r * D : nullptr);
-      copy_row(sTw, C::kNT, r, r < trows ? a.tw + r * D : nullptr);
-    }
-    mbar_arrive(&bars[kBarTab]);
-    cp_async_arrive_noinc(&bars[kBarTab]);
 
     auto load_q = [&](int lt_) -> bool {
       const int tile = blockIdx.x + lt_ * gridDim.x;
       const int row = tile / a.n_tiles, qtile = tile - row * a.n_tiles;
       const int seq = row / a.heads, head = row - seq * a.heads;
       const int32_t* perm = a.perm + static_cast<int64_t>(row) * N;
-      const __nv_bfloat16* q_base = a.qkv + static_cast<int64_t>(seq) * N * a.ld_qkv + head * D;
-      int qt[4];
-#pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        const int p = qtile * kAttnBM + lane + 32 * i;
-        qt[i] = p < N ? __ldg(perm + p) : -1;
+      int qt[1];  // row 32 lw + lane of the tile
+      {
+        const int p = qtile * kAttnBM + 32 * lw + lane;
+        qt[0] = p < N ? __ldg(perm + p) : -1;
       }
       const int qb = lt_ & 1;
       if (!wait_or_abort(kBarQEmpty + qb, ((lt_ >> 1) & 1) ^ 1)) return false;
-      const uint32_t sQ = sb + L.q + qb * TG::bytes(kAttnBM);
-#pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        const int r = lane + 32 * i;
-        s_tok[qb * kAttnBM + r] = qt[i];
-        copy_row(sQ, kAttnBM, r, qt[i] >= 0 ? q_base + static_cast<int64_t>(qt[i]) * a.ld_qkv : nullptr);
-      }
+      if constexpr (SMALL) s_tok[qb * kAttnBM + 32 * lw + lane] = qt[0];
+      copy_rows(One{}, sb + L.q + qb * TG::bytes(kAttnBM), kAttnBM, 32 * lw, qt,
+                a.qkv + static_cast<int64_t>(seq) * N * a.ld_qkv, head * D);
       mbar_arrive(&bars[kBarQFull + qb]);
       cp_async_arrive_noinc(&bars[kBarQFull + qb]);
+      if (!SMALL && kv == 1) {  // bias rows 64h..64h+63 of the tile (256 B each), two rows per instruction
+        if (!wait_or_abort(kBarABSFree, (lt_ & 1) ^ 1)) return false;
+        const uint8_t* src = reinterpret_cast<const uint8_t*>(
+            a.bias_ws + (static_cast<int64_t>(row) * a.n_tiles + qtile) * kAttnBM * 128);
+        const int c = lane & 15;
+#pragma unroll 8
+        for (int i = 0; i < kAttnBM / 4; ++i) {
+          const int r = 64 * half + 2 * i + (lane >> 4);
+          cp_async16(sb + L.ab + (c >> 3) * (kAttnBM * 128) + r * 128 + (((c & 7) ^ (r & 7)) << 4),
+                     src + r * 256 + c * 16, 16u);
+        }
+        mbar_arrive(&bars[kBarABSFull]);
+        cp_async_arrive_noinc(&bars[kBarABSFull]);
+      }
       return true;
     };
 
     int g = 0;
-    bool ok = tile_exists(0) ? load_q(0) : true;
+    bool ok = true;
+    if (tile_exists(0)) ok = load_q(0);
     for (int lt = 0; ok && tile_exists(lt) && !*abort_flag; ++lt) {
       if (tile_exists(lt + 1) && !(ok = load_q(lt + 1))) break;
       const int tile = blockIdx.x + lt * gridDim.x;
       const int row = tile / a.n_tiles, qtile = tile - row * a.n_tiles;
       const int seq = row / a.heads, head = row - seq * a.heads;
       const int32_t* perm = a.perm + static_cast<int64_t>(row) * N;
-      const __nv_bfloat16* k_base = a.qkv + static_cast<int64_t>(seq) * N * a.ld_qkv + a.C + head * D;
+      const __nv_bfloat16* base = a.qkv + static_cast<int64_t>(seq) * N * a.ld_qkv;
+      const int xcol = (kv == 0 ? a.C : 2 * a.C) + head * D;
       const TileBlocks tb(a, qtile);
-      int nt0 = -1, nt1 = -1;
-      if (tb.n > 0) {
-        const int kp = tb.at(0) * kAttnBN + lane;
-        nt0 = kp < N ? __ldg(perm + kp) : -1;
-        nt1 = kp + 32 < N ? __ldg(perm + kp + 32) : -1;
-      }
-      for (int j = 0; j < tb.n; ++j, ++g) {
-        const int t0 = nt0, t1 = nt1;
-        if (j + 1 < tb.n) {  // prefetch the next block's tokens
-          const int kp = tb.at(j + 1) * kAttnBN + lane;
-          nt0 = kp < N ? __ldg(perm + kp) : -1;
-          nt1 = kp + 32 < N ? __ldg(perm + kp + 32) : -1;
-        }
-        const int stage = g % C::kStages;
-        if (!(ok = wait_or_abort(kBarKVEmpty + stage, ((g / C::kStages) & 1) ^ 1))) break;
-        int* kinfo = s_kinfo + stage * kAttnBN;
-        const uint32_t sK = sb + L.kv + stage * LAY::kStage;
-        const uint32_t sV = sK + TG::bytes(kAttnBN);
-        uint8_t* oh_h = smem + L.kv + stage * LAY::kStage + 2 * TG::bytes(kAttnBN);
-        uint8_t* oh_w = oh_h + kAttnBN * C::kBW * 2;
+      int nt[2];  // tokens of keys 64 half + lane + 32 i of the next block
+      auto fetch = [&](int jb) {
+        const int kp = tb.at(jb) * kAttnBN + 64 * half + lane;
 #pragma unroll
-        for (int i = 0; i < 2; ++i) {
-          const int r = lane + 32 * i;
-          const int t = i == 0 ? t0 : t1;
-          int info = -1;
-          if (t >= 0) {
-            const int kh = t / win;
-            info = kh | ((t - kh * win) << 16);
+        for (int i = 0; i < 2; ++i) nt[i] = kp + 32 * i < N ? __ldg(perm + kp + 32 * i) : -1;
+      };
+      if (tb.n > 0) fetch(0);
+      for (int j = 0; j < tb.n; ++j, ++g) {
+        int t[2];
+#pragma unroll
+        for (int i = 0; i < 2; ++i) t[i] = nt[i];
+        if (j + 1 < tb.n) fetch(j + 1);  // the next block's tokens, one block ahead
+        const int stage = g % C::kStages;
+        const int full_bar = (kv == 0 ? kBarKFull : kBarVFull) + stage;
+        if (!(ok = wait_or_abort((kv == 0 ? kBarKEmpty : kBarVEmpty) + stage, ((g / C::kStages) & 1) ^ 1))) break;
+        const uint32_t sK = sb + L.kv + stage * LAY::kStage;
+        if (kv == 0) {  // one-hot rows of this lane's two keys
+          uint8_t* oh_h = smem + L.kv + stage * LAY::kStage + 2 * TG::bytes(kAttnBN);
+          uint8_t* oh_w = oh_h + kAttnBN * C::kBW * 2;
+#pragma unroll
+          for (int s2 = 0; s2 < C::kStages; ++s2) {
+            if (s2 != stage) continue;  // keeps oh_prev in registers
+#pragma unroll
+            for (int i = 0; i < 2; ++i) {
+              const int r = 64 * half + lane + 32 * i;
+              int info = -1;
+              if (t[i] >= 0) {
+                const int kh = t[i] / win;
+                info = kh | ((t[i] - kh * win) << 16);
+              }
+              const int old = oh_prev[s2][i];
+              if (old >= 0) {  // clear the previous one-hot entries of this row
+                *reinterpret_cast<uint16_t*>(oh_h + bias_off<SMALL>(r, old & 0xffff)) = 0;
+                *reinterpret_cast<uint16_t*>(oh_w + bias_off<SMALL>(r, old >> 16)) = 0;
+              }
+              if (info >= 0) {
+                *reinterpret_cast<uint16_t*>(oh_h + bias_off<SMALL>(r, info & 0xffff)) = 0x3C00;  // fp16 1.0
+                *reinterpret_cast<uint16_t*>(oh_w + bias_off<SMALL>(r, info >> 16)) = 0x3C00;
+              }
+              oh_prev[s2][i] = info;
+            }
           }
-          const int old = kinfo[r];
-          if (old >= 0) {  // clear the previous one-hot entries of this row
-            *reinterpret_cast<uint16_t*>(oh_h + bias_off<SMALL>(r, old & 0xffff)) = 0;
-            *reinterpret_cast<uint16_t*>(oh_w + bias_off<SMALL>(r, old >> 16)) = 0;
-          }
-          if (info >= 0) {
-            *reinterpret_cast<uint16_t*>(oh_h + bias_off<SMALL>(r, info & 0xffff)) = 0x3C00;  // fp16 1.0
-            *reinterpret_cast<uint16_t*>(oh_w + bias_off<SMALL>(r, info >> 16)) = 0x3C00;
-          }
-          kinfo[r] = info;
-          const __nv_bfloat16* krow = t >= 0 ? k_base + static_cast<int64_t>(t) * a.ld_qkv : nullptr;
-          copy_row(sK, kAttnBN, r, krow);
-          copy_row(sV, kAttnBN, r, krow != nullptr ? krow + a.C : nullptr);
+          fence_proxy_async_smem();  // one-hot rows (generic stores) -> UMMA reads
         }
-        fence_proxy_async_smem();  // one-hot rows (generic stores) -> UMMA reads
-        mbar_arrive(&bars[kBarKVFull + stage]);
-        cp_async_arrive_noinc(&bars[kBarKVFull + stage]);
+        copy_rows(Two{}, kv == 0 ? sK : sK + TG::bytes(kAttnBN), kAttnBN, 64 * half, t, base, xcol);
+        mbar_arrive(&bars[full_bar]);
+        cp_async_arrive_noinc(&bars[full_bar]);
       }
     }
     cp_async_wait_all();
-  } else if (warp == 5) {
+  } else if (warp == 8) {
     // =========================== UMMA issuer ===========================
     if (lane == 0) {
-      const uint32_t sTh = sb + L.th, sTw = sb + L.tw;
-      const uint32_t idesc_t = make_idesc_bf16(kAttnBM, C::kNT, 0, 0);
+      const uint32_t idesc_t = make_idesc_bf16(kAttnBM, 2 * C::kNT, 0, 0);
       const uint32_t idesc_s = make_idesc_bf16(kAttnBM, kAttnBN, 0, 0);
       const uint32_t idesc_b = make_idesc_f16(kAttnBM, kAttnBN);
-      const uint32_t idesc_o64 = make_idesc_bf16(kAttnBM, 64, 0, 1);
-      const uint32_t idesc_o16 = make_idesc_bf16(kAttnBM, 16, 0, 1);
-      bool ok = wait_or_abort(kBarTab, 0);
-      fence_proxy_async_smem();
+      const uint32_t idesc_o = make_idesc_bf16(kAttnBM, D, 0, 1);
+      bool ok = !SMALL || wait_or_abort(kBarTab, 0);
 
-      auto issue_ph = [&](int lt_) -> bool {  // P_H / P_W of tile lt_
-        const int qb = lt_ & 1, pb = lt_ % C::kPH;
+      auto issue_ph = [&](int lt_) -> bool {  // [P_H | P_W] of tile lt_ (SMALL)
+        const int qb = lt_ & 1;
         if (!wait_or_abort(kBarQFull + qb, (lt_ >> 1) & 1)) return false;
-        if (!wait_or_abort(kBarPHFree + pb, ((lt_ / C::kPH) & 1) ^ 1)) return false;
+        if (!wait_or_abort(kBarPHFree, (lt_ & 1) ^ 1)) return false;
         tc_fence_after();
         fence_proxy_async_smem();
         const uint32_t sQ = sb + L.q + qb * TG::bytes(kAttnBM);
-        const uint32_t tPH = tmem + C::kTmPH + pb * 2 * C::kNT;
 #pragma unroll
-        for (int ks = 0; ks < D / 16; ++ks) {
-          umma_f16_ss(tPH, kmajor_desc<D>(sQ, kAttnBM, ks), kmajor_desc<D>(sTh, C::kNT, ks), idesc_t, ks > 0);
-          umma_f16_ss(tPH + C::kNT, kmajor_desc<D>(sQ, kAttnBM, ks), kmajor_desc<D>(sTw, C::kNT, ks), idesc_t,
-                      ks > 0);
-        }
-        umma_commit(&bars[kBarPHFull + pb]);
+        for (int ks = 0; ks < D / 16; ++ks)
+          umma_f16_ss(tmem + C::kTmPH, kmajor_desc<D>(sQ, kAttnBM, ks), kmajor_desc<D>(sb + L.tab, 2 * C::kNT, ks),
+                      idesc_t, ks > 0);
+        umma_commit(&bars[kBarPHFull]);
         return true;
       };
       auto issue_qk = [&](const BlockCursor& c) -> bool {
@@ -436,38 +520,38 @@ __global__ void __launch_bounds__(kAttnThreads, 1) sparse_attn_kernel(const Attn
           if constexpr (SMALL) {
             if (tile_exists(c.lt + 1) && !issue_ph(c.lt + 1)) return false;
           } else {
-            if (!issue_ph(c.lt)) return false;
+            if (!wait_or_abort(kBarQFull + (c.lt & 1), (c.lt >> 1) & 1)) return false;
           }
-          if (!wait_or_abort(kBarABFull + c.lt % C::kAB, (c.lt / C::kAB) & 1)) return false;
+          if (!wait_or_abort(kBarABFull + (c.lt & 1), (c.lt >> 1) & 1)) return false;
         }
         const int st = c.g % C::kStages, sbuf = c.g % C::kS;
-        if (!wait_or_abort(kBarKVFull + st, (c.g / C::kStages) & 1)) return false;
+        if (!wait_or_abort(kBarKFull + st, (c.g / C::kStages) & 1)) return false;
         if (!wait_or_abort(kBarSFree + sbuf, ((c.g / C::kS) & 1) ^ 1)) return false;
         tc_fence_after();
         fence_proxy_async_smem();
         const uint32_t sQ = sb + L.q + (c.lt & 1) * TG::bytes(kAttnBM);
         const uint32_t sK = sb + L.kv + st * LAY::kStage;
         const uint32_t sOH = sK + 2 * TG::bytes(kAttnBN);
-        const uint32_t sAB = sb + L.ab + (c.lt % C::kAB) * C::kABBytes;
+        const uint32_t tAB = tmem + C::kTmAB + (c.lt & 1) * C::kABCols;
         const uint32_t tS = tmem + sbuf * kAttnBN;
 #pragma unroll
         for (int ks = 0; ks < D / 16; ++ks)
           umma_f16_ss(tS, kmajor_desc<D>(sQ, kAttnBM, ks), kmajor_desc<D>(sK, kAttnBN, ks), idesc_s, ks > 0);
-        // + A_bias . onehot^T  (relH / scale at kh, relW / scale at kw)
+        // + A_bias . onehot^T  (relH / scale at kh, relW / scale at kw); A_bias from TMEM
 #pragma unroll
         for (int part = 0; part < 2; ++part) {
-          const uint32_t ab = sAB + part * kAttnBM * C::kBW * 2;
+          const uint32_t ab = tAB + part * (C::kBW / 2);
           const uint32_t oh = sOH + part * kAttnBN * C::kBW * 2;
           if constexpr (SMALL) {
-            umma_f16_ss(tS, make_smem_desc(ab, 16, 256, kSw32), make_smem_desc(oh, 16, 256, kSw32), idesc_b, 1u);
+            umma_f16_ts(tS, ab, make_smem_desc(oh, 16, 256, kSw32), idesc_b, 1u);
           } else {
 #pragma unroll
             for (int ks = 0; ks < 4; ++ks)
-              umma_f16_ss(tS, make_smem_desc(ab + ks * 32, 16, 1024, kSw128),
-                          make_smem_desc(oh + ks * 32, 16, 1024, kSw128), idesc_b, 1u);
+              umma_f16_ts(tS, ab + ks * 8, make_smem_desc(oh + ks * 32, 16, 1024, kSw128), idesc_b, 1u);
           }
         }
         umma_commit(&bars[kBarSFull + sbuf]);
+        umma_commit(&bars[kBarKEmpty + st]);
         if (c.j == c.tb.n - 1) umma_commit(&bars[kBarQEmpty + (c.lt & 1)]);
         return true;
       };
@@ -475,22 +559,22 @@ __global__ void __launch_bounds__(kAttnThreads, 1) sparse_attn_kernel(const Attn
         if (!wait_or_abort(kBarPFull + (c.g & 1), (c.g >> 1) & 1)) return false;
         const int ob = c.lt % C::kO;
         if (c.j == 0 && !wait_or_abort(kBarOFree + ob, ((c.lt / C::kO) & 1) ^ 1)) return false;
+        const int st = c.g % C::kStages, sbuf = c.g % C::kS;
+        if (!wait_or_abort(kBarVFull + st, (c.g / C::kStages) & 1)) return false;
         tc_fence_after();
         fence_proxy_async_smem();
-        const int st = c.g % C::kStages;
-        const uint32_t sP = sb + L.p + (c.g & 1) * (kAttnBM * 128);
+        const uint32_t tP = tmem + sbuf * kAttnBN;
         const uint32_t sV = sb + L.kv + st * LAY::kStage + TG::bytes(kAttnBN);
         const uint32_t tO = tmem + C::kTmO + ob * D;
+        // V as an MN-major operand with N = D: 32B-swizzled atoms of 8 keys x 16
+        // channels, the D/16 channel regions LBO = 128 * 32 bytes apart.
 #pragma unroll
-        for (int ks = 0; ks < kAttnBN / 16; ++ks) {
-          const uint64_t pd = make_smem_desc(sP + ks * 32, 16, 1024, kSw128);
-          const uint32_t acc = (c.j > 0 || ks > 0) ? 1u : 0u;
-          umma_f16_ss(tO, pd, make_smem_desc(sV + ks * 2048, 8192, 1024, kSw128), idesc_o64, acc);
-          if constexpr (TG::kTail)
-            umma_f16_ss(tO + 64, pd, make_smem_desc(sV + kAttnBN * 128 + ks * 512, 4096, 256, kSw32), idesc_o16, acc);
-        }
+        for (int ks = 0; ks < kAttnBN / 16; ++ks)
+          umma_f16_ts(tO, tP + ks * 8, make_smem_desc(sV + ks * 512, kAttnBN * 32, 256, kSw32), idesc_o,
+                      (c.j > 0 || ks > 0) ? 1u : 0u);
         umma_commit(&bars[kBarODone + (c.g & 1)]);
-        umma_commit(&bars[kBarKVEmpty + st]);
+        umma_commit(&bars[kBarVEmpty + st]);
+        umma_commit(&bars[kBarSFree + sbuf]);
         return true;
       };
 
@@ -499,7 +583,9 @@ __global__ void __launch_bounds__(kAttnThreads, 1) sparse_attn_kernel(const Attn
       cq.start(a);
       cp.start(a);
       while (ok && !cp.done) {
-        while (ok && !cq.done && cq.g < cp.g + C::kS) {
+        // QK^T of block g+1 goes ahead of P.V of block g, no further: a deeper
+        // lookahead would make P.V(g) wait for a K/V stage that only P.V(g-1) frees.
+        while (ok && !cq.done && cq.g <= cp.g + 1) {
           ok = issue_qk(cq);
           cq.advance(a);
         }
@@ -514,44 +600,73 @@ __global__ void __launch_bounds__(kAttnThreads, 1) sparse_attn_kernel(const Attn
     // ======================== softmax warpgroup ========================
     const uint32_t t_lane = tmem + (static_cast<uint32_t>(warp * 32) << 16);
 
-    // rel-pos bias of tile lt_ -> A_bias[lt_ % kAB] row tid (fp16, relH/scale at column j)
-    auto extract_bias = [&](int lt_, int& tok_out) -> bool {
-      const int qb = lt_ & 1, pb = lt_ % C::kPH;
-      if (!wait_or_abort(kBarQFull + qb, (lt_ >> 1) & 1)) return false;
-      const int t = s_tok[qb * kAttnBM + tid];
-      tok_out = t;
-      const int qh = t >= 0 ? t / win : 0;
-      const int qw = t >= 0 ? t - qh * win : 0;
-      if (!wait_or_abort(kBarPHFull + pb, (lt_ / C::kPH) & 1)) return false;
-      tc_fence_after();
-      uint8_t* ab_h = smem + L.ab + (lt_ % C::kAB) * C::kABBytes;
-      uint8_t* ab_w = ab_h + kAttnBM * C::kBW * 2;
-      const uint32_t tPH = t_lane + C::kTmPH + pb * 2 * C::kNT;
-      for (int c0 = 0; c0 < C::kNT; c0 += 32) {
+    // A_bias of tile lt_ -> TMEM buffer lt_ & 1 (row tid): fp16 pairs, relH/scale
+    // at column j then relW/scale. Called once S of the current tile's first block
+    // is in, so every QK^T that read the buffer's previous contents has completed.
+    auto stage_bias = [&](int lt_, int& tok_out) -> bool {
+      const uint32_t tAB = t_lane + C::kTmAB + (lt_ & 1) * C::kABCols;
+      if constexpr (SMALL) {
+        const int qb = lt_ & 1;
+        if (!wait_or_abort(kBarQFull + qb, (lt_ >> 1) & 1)) return false;
+        const int t = s_tok[qb * kAttnBM + tid];
+        tok_out = t;
+        const int qh = t >= 0 ? t / win : 0;
+        const int qw = t >= 0 ? t - qh * win : 0;
+        if (!wait_or_abort(kBarPHFull, lt_ & 1)) return false;
+        tc_fence_after();
+        uint8_t* row = smem + L.ab + tid * C::kABRow;  // 16 relH then 16 relW fp16
         uint32_t rh[32], rw[32];
-        tmem_ld_32x32b_x32(tPH + c0, rh);
-        tmem_ld_32x32b_x32(tPH + C::kNT + c0, rw);
+        tmem_ld_32x32b_x32(t_lane + C::kTmPH, rh);
+        tmem_ld_32x32b_x32(t_lane + C::kTmPH + C::kNT, rw);
         tmem_ld_wait();
+        tc_fence_before();
+        mbar_arrive(&bars[kBarPHFree]);
 #pragma unroll
-        for (int j = 0; j < 32; ++j) {
-          const int jh = qh + win - 1 - (c0 + j);
-          if (jh >= 0 && jh < win)
-            *reinterpret_cast<__half*>(ab_h + bias_off<SMALL>(tid, jh)) =
-                __float2half_rn(__uint_as_float(rh[j]) * a.inv_scale);
-          const int jw = qw + win - 1 - (c0 + j);
-          if (jw >= 0 && jw < win)
-            *reinterpret_cast<__half*>(ab_w + bias_off<SMALL>(tid, jw)) =
-                __float2half_rn(__uint_as_float(rw[j]) * a.inv_scale);
+        for (int j = 0; j < 16; j += 2) {  // padding columns must not hold NaN/Inf
+          *reinterpret_cast<uint32_t*>(row + j * 2) = 0u;
+          *reinterpret_cast<uint32_t*>(row + 32 + j * 2) = 0u;
         }
+#pragma unroll
+        for (int c = 0; c < 32; ++c) {
+          const int jh = qh + win - 1 - c;
+          if (jh >= 0 && jh < win)
+            *reinterpret_cast<__half*>(row + jh * 2) = __float2half_rn(__uint_as_float(rh[c]) * a.inv_scale);
+          const int jw = qw + win - 1 - c;
+          if (jw >= 0 && jw < win)
+            *reinterpret_cast<__half*>(row + 32 + jw * 2) = __float2half_rn(__uint_as_float(rw[c]) * a.inv_scale);
+        }
+        uint32_t v[16];
+#pragma unroll
+        for (int i = 0; i < 16; ++i) v[i] = *reinterpret_cast<const uint32_t*>(row + 4 * i);
+        tmem_st_32x32b_x16(tAB, v);
+      } else {
+        if (!wait_or_abort(kBarABSFull, lt_ & 1)) return false;
+        const uint8_t* hrow = smem + L.ab + tid * 128;
+        const uint8_t* wrow = hrow + kAttnBM * 128;
+        uint32_t v[32];
+#pragma unroll
+        for (int c = 0; c < 8; ++c) {
+          const uint4 x = *reinterpret_cast<const uint4*>(hrow + ((c ^ (tid & 7)) << 4));
+          v[4 * c] = x.x;
+          v[4 * c + 1] = x.y;
+          v[4 * c + 2] = x.z;
+          v[4 * c + 3] = x.w;
+        }
+        tmem_st_32x32b_x32(tAB, v);
+#pragma unroll
+        for (int c = 0; c < 8; ++c) {
+          const uint4 x = *reinterpret_cast<const uint4*>(wrow + ((c ^ (tid & 7)) << 4));
+          v[4 * c] = x.x;
+          v[4 * c + 1] = x.y;
+          v[4 * c + 2] = x.z;
+          v[4 * c + 3] = x.w;
+        }
+        tmem_st_32x32b_x32(tAB + 32, v);
+        mbar_arrive(&bars[kBarABSFree]);
       }
-      for (int j = win; j < C::kBW; ++j) {  // padding columns must not hold NaN/Inf
-        *reinterpret_cast<__half*>(ab_h + bias_off<SMALL>(tid, j)) = __float2half_rn(0.f);
-        *reinterpret_cast<__half*>(ab_w + bias_off<SMALL>(tid, j)) = __float2half_rn(0.f);
-      }
-      fence_proxy_async_smem();
+      tmem_st_wait();
       tc_fence_before();
-      mbar_arrive(&bars[kBarABFull + lt_ % C::kAB]);
-      mbar_arrive(&bars[kBarPHFree + pb]);
+      mbar_arrive(&bars[kBarABFull + (lt_ & 1)]);
       return true;
     };
     // O / l of tile lt_, stored at the raster token (inverse permutation and head merge)
@@ -585,10 +700,20 @@ __global__ void __launch_bounds__(kAttnThreads, 1) sparse_attn_kernel(const Attn
       mbar_arrive(&bars[kBarOFree + lt_ % C::kO]);
       return true;
     };
+    // LARGE: this thread's query token of tile lt_, straight from the permutation.
+    auto query_token = [&](int lt_) -> int {
+      const int tile = blockIdx.x + lt_ * gridDim.x;
+      const int row = tile / a.n_tiles, qtile = tile - row * a.n_tiles;
+      const int p = qtile * kAttnBM + tid;
+      return p < N ? __ldg(a.perm + static_cast<int64_t>(row) * N + p) : -1;
+    };
 
     bool ok = true;
     int tok_cur = -1, tok_next = -1;
-    if (tile_exists(0)) ok = extract_bias(0, tok_cur);
+    if (tile_exists(0)) {
+      ok = stage_bias(0, tok_cur);
+      if (!SMALL) tok_cur = query_token(0);
+    }
     int pend_lt = -1, pend_g = -1, pend_tok = -1;  // deferred epilogue
     float pend_l = 0.f;
     int g = 0;
@@ -598,43 +723,41 @@ __global__ void __launch_bounds__(kAttnThreads, 1) sparse_attn_kernel(const Attn
       const TileBlocks tb(a, qtile);
       const int my_mb = 2 * qtile + (tid >= 64 ? 1 : 0);
       const uint32_t tO = t_lane + C::kTmO + (lt % C::kO) * D;
+      if (!SMALL && tile_exists(lt + 1)) tok_next = query_token(lt + 1);
       float m_run = -INFINITY, l_run = 0.f;
       for (int j = 0; j < tb.n; ++j, ++g) {
-        const int st = g % C::kStages, sbuf = g % C::kS;
+        const int sbuf = g % C::kS;
         const int kb = tb.at(j);
-        if (!(ok = wait_or_abort(kBarKVFull + st, (g / C::kStages) & 1))) break;  // kinfo visibility
         if (!(ok = wait_or_abort(kBarSFull + sbuf, (g / C::kS) & 1))) break;
         tc_fence_after();
-        uint32_t s[64];
-        {
-          uint32_t (&s0)[32] = *reinterpret_cast<uint32_t(*)[32]>(&s[0]);
-          uint32_t (&s1)[32] = *reinterpret_cast<uint32_t(*)[32]>(&s[32]);
-          tmem_ld_32x32b_x32(t_lane + sbuf * kAttnBN, s0);
-          tmem_ld_32x32b_x32(t_lane + sbuf * kAttnBN + 32, s1);
-          tmem_ld_wait();
-        }
-        tc_fence_before();
-        mbar_arrive(&bars[kBarSFree + sbuf]);
-
-        const bool full = kb < tb.nk && (kb + 1) * kAttnBN <= N;
+        const uint32_t tS = t_lane + sbuf * kAttnBN;
+        // 64-key halves of the block: enabled by the keep bar or the diagonal
+        const int m0 = 2 * kb;
+        const bool full = m0 + 1 < tb.nk && (kb + 1) * kAttnBN <= N;
+        const int kvalid = N - kb * kAttnBN;  // keys of the block inside the sequence
+        const bool on0 = full || m0 < tb.nk || (a.with_diag && m0 == my_mb);
+        const bool on1 = full || m0 + 1 < tb.nk || (a.with_diag && m0 + 1 == my_mb);
+        // pass 1: row maximum of the raw logits (scale > 0 commutes with max)
         float mx = -INFINITY;
-        if (full) {
 #pragma unroll
-          for (int jj = 0; jj < 64; ++jj) {
-            const float x = __uint_as_float(s[jj]) * a.scale_log2;
-            s[jj] = __float_as_uint(x);
-            mx = fmaxf(mx, x);
-          }
-        } else {
-          const int* kinfo = s_kinfo + st * kAttnBN;
-          const bool row_on = (kb < tb.nk) || (kb == my_mb);
+        for (int h = 0; h < 2; ++h) {
+          uint32_t s0[32], s1[32];
+          tmem_ld_32x32b_x32(tS + 64 * h, s0);
+          tmem_ld_32x32b_x32(tS + 64 * h + 32, s1);
+          tmem_ld_wait();
+          const bool on = h == 0 ? on0 : on1;
+          if (full) {
 #pragma unroll
-          for (int jj = 0; jj < 64; ++jj) {
-            const float x = (row_on && kinfo[jj] >= 0) ? __uint_as_float(s[jj]) * a.scale_log2 : -INFINITY;
-            s[jj] = __float_as_uint(x);
-            mx = fmaxf(mx, x);
+            for (int jj = 0; jj < 32; ++jj) mx = fmaxf(mx, fmaxf(__uint_as_float(s0[jj]), __uint_as_float(s1[jj])));
+          } else if (on) {
+#pragma unroll
+            for (int jj = 0; jj < 32; ++jj) {
+              if (64 * h + jj < kvalid) mx = fmaxf(mx, __uint_as_float(s0[jj]));
+              if (64 * h + 32 + jj < kvalid) mx = fmaxf(mx, __uint_as_float(s1[jj]));
+            }
           }
         }
+        mx = mx == -INFINITY ? -INFINITY : mx * a.scale_log2;
         const float m_new = fmaxf(m_run, mx);
         float m_use = m_run;
         bool rescale = false;
@@ -647,18 +770,6 @@ __global__ void __launch_bounds__(kAttnThreads, 1) sparse_attn_kernel(const Attn
         const float m_off = m_use == -INFINITY ? 0.f : m_use;
         const float alpha = rescale ? fast_exp2(m_run - m_use) : 1.f;
         float sum = 0.f;
-        uint32_t pk[32];
-#pragma unroll
-        for (int e = 0; e < 32; ++e) {
-          const float p0 = fast_exp2(__uint_as_float(s[2 * e]) - m_off);
-          const float p1 = fast_exp2(__uint_as_float(s[2 * e + 1]) - m_off);
-          sum += p0 + p1;
-          pk[e] = pack_bf16x2(p0, p1);
-        }
-        l_run = (j == 0 ? 0.f : l_run * alpha) + sum;
-        m_run = m_use;
-        // P buffer g&1 was last read by PV(g-2)
-        if (g >= 2 && !(ok = wait_or_abort(kBarODone + (g & 1), ((g >> 1) - 1) & 1))) break;
         // tcgen05.ld/st are warp-collective (.sync.aligned): the O rescale runs on
         // the whole warp when any of its rows needs it (the others scale by 1).
         if (__any_sync(0xffffffffu, rescale)) {
@@ -673,34 +784,60 @@ __global__ void __launch_bounds__(kAttnThreads, 1) sparse_attn_kernel(const Attn
             for (int e = 0; e < 16; ++e) r16[e] = __float_as_uint(__uint_as_float(r16[e]) * alpha);
             tmem_st_32x32b_x16(tO + c0, r16);
           }
-          tmem_st_wait();
         }
-        uint8_t* prow = smem + L.p + (g & 1) * (kAttnBM * 128) + tid * 128;
+        // pass 2: P = exp2(s * scale log2e - m) as bf16 pairs, kept in registers
+        // and stored over the first 64 S columns once every S chunk has been read
+        uint32_t pk[64];
 #pragma unroll
-        for (int c = 0; c < 8; ++c)
-          *reinterpret_cast<uint4*>(prow + ((c ^ (tid & 7)) << 4)) =
-              make_uint4(pk[4 * c], pk[4 * c + 1], pk[4 * c + 2], pk[4 * c + 3]);
-        fence_proxy_async_smem();
+        for (int q4 = 0; q4 < 4; ++q4) {
+          uint32_t sq[32];
+          tmem_ld_32x32b_x32(tS + 32 * q4, sq);
+          tmem_ld_wait();
+          if (full) {
+#pragma unroll
+            for (int e = 0; e < 16; ++e) {
+              const float p0 = fast_exp2(fmaf(__uint_as_float(sq[2 * e]), a.scale_log2, -m_off));
+              const float p1 = fast_exp2(fmaf(__uint_as_float(sq[2 * e + 1]), a.scale_log2, -m_off));
+              sum += p0 + p1;
+              pk[16 * q4 + e] = pack_bf16x2(p0, p1);
+            }
+          } else {
+            const bool on = q4 < 2 ? on0 : on1;
+#pragma unroll
+            for (int e = 0; e < 16; ++e) {
+              const bool v0 = on && 32 * q4 + 2 * e < kvalid;
+              const bool v1 = on && 32 * q4 + 2 * e + 1 < kvalid;
+              const float p0 = v0 ? fast_exp2(fmaf(__uint_as_float(sq[2 * e]), a.scale_log2, -m_off)) : 0.f;
+              const float p1 = v1 ? fast_exp2(fmaf(__uint_as_float(sq[2 * e + 1]), a.scale_log2, -m_off)) : 0.f;
+              sum += p0 + p1;
+              pk[16 * q4 + e] = pack_bf16x2(p0, p1);
+            }
+          }
+        }
+        {
+          uint32_t (&p0)[32] = *reinterpret_cast<uint32_t(*)[32]>(&pk[0]);
+          uint32_t (&p1)[32] = *reinterpret_cast<uint32_t(*)[32]>(&pk[32]);
+          tmem_st_32x32b_x32(tS, p0);
+          tmem_st_32x32b_x32(tS + 32, p1);
+        }
+        l_run = (j == 0 ? 0.f : l_run * alpha) + sum;
+        m_run = m_use;
+        tmem_st_wait();
         tc_fence_before();
         mbar_arrive(&bars[kBarPFull + (g & 1)]);
 
-        if (SMALL && j == 0) {
-          // bias of the next tile and the previous tile's epilogue, off the critical path
-          if (tile_exists(lt + 1) && !(ok = extract_bias(lt + 1, tok_next))) break;
+        if (j == 0) {
+          // next tile's bias operand and the previous tile's epilogue, off the critical path
+          if (tile_exists(lt + 1) && !(ok = stage_bias(lt + 1, tok_next))) break;
           if (pend_lt >= 0 && !(ok = epilogue(pend_lt, pend_g, pend_tok, pend_l))) break;
           pend_lt = -1;
         }
       }
       if (!ok) break;
-      if constexpr (SMALL) {
-        pend_lt = lt;
-        pend_g = tb.n > 0 ? g - 1 : -1;
-        pend_tok = tok_cur;
-        pend_l = l_run;
-      } else {
-        if (tile_exists(lt + 1) && !(ok = extract_bias(lt + 1, tok_next))) break;
-        if (!(ok = epilogue(lt, tb.n > 0 ? g - 1 : -1, tok_cur, l_run))) break;
-      }
+      pend_lt = lt;
+      pend_g = tb.n > 0 ? g - 1 : -1;
+      pend_tok = tok_cur;
+      pend_l = l_run;
       tok_cur = tok_next;
     }
     if (ok && pend_lt >= 0) epilogue(pend_lt, pend_g, pend_tok, pend_l);
@@ -709,20 +846,146 @@ __global__ void __launch_bounds__(kAttnThreads, 1) sparse_attn_kernel(const Attn
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
-  if (warp == 5) tmem_dealloc(tmem, kAttnTmemCols);
+  if (warp == 8) tmem_dealloc(tmem, kAttnTmemCols);
+}
+
+// ---------------------------------------------------------------------------
+// relbias_kernel (global grids): for one 128-query tile of one (image, head)
+// row, P_H = Q Th^T and P_W = Q Tw^T on the tensor cores, then each thread
+// extracts its query's band relH[j] = P_H[qh - j + win - 1] (and relW) and
+// writes [relH / scale | relW / scale] (fp16, 64 + 64 columns, zero padding) to
+// bias_ws[row][p] in permuted query order — the operand the attention kernel
+// streams in with the query tile (sam.py:62-73, computed once per query).
+// ---------------------------------------------------------------------------
+constexpr int kRelThreads = 128;
+
+template <int D>
+__global__ void __launch_bounds__(kRelThreads) relbias_kernel(const AttnParams a) {
+  using TG = TileGeom<D>;
+  constexpr int kNT = 128;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const uint32_t sb = smem_u32(smem);
+  const uint32_t sTh = sb, sTw = sb + TG::bytes(kNT), sQ = sb + 2 * TG::bytes(kNT);
+  uint8_t* stage = smem + 3 * TG::bytes(kNT);  // [2][128 rows][128 B] swizzled bias rows
+  uint64_t* bar = reinterpret_cast<uint64_t*>(stage + 2 * kAttnBM * 128);
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(bar + 1);
+
+  const int tid = threadIdx.x, warp = tid >> 5;
+  const int tile = blockIdx.x;
+  const int row = tile / a.n_tiles, qtile = tile - row * a.n_tiles;
+  const int seq = row / a.heads, head = row - seq * a.heads;
+  const int N = a.N, win = a.win;
+  const int p = qtile * kAttnBM + tid;
+  const int t = p < N ? __ldg(a.perm + static_cast<int64_t>(row) * N + p) : -1;
+
+  if (tid == 0) {
+    mbar_init(bar, 1);
+    fence_mbar_init();
+  }
+  if (warp == 0) {
+    tmem_alloc(tmem_holder, 256);
+    tmem_relinquish();
+  }
+  // tables (row tid) and this thread's query row
+  const int trows = 2 * win - 1;
+  const __nv_bfloat16* q_src =
+      t >= 0 ? a.qkv + (static_cast<int64_t>(seq) * N + t) * a.ld_qkv + head * D : nullptr;
+#pragma unroll
+  for (int c = 0; c < TG::kChunks; ++c) {
+    cp_async16(tile_chunk_addr<D>(sTh, kNT, tid, c), tid < trows ? a.th + tid * D + c * 8 : a.th,
+               tid < trows ? 16u : 0u);
+    cp_async16(tile_chunk_addr<D>(sTw, kNT, tid, c), tid < trows ? a.tw + tid * D + c * 8 : a.tw,
+               tid < trows ? 16u : 0u);
+    cp_async16(tile_chunk_addr<D>(sQ, kAttnBM, tid, c), q_src != nullptr ? q_src + c * 8 : a.qkv,
+               q_src != nullptr ? 16u : 0u);
+  }
+  cp_async_wait_all();
+  fence_proxy_async_smem();
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_holder;
+  if (tid == 0) {
+    const uint32_t idesc = make_idesc_bf16(kAttnBM, kNT, 0, 0);
+#pragma unroll
+    for (int ks = 0; ks < D / 16; ++ks) {
+      umma_f16_ss(tmem, kmajor_desc<D>(sQ, kAttnBM, ks), kmajor_desc<D>(sTh, kNT, ks), idesc, ks > 0);
+      umma_f16_ss(tmem + kNT, kmajor_desc<D>(sQ, kAttnBM, ks), kmajor_desc<D>(sTw, kNT, ks), idesc, ks > 0);
+    }
+    umma_commit(bar);
+  }
+  const bool ok = __syncthreads_and(mbar_wait(bar, 0));
+  tc_fence_after();
+  if (ok) {
+    const int qh = t >= 0 ? t / win : 0;
+    const int qw = t >= 0 ? t - qh * win : 0;
+    uint8_t* st_h = stage;
+    uint8_t* st_w = stage + kAttnBM * 128;
+    const uint32_t t_lane = tmem + (static_cast<uint32_t>(warp * 32) << 16);
+    for (int c0 = 0; c0 < kNT; c0 += 32) {
+      uint32_t rh[32], rw[32];
+      tmem_ld_32x32b_x32(t_lane + c0, rh);
+      tmem_ld_32x32b_x32(t_lane + kNT + c0, rw);
+      tmem_ld_wait();
+#pragma unroll
+      for (int j = 0; j < 32; ++j) {
+        const int jh = qh + win - 1 - (c0 + j);
+        if (jh >= 0 && jh < win)
+          *reinterpret_cast<__half*>(st_h + bias_off<false>(tid, jh)) =
+              __float2half_rn(__uint_as_float(rh[j]) * a.inv_scale);
+        const int jw = qw + win - 1 - (c0 + j);
+        if (jw >= 0 && jw < win)
+          *reinterpret_cast<__half*>(st_w + bias_off<false>(tid, jw)) =
+              __float2half_rn(__uint_as_float(rw[j]) * a.inv_scale);
+      }
+    }
+    for (int j = win; j < 64; ++j) {
+      *reinterpret_cast<__half*>(st_h + bias_off<false>(tid, j)) = __float2half_rn(0.f);
+      *reinterpret_cast<__half*>(st_w + bias_off<false>(tid, j)) = __float2half_rn(0.f);
+    }
+    // this thread's row: unswizzle and store 256 B (zeros for queries past N)
+    uint4* dst = reinterpret_cast<uint4*>(a.bias_ws + (static_cast<int64_t>(row) * a.n_tiles + qtile) * kAttnBM * 128 +
+                                          static_cast<int64_t>(tid) * 128);
+#pragma unroll
+    for (int c = 0; c < 16; ++c) {
+      const uint8_t* src = stage + (c >> 3) * (kAttnBM * 128) + tid * 128 + (((c & 7) ^ (tid & 7)) << 4);
+      dst[c] = t >= 0 ? *reinterpret_cast<const uint4*>(src) : make_uint4(0u, 0u, 0u, 0u);
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 0) tmem_dealloc(tmem, 256);
+}
+
+size_t sparse_attn_workspace_size(int n_seq, int heads, int win) {
+  if (n_seq <= 0 || heads <= 0 || win <= 16) return 0;  // windowed grids compute the bias in-kernel
+  const int64_t n_tiles = (static_cast<int64_t>(win) * win + kAttnBM - 1) / kAttnBM;
+  return static_cast<size_t>(n_seq) * heads * n_tiles * kAttnBM * 128 * 2;
 }
 
 template <int D, bool SMALL>
 static int launch_attn(const AttnParams& p, cudaStream_t stream) {
-  const AttnLayout<D, SMALL> L(p.win);
+  const AttnLayout<D, SMALL> L;
   static bool configured[64] = {false};
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return SSAM_ERR_CUDA;
+  constexpr int kRelSmem = 3 * TileGeom<D>::bytes(128) + 2 * kAttnBM * 128 + 64 + 1024;
   if (!configured[dev]) {
     if (cudaFuncSetAttribute(sparse_attn_kernel<D, SMALL>, cudaFuncAttributeMaxDynamicSharedMemorySize, L.total) !=
         cudaSuccess)
       return SSAM_ERR_CUDA;
+    if (!SMALL && cudaFuncSetAttribute(relbias_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize, kRelSmem) !=
+                      cudaSuccess)
+      return SSAM_ERR_CUDA;
     configured[dev] = true;
+  }
+  if (!SMALL) {
+    // two CTAs per SM at most: 2 x 256 TMEM columns
+    const int rel_smem = kRelSmem > 80 * 1024 ? kRelSmem : 80 * 1024;
+    relbias_kernel<D><<<p.total_tiles, kRelThreads, rel_smem, stream>>>(p);
+    if (cudaGetLastError() != cudaSuccess) return SSAM_ERR_CUDA;
   }
   // One persistent CTA per SM (the plan exceeds half the SM's shared memory),
   // so its 512 TMEM columns are always available.
@@ -735,10 +998,11 @@ static int launch_attn(const AttnParams& p, cudaStream_t stream) {
 
 int sparse_attn_fwd(const void* qkv, int64_t ld_qkv, int n_seq, int heads, int win, int d, const void* rel_pos_h,
                     const void* rel_pos_w, const int32_t* perm, int n_init_blocks, int with_diag, float scale,
-                    void* out, int64_t ld_out, cudaStream_t stream) {
+                    void* out, int64_t ld_out, void* workspace, size_t workspace_bytes, cudaStream_t stream) {
   if (qkv == nullptr || rel_pos_h == nullptr || rel_pos_w == nullptr || perm == nullptr || out == nullptr)
     return SSAM_ERR_INVALID;
   if (n_seq <= 0 || heads <= 0 || win <= 0 || n_init_blocks < 0) return SSAM_ERR_INVALID;
+  if (n_init_blocks == 0 && !with_diag) return SSAM_ERR_INVALID;  // every query would have no key
   if (d != 64 && d != 80) return SSAM_ERR_UNSUPPORTED;
   if (win > 64) return SSAM_ERR_UNSUPPORTED;  // 2*win-1 table rows must fit one 128-wide MMA
   if (!(scale > 0.f)) return SSAM_ERR_INVALID;
@@ -767,7 +1031,14 @@ int sparse_attn_fwd(const void* qkv, int64_t ld_qkv, int n_seq, int heads, int w
   const int64_t total = static_cast<int64_t>(p.n_tiles) * n_seq * heads;
   if (total > INT32_MAX) return SSAM_ERR_UNSUPPORTED;
   p.total_tiles = static_cast<int>(total);
-  const bool small = win <= 16;  // 32-row tables, 16-wide bias operands
+  const bool small = win <= 16;
+  p.bias_ws = nullptr;
+  if (!small) {
+    const size_t need = sparse_attn_workspace_size(n_seq, heads, win);
+    if (workspace == nullptr || workspace_bytes < need) return SSAM_ERR_INVALID;
+    if (!aligned16(workspace)) return SSAM_ERR_ALIGN;
+    p.bias_ws = static_cast<__half*>(workspace);
+  }
   if (d == 64) return small ? launch_attn<64, true>(p, stream) : launch_attn<64, false>(p, stream);
   return small ? launch_attn<80, true>(p, stream) : launch_attn<80, false>(p, stream);
 }

@@ -65,11 +65,16 @@ int ssam_a_shape_mask(int N, int m_block, int n_block, int n_init, int with_diag
   return ssam::a_shape_mask(N, m_block, n_block, n_init, with_diag, mask);
 }
 
+size_t ssam_sparse_attn_workspace_size(int n_seq, int heads, int win, int d) {
+  (void)d;
+  return ssam::sparse_attn_workspace_size(n_seq, heads, win);
+}
+
 int ssam_sparse_attn_fwd(const void* qkv, int64_t ld_qkv, int n_seq, int heads, int win, int d, const void* rel_pos_h,
                          const void* rel_pos_w, const int32_t* perm, int n_init_blocks, int with_diag, float scale,
-                         void* out, int64_t ld_out, void* stream) {
+                         void* out, int64_t ld_out, void* workspace, size_t workspace_bytes, void* stream) {
   return ssam::sparse_attn_fwd(qkv, ld_qkv, n_seq, heads, win, d, rel_pos_h, rel_pos_w, perm, n_init_blocks, with_diag,
-                               scale, out, ld_out, static_cast<cudaStream_t>(stream));
+                               scale, out, ld_out, workspace, workspace_bytes, static_cast<cudaStream_t>(stream));
 }
 
 int ssam_keep_select(const int32_t* inv_perm_group, int B, int heads, int N, int keep_n, int32_t* idx, int32_t* rows,
@@ -120,6 +125,14 @@ int ssam_layernorm_rows(const float* x, int n_rows, int C, const float* w, const
 
 int ssam_split_bf16x2(const float* x, int n_rows, int C, void* out, void* stream) {
   return ssam::split_bf16x2(x, n_rows, C, out, static_cast<cudaStream_t>(stream));
+}
+
+int ssam_split_bf16x3(const float* x, int n_rows, int C, void* out, void* stream) {
+  return ssam::split_bf16x3(x, n_rows, C, out, static_cast<cudaStream_t>(stream));
+}
+
+int ssam_patch_im2col_split3(const float* img, int B, int Cin, int H, int W, int p, void* out, void* stream) {
+  return ssam::patch_im2col_split3(img, B, Cin, H, W, p, out, static_cast<cudaStream_t>(stream));
 }
 
 }  // extern "C"

@@ -81,15 +81,29 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
 // Wait until the phase with the given parity has completed. Returns false (and
 // raises SSAM_ERR_TIMEOUT on the device flag) when neither the iteration cap
 // nor the ~2 s wall-clock limit is met; callers must then unwind.
+// try_wait that may suspend the thread for up to `hint_ns` until the phase
+// completes (no issue slots are spent while suspended).
+__device__ __forceinline__ bool mbar_try_wait_sleep(uint64_t* bar, uint32_t parity, uint32_t hint_ns) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}\n"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity), "r"(hint_ns)
+      : "memory");
+  return ok != 0;
+}
+
+// Bounded wait: suspended try_waits of at most 100 us each, abandoned after 2 s
+// (globaltimer) or 4e9 SM cycles, whichever comes first.
 __device__ __noinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
   if (mbar_try_wait(bar, parity)) return true;
   const uint64_t t0 = globaltimer_ns();
   const long long c0 = clock64();
   for (uint32_t it = 0; it < kWaitMaxIters; ++it) {
-    if (mbar_try_wait(bar, parity)) return true;
-    if ((it & 255u) == 255u &&
-        (globaltimer_ns() - t0 > kWaitTimeoutNs || clock64() - c0 > kWaitTimeoutCycles))
-      break;
+    if (mbar_try_wait_sleep(bar, parity, 100000u)) return true;
+    if (globaltimer_ns() - t0 > kWaitTimeoutNs || clock64() - c0 > kWaitTimeoutCycles) break;
   }
   set_device_error(SSAM_ERR_TIMEOUT);
   return false;

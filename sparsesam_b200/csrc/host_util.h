@@ -34,9 +34,10 @@ int keep_select(const int32_t* inv_perm_group, int B, int heads, int N, int keep
                 cudaStream_t stream);
 int a_shape_n_init(int N, int n_block, double ratio, int is_global);
 int a_shape_mask(int N, int m_block, int n_block, int n_init, int with_diag, uint8_t* mask);
+size_t sparse_attn_workspace_size(int n_seq, int heads, int win);
 int sparse_attn_fwd(const void* qkv, int64_t ld_qkv, int n_seq, int heads, int win, int d, const void* rel_pos_h,
                     const void* rel_pos_w, const int32_t* perm, int n_init_blocks, int with_diag, float scale,
-                    void* out, int64_t ld_out, cudaStream_t stream);
+                    void* out, int64_t ld_out, void* workspace, size_t workspace_bytes, cudaStream_t stream);
 int layernorm_gather(const float* x, int64_t ldx, const int32_t* src_rows, int n_rows, int C, const float* w,
                      const float* b, float eps, void* out, int64_t ld_out, cudaStream_t stream);
 int layernorm_rows(const float* x, int n_rows, int C, const float* w, const float* b, float eps, void* out,
@@ -47,6 +48,8 @@ int broadcast_rows(const float* pos, int B, int T, int C, float* x, cudaStream_t
 int im2col3x3_nhwc(const void* in, int B, int H, int W, int C, void* out, cudaStream_t stream);
 int nhwc_to_nchw(const float* in, int B, int HW, int C, float* out, cudaStream_t stream);
 int split_bf16x2(const float* x, int n_rows, int C, void* out, cudaStream_t stream);
+int split_bf16x3(const float* x, int n_rows, int C, void* out, cudaStream_t stream);
+int patch_im2col_split3(const float* img, int B, int Cin, int H, int W, int p, void* out, cudaStream_t stream);
 size_t rc_mlp_workspace_size(int n_rows, int C, int hidden);
 int rc_mlp_fwd(float* x, int64_t ldx, const int32_t* rows, int n_rows, int C, int hidden, const float* ln_w,
                const float* ln_b, float eps, const void* w1, const float* b1, const void* w2, const float* b2,

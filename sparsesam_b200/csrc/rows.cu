@@ -192,6 +192,43 @@ int patch_im2col(const float* img, int B, int Cin, int H, int W, int p, void* ou
   return status_from_cuda(cudaGetLastError());
 }
 
+// Patch-embed im2col with the 3-term split of every pixel: a row holds
+// [hi | lo | hi] (3 Cin p p columns, each part in (cin, ky, kx) order) with
+// hi = bf16(x) and lo = bf16(x - hi); against [W_hi | W_hi | W_lo] the GEMM sums
+// x_hi W_hi + x_lo W_hi + x_hi W_lo, i.e. the fp32 product up to the lo*lo term.
+__global__ void patch_im2col_split3_kernel(const float* __restrict__ img, int B, int Cin, int H, int W, int p,
+                                           __nv_bfloat16* __restrict__ out) {
+  const int gh = H / p, gw = W / p;
+  const int64_t total = static_cast<int64_t>(B) * gh * gw * Cin * p;
+  const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (i >= total) return;
+  const int ky = static_cast<int>(i % p);
+  const int cin = static_cast<int>((i / p) % Cin);
+  const int64_t tok = i / (static_cast<int64_t>(p) * Cin);
+  const int px = static_cast<int>(tok % gw), py = static_cast<int>((tok / gw) % gh);
+  const int b = static_cast<int>(tok / (static_cast<int64_t>(gw) * gh));
+  const int K = Cin * p * p;
+  const float* src = img + ((static_cast<int64_t>(b) * Cin + cin) * H + (py * p + ky)) * W + px * p;
+  __nv_bfloat16* dst = out + tok * (3 * static_cast<int64_t>(K)) + (cin * p + ky) * p;
+  for (int kx = 0; kx < p; kx += 2) {
+    const float2 v = *reinterpret_cast<const float2*>(src + kx);
+    const float h0 = __bfloat162float(__float2bfloat16_rn(v.x)), h1 = __bfloat162float(__float2bfloat16_rn(v.y));
+    const uint32_t hi = pack_bf16x2(h0, h1);
+    *reinterpret_cast<uint32_t*>(dst + kx) = hi;
+    *reinterpret_cast<uint32_t*>(dst + K + kx) = pack_bf16x2(v.x - h0, v.y - h1);
+    *reinterpret_cast<uint32_t*>(dst + 2 * K + kx) = hi;
+  }
+}
+
+int patch_im2col_split3(const float* img, int B, int Cin, int H, int W, int p, void* out, cudaStream_t stream) {
+  if (img == nullptr || out == nullptr || B <= 0 || Cin <= 0 || p <= 0 || H % p || W % p) return SSAM_ERR_INVALID;
+  if (p % 2 || (reinterpret_cast<uintptr_t>(img) & 7) || (reinterpret_cast<uintptr_t>(out) & 3)) return SSAM_ERR_ALIGN;
+  const int64_t total = static_cast<int64_t>(B) * (H / p) * (W / p) * Cin * p;
+  patch_im2col_split3_kernel<<<static_cast<unsigned>((total + 255) / 256), 256, 0, stream>>>(
+      img, B, Cin, H, W, p, static_cast<__nv_bfloat16*>(out));
+  return status_from_cuda(cudaGetLastError());
+}
+
 __global__ void broadcast_rows_kernel(const float4* __restrict__ pos, int64_t per_image4, int64_t total4,
                                       float4* __restrict__ x) {
   const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
@@ -284,6 +321,34 @@ int split_bf16x2(const float* x, int n_rows, int C, void* out, cudaStream_t stre
   if (C % 4 || !aligned16(x) || (reinterpret_cast<uintptr_t>(out) & 7)) return SSAM_ERR_ALIGN;
   const int64_t n4 = static_cast<int64_t>(n_rows) * (C / 4);
   split_bf16x2_kernel<<<static_cast<unsigned>((n4 + 255) / 256), 256, 0, stream>>>(
+      reinterpret_cast<const float4*>(x), n4, C / 4, static_cast<uint2*>(out));
+  return status_from_cuda(cudaGetLastError());
+}
+
+// 3-term split of fp32 rows: out[r] = [hi | lo | hi] (3 C columns), hi = bf16(x),
+// lo = bf16(x - hi); against [W_hi | W_hi | W_lo] a GEMM carries both the fp32
+// activation and the fp32 weight up to the lo*lo term.
+__global__ void split_bf16x3_kernel(const float4* __restrict__ x, int64_t n4, int c4, uint2* __restrict__ out) {
+  const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (i >= n4) return;
+  const int64_t r = i / c4;
+  const int c = static_cast<int>(i - r * c4);
+  const float4 v = __ldg(x + i);
+  const float h0 = __bfloat162float(__float2bfloat16_rn(v.x)), h1 = __bfloat162float(__float2bfloat16_rn(v.y));
+  const float h2 = __bfloat162float(__float2bfloat16_rn(v.z)), h3 = __bfloat162float(__float2bfloat16_rn(v.w));
+  const uint2 hi = make_uint2(pack_bf16x2(h0, h1), pack_bf16x2(h2, h3));
+  uint2* row = out + r * 3 * c4;
+  row[c] = hi;
+  row[c4 + c] = make_uint2(pack_bf16x2(v.x - h0, v.y - h1), pack_bf16x2(v.z - h2, v.w - h3));
+  row[2 * c4 + c] = hi;
+}
+
+int split_bf16x3(const float* x, int n_rows, int C, void* out, cudaStream_t stream) {
+  if (x == nullptr || out == nullptr || n_rows < 0 || C <= 0) return SSAM_ERR_INVALID;
+  if (n_rows == 0) return SSAM_OK;
+  if (C % 4 || !aligned16(x) || (reinterpret_cast<uintptr_t>(out) & 7)) return SSAM_ERR_ALIGN;
+  const int64_t n4 = static_cast<int64_t>(n_rows) * (C / 4);
+  split_bf16x3_kernel<<<static_cast<unsigned>((n4 + 255) / 256), 256, 0, stream>>>(
       reinterpret_cast<const float4*>(x), n4, C / 4, static_cast<uint2*>(out));
   return status_from_cuda(cudaGetLastError());
 }

@@ -203,11 +203,14 @@ def sparse_attn(qkv: torch.Tensor, n_seq: int, heads: int, win: int, d: int, rel
     if out is None:
         out = torch.empty(n_seq * N, heads * d, dtype=torch.bfloat16, device=qkv.device)
     ld_out = _rowmajor(out, "out")
+    ws_bytes = int(_lib.load().ssam_sparse_attn_workspace_size(n_seq, heads, win, d))
+    ws = torch.empty(ws_bytes, dtype=torch.uint8, device=qkv.device) if ws_bytes else None
     t0 = KernelTimer.begin()
     _lib.call("ssam_sparse_attn_fwd", qkv.data_ptr(), ld, n_seq, heads, win, d, rel_pos_h.data_ptr(),
               rel_pos_w.data_ptr(), perm.data_ptr(), n_init_blocks, 1 if with_diag else 0, float(scale),
-              out.data_ptr(), ld_out, _stream(qkv))
-    KernelTimer.end(t0, "attention", attention_flops(n_seq * heads, N, d, n_init_blocks, with_diag))
+              out.data_ptr(), ld_out, _ptr(ws), ws_bytes, _stream(qkv), launches=2 if ws_bytes else 1)
+    KernelTimer.end(t0, "attention_global" if ws_bytes else "attention_window",
+                    attention_flops(n_seq * heads, N, d, n_init_blocks, with_diag))
     return out
 
 
@@ -284,6 +287,17 @@ def patch_im2col(img: torch.Tensor, p: int, out: torch.Tensor | None = None) -> 
     return out
 
 
+def patch_im2col_split3(img: torch.Tensor, p: int, out: torch.Tensor | None = None) -> torch.Tensor:
+    """fp32 NCHW image -> bf16 (tokens, 3 Cin p p) = [hi | lo | hi] patch rows."""
+    _check_cuda(img, out)
+    img = img.contiguous().float()
+    B, Cin, H, W = img.shape
+    if out is None:
+        out = torch.empty(B * (H // p) * (W // p), 3 * Cin * p * p, dtype=torch.bfloat16, device=img.device)
+    _lib.call("ssam_patch_im2col_split3", img.data_ptr(), B, Cin, H, W, p, out.data_ptr(), _stream(img))
+    return out
+
+
 def broadcast_rows(pos: torch.Tensor, B: int, out: torch.Tensor) -> torch.Tensor:
     _check_cuda(pos, out)
     T, C = pos.shape[-3] * pos.shape[-2] if pos.dim() == 4 else pos.shape[0], pos.shape[-1]
@@ -331,3 +345,24 @@ def split_bf16x2(x: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tens
         out = torch.empty(n, 2 * C, dtype=torch.bfloat16, device=x.device)
     _lib.call("ssam_split_bf16x2", x2.data_ptr(), n, C, out.data_ptr(), _stream(x))
     return out
+
+
+def split_bf16x3(x: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
+    """fp32 (rows, C) -> bf16 (rows, 3C) = [hi | lo | hi]; pair with weights [W_hi | W_hi | W_lo]."""
+    _check_cuda(x, out)
+    x2 = x.reshape(-1, x.shape[-1])
+    if x2.dtype != torch.float32 or not x2.is_contiguous():
+        raise TypeError("split_bf16x3 takes a contiguous fp32 tensor")
+    n, C = x2.shape
+    if out is None:
+        out = torch.empty(n, 3 * C, dtype=torch.bfloat16, device=x.device)
+    _lib.call("ssam_split_bf16x3", x2.data_ptr(), n, C, out.data_ptr(), _stream(x))
+    return out
+
+
+def split_weight3(w: torch.Tensor) -> torch.Tensor:
+    """fp32 weight (N, K) -> bf16 (N, 3K) = [W_hi | W_hi | W_lo] (setup-time, host side of the split GEMM)."""
+    w = w.float()
+    hi = w.to(torch.bfloat16)
+    lo = (w - hi.float()).to(torch.bfloat16)
+    return torch.cat([hi, hi, lo], dim=1).contiguous()

@@ -273,12 +273,20 @@ def _stem_neck_weights(enc) -> _StemNeckWeights:
         pos = None
         if enc.pos_embed is not None:
             pos = enc.pos_embed.detach().to(torch.float32).reshape(-1, C).contiguous()
+        # The stem and the neck run at fp32 accuracy on the tensor cores: their
+        # activations enter as [hi | lo | hi] bf16 splits and the weights as
+        # [W_hi | W_hi | W_lo] (ops.split_weight3), three times K. These few GEMMs
+        # carry no sparsity and cost under 1% of the encoder's FLOPs; kept at bf16
+        # the patch embedding alone adds about 5e-3 to the output embeddings.
+        n2 = n[2].weight.detach().float().permute(0, 2, 3, 1)  # (out, ky, kx, cin)
+        n2_hi = n2.to(torch.bfloat16)
+        n2_lo = (n2 - n2_hi.float()).to(torch.bfloat16)
         w = _StemNeckWeights(
-            patch_w=_bf16(conv.weight.reshape(C, -1)), patch_b=_f32(conv.bias, C, dev), pos=pos,
-            # [W | W] against the hi/lo split of the fp32 activations (ops.split_bf16x2)
-            neck0_w=_bf16(n[0].weight.reshape(n[0].weight.shape[0], -1).repeat(1, 2)),
+            patch_w=ops.split_weight3(conv.weight.detach().reshape(C, -1)),
+            patch_b=_f32(conv.bias, C, dev), pos=pos,
+            neck0_w=ops.split_weight3(n[0].weight.detach().reshape(n[0].weight.shape[0], -1)),
             ln_a_w=_f32(n[1].weight, 0, dev), ln_a_b=_f32(n[1].bias, 0, dev),
-            neck2_w=_bf16(n[2].weight.permute(0, 2, 3, 1).repeat(1, 1, 1, 2).reshape(n[2].weight.shape[0], -1)),
+            neck2_w=torch.cat([n2_hi, n2_hi, n2_lo], dim=3).reshape(n2.shape[0], -1).contiguous(),
             ln_b_w=_f32(n[3].weight, 0, dev), ln_b_b=_f32(n[3].bias, 0, dev),
             eps_a=float(getattr(n[1], "eps", 1e-6)), eps_b=float(getattr(n[3], "eps", 1e-6)))
         enc._ssam_w = w
@@ -298,7 +306,7 @@ def encoder_forward(enc, img: torch.Tensor):
     gh, gw = Hi // p, Wi // p
     C = conv.weight.shape[0]
     T = gh * gw
-    cols = ops.patch_im2col(img.to(torch.float32), p)
+    cols = ops.patch_im2col_split3(img.to(torch.float32), p)
     x = torch.empty(B * T, C, dtype=torch.float32, device=img.device)
     if w.pos is not None:
         ops.broadcast_rows(w.pos, B, x)
@@ -310,10 +318,10 @@ def encoder_forward(enc, img: torch.Tensor):
         blk._forward_residual(x, B, gh, gw)
         if blk.window_size == 0:
             interm.append(x.view(B, gh, gw, C).clone())
-    # neck: fp32 activations enter the GEMMs as a hi/lo bf16 split (2x K)
-    y = ops.gemm_bf16(ops.split_bf16x2(x), w.neck0_w, None, epilogue=ops.SSAM_EPI_F32)
+    # neck: fp32 activations and weights through the 3-term split (3x K)
+    y = ops.gemm_bf16(ops.split_bf16x3(x), w.neck0_w, None, epilogue=ops.SSAM_EPI_F32)
     ya = ops.layernorm_rows(y, w.ln_a_w, w.ln_a_b, w.eps_a, out_bf16=False)
-    cols3 = ops.im2col3x3_nhwc(ops.split_bf16x2(ya).view(B, gh, gw, -1))
+    cols3 = ops.im2col3x3_nhwc(ops.split_bf16x3(ya).view(B, gh, gw, -1))
     z = ops.gemm_bf16(cols3, w.neck2_w, None, epilogue=ops.SSAM_EPI_F32)
     z = ops.layernorm_rows(z, w.ln_b_w, w.ln_b_b, w.eps_b, out_bf16=False)
     feats = ops.nhwc_to_nchw(z, B, gh, gw, z.shape[1])

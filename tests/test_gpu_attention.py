@@ -68,3 +68,14 @@ def test_identity_perm_dense_matches_sdpa(cuda_device):
     ref = torch.nn.functional.scaled_dot_product_attention(q, k, v).permute(0, 2, 1, 3).reshape(n_seq * N, C)
     assert (out.float() - ref).abs().max().item() < 2e-2
     assert ops.device_error() == 0
+
+
+@pytest.mark.parametrize("d", [64, 80])
+@pytest.mark.parametrize("win,n_seq,heads,is_global", [(14, 300, 2, False), (64, 3, 4, True)])
+def test_persistent_ctas_run_many_tiles(cuda_device, d, win, n_seq, heads, is_global):
+    """More query tiles than SMs: every CTA walks several tiles, which exercises the
+    double-buffered O accumulators, the deferred epilogue and the Q/bias reuse."""
+    err, _ = _case(cuda_device, n_seq=n_seq, heads=heads, win=win, d=d, ratio=0.3, is_global=is_global, seed=3)
+    assert err.max().item() < 3e-2, err.max().item()
+    assert err.mean().item() < 3e-3
+    assert ops.device_error() == 0

@@ -86,3 +86,36 @@ def test_neck_pieces(cuda_device):
     xb = torch.empty(B * H * W, 32, device=cuda_device)
     ops.broadcast_rows(pos, B, xb)
     assert torch.equal(xb.view(B, H * W, 32), pos.expand(B, -1, -1))
+
+
+def test_split_bf16x3_parts(cuda_device):
+    x = torch.randn(37, 96, device=cuda_device) * 3
+    out = ops.split_bf16x3(x).float()
+    hi, lo, hi2 = out[:, :96], out[:, 96:192], out[:, 192:]
+    assert torch.equal(hi, x.to(torch.bfloat16).float())
+    assert torch.equal(hi2, hi)
+    assert torch.equal(lo, (x - hi).to(torch.bfloat16).float())
+    assert (hi + lo - x).abs().max().item() <= 2.0 ** -16 * x.abs().max().item()
+
+
+def test_patch_embed_split3_matches_fp32_conv(cuda_device):
+    """[hi | lo | hi] patches x [W_hi | W_hi | W_lo]: the stem GEMM at fp32 accuracy."""
+    img = torch.randn(2, 3, 64, 64, device=cuda_device)
+    conv = torch.nn.Conv2d(3, 96, 16, 16).to(cuda_device)
+    cols = ops.patch_im2col_split3(img, 16)
+    assert cols.shape == (2 * 16, 3 * 768)
+    single = ops.patch_im2col(img, 16)
+    assert torch.equal(cols[:, :768], single) and torch.equal(cols[:, 1536:], single)
+    w3 = ops.split_weight3(conv.weight.detach().reshape(96, -1))
+    out = ops.gemm_bf16(cols, w3, conv.bias.detach().float().contiguous(), epilogue=ops.SSAM_EPI_F32)
+    with torch.backends.cudnn.flags(allow_tf32=False):
+        ref = conv(img).permute(0, 2, 3, 1).reshape(-1, 96)
+    assert (out - ref).abs().max().item() < 2e-4
+
+
+def test_split3_gemm_matches_fp32_linear(cuda_device):
+    x = torch.randn(300, 256, device=cuda_device)
+    w = torch.randn(128, 256, device=cuda_device) * 0.05
+    out = ops.gemm_bf16(ops.split_bf16x3(x), ops.split_weight3(w), None, epilogue=ops.SSAM_EPI_F32)
+    ref = (x.double() @ w.double().T).float()
+    assert (out - ref).abs().max().item() < 1e-4
