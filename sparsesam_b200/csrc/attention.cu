@@ -11,19 +11,18 @@
 // and the result of permuted row p is written to raster token perm[p]
 // (the inverse permutation and the head merge are fused into the store).
 //
-// Persistent, warp-specialised CTA (one per SM), 288 threads:
-//   warps 0-3  softmax warpgroup: thread i owns query row i of the current
-//              128-query tile; runs the online softmax out of TMEM, writes P
-//              (bf16) back into the TMEM columns of its S block, places the
-//              rel-pos bias operand of the next tile in TMEM and does the
-//              deferred epilogue of the previous tile;
-//   warps 4-7  loaders: coalesced cp.async gathers of the permuted Q / K / V
-//              rows (eight lanes per 128-byte row segment) into 128-key stages,
-//              the one-hot key-position operand, and (global grids) the
-//              precomputed bias rows;
-//   warp 8     UMMA issuer: S = Q K^T + A_bias onehot^T (A_bias from TMEM),
-//              O += P V (P from TMEM, V as one N = D operand); for windowed
-//              grids also [P_H | P_W] = Q [Th ; Tw]^T of the next tile.
+// Persistent, warp-specialised CTA (one per SM), 416 threads:
+//   warps 0-7   softmax: warps w and w+4 share TMEM lane quarter w % 4 (query
+//               rows 32(w%4)..+31 of the tile) and split each 128-key block
+//               into two 64-key halves; the row maxima are exchanged through
+//               shared memory. They also place the next tile's rel-pos bias
+//               operand in TMEM and run the deferred epilogue, split the same way;
+//   warps 8-11  loaders: coalesced cp.async gathers of the permuted K (with the
+//               one-hot key-position operand), V and Q rows (eight lanes per
+//               128-byte row segment) and, for global grids, the bias rows;
+//   warp 12     UMMA issuer: S = Q K^T + A_bias onehot^T (A_bias from TMEM),
+//               O += P V (P from TMEM, V as one N = D operand); for windowed
+//               grids also [P_H | P_W] = Q [Th ; Tw]^T of the next tile.
 // Every tcgen05.mma occupies the tensor pipe for about 100 cycles up to N = 128,
 // so the blocks are 128 keys wide and P.V is one MMA per 16 keys.
 // O is rescaled lazily: only when a row maximum grows by more than 2^8 is the
@@ -42,7 +41,7 @@ namespace ssam {
 constexpr int kAttnBM = 128;   // queries per tile
 constexpr int kAttnBN = 128;   // keys per block
 constexpr int kMaskBlk = 64;   // the reference's mask granularity (64-token blocks)
-constexpr int kAttnThreads = 288;
+constexpr int kAttnThreads = 416;
 constexpr int kAttnTmemCols = 512;
 constexpr float kRescaleThreshold = 8.0f;  // log2 units
 
@@ -79,6 +78,11 @@ __device__ __forceinline__ void tmem_st_32x32b_x32(uint32_t taddr, const uint32_
       "r"(r[19]), "r"(r[20]), "r"(r[21]), "r"(r[22]), "r"(r[23]), "r"(r[24]), "r"(r[25]), "r"(r[26]), "r"(r[27]),
       "r"(r[28]), "r"(r[29]), "r"(r[30]), "r"(r[31])
       : "memory");
+}
+__device__ __forceinline__ void tmem_st_32x32b_x8(uint32_t taddr, const uint32_t (&r)[8]) {
+  asm volatile("tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8};" ::"r"(taddr), "r"(r[0]),
+               "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7])
+               : "memory");
 }
 __device__ __forceinline__ void tmem_st_wait() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 
@@ -146,7 +150,8 @@ struct AttnCfg {
   static constexpr int kTmAB = kTmO + kO * D;     // TMEM column of A_bias[0]
   static constexpr int kTmPH = kTmAB + 2 * kABCols;
   static constexpr int kOHBytes = 2 * kAttnBN * kBW * 2;  // one-hot H | W regions per stage
-  static constexpr int kABRow = 68;                       // SMALL bias scratch row (bytes, odd word stride)
+  static constexpr int kABRow = 36;                       // SMALL bias scratch row per half (bytes, odd word stride)
+  static constexpr int kOSplit = D == 80 ? 48 : D / 2;    // O columns of the first softmax half
   static_assert(kTmPH + kPHCols <= kAttnTmemCols, "TMEM plan exceeds 512 columns");
 };
 
@@ -165,15 +170,16 @@ struct AttnLayout {
   using TG = TileGeom<D>;
   static constexpr int kStage = 2 * TG::bytes(kAttnBN) + C::kOHBytes;  // K | V | one-hot
   static constexpr int kTables = SMALL ? TG::bytes(2 * C::kNT) : 0;
-  static constexpr int kABStage = SMALL ? kAttnBM * C::kABRow : kAttnBM * 256;  // scratch / staged bias rows
-  int tab, q, kv, ab, tok, bars, total;
+  static constexpr int kABStage = SMALL ? 2 * kAttnBM * C::kABRow : kAttnBM * 256;  // scratch / staged bias rows
+  int tab, q, kv, ab, tok, xchg, bars, total;
   __host__ __device__ AttnLayout() {
     tab = 0;
     q = align1k(tab + kTables);                   // [2] x bytes(128)
     kv = align1k(q + 2 * TG::bytes(kAttnBM));     // [stages] x kStage
     ab = align1k(kv + C::kStages * kStage);       // kABStage
     tok = ab + kABStage;                          // int [2][128]
-    bars = (tok + 2 * kAttnBM * 4 + 7) & ~7;      // mbarriers
+    xchg = tok + 2 * kAttnBM * 4;                 // float [2 rounds][2 halves][2 values][128]
+    bars = (xchg + 2 * 2 * 2 * kAttnBM * 4 + 7) & ~7;  // mbarriers
     total = bars + 40 * 8 + 16 + 1024;            // + alignment slack
   }
 };
@@ -260,8 +266,9 @@ enum {
   kBarPFull = 27,    // [2]  softmax
   kBarODone = 29,    // [2]  UMMA commit after P.V
   kBarOFree = 31,    // [2]  softmax epilogue
-  kBarDrain = 33,
-  kNumBars = 34
+  kBarXchg = 33,     // [2]  softmax halves exchanged row maxima / sums
+  kBarDrain = 35,
+  kNumBars = 36
 };
 
 template <int D, bool SMALL>
@@ -287,17 +294,18 @@ __global__ void __launch_bounds__(kAttnThreads, 1) sparse_attn_kernel(const Attn
     for (int i = 0; i < 2; ++i) {
       mbar_init(&bars[kBarQFull + i], 256);
       mbar_init(&bars[kBarQEmpty + i], 1);
-      mbar_init(&bars[kBarABFull + i], 128);
+      mbar_init(&bars[kBarABFull + i], 256);
       mbar_init(&bars[kBarSFull + i], 1);
       mbar_init(&bars[kBarSFree + i], 1);
-      mbar_init(&bars[kBarPFull + i], 128);
+      mbar_init(&bars[kBarPFull + i], 256);
       mbar_init(&bars[kBarODone + i], 1);
-      mbar_init(&bars[kBarOFree + i], 128);
+      mbar_init(&bars[kBarOFree + i], 256);
+      mbar_init(&bars[kBarXchg + i], 256);
     }
     mbar_init(&bars[kBarPHFull], 1);
-    mbar_init(&bars[kBarPHFree], 128);
+    mbar_init(&bars[kBarPHFree], 256);
     mbar_init(&bars[kBarABSFull], 128);
-    mbar_init(&bars[kBarABSFree], 128);
+    mbar_init(&bars[kBarABSFree], 256);
     for (int s = 0; s < C::kStages; ++s) {
       mbar_init(&bars[kBarKFull + s], 128);
       mbar_init(&bars[kBarKEmpty + s], 1);
@@ -308,7 +316,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1) sparse_attn_kernel(const Attn
     *abort_flag = 0;
     fence_mbar_init();
   }
-  if (warp == 8) {
+  if (warp == 12) {
     tmem_alloc(tmem_holder, kAttnTmemCols);
     tmem_relinquish();
   }
@@ -330,18 +338,18 @@ __global__ void __launch_bounds__(kAttnThreads, 1) sparse_attn_kernel(const Attn
   };
   auto tile_exists = [&](int lt_) { return static_cast<int>(blockIdx.x) + lt_ * static_cast<int>(gridDim.x) < a.total_tiles; };
 
-  if (warp >= 4 && warp < 8) {
+  if (warp >= 8 && warp < 12) {
     // =========================== loader warps ===========================
-    // Warp 4 + h (h = 0, 1): K rows 64h..64h+63 of each block with their one-hot
-    // rows; warp 6 + h: the V rows. Warp 4 + w also copies Q rows
-    // 32w..32w+31 of each tile; warp 4 the rel-pos tables; warps 6-7 the staged
-    // bias rows (LARGE).
+    // Warp 8 + h (h = 0, 1): K rows 64h..64h+63 of each block with their one-hot
+    // rows; warp 10 + h: the V rows. Warp 8 + w also copies Q rows
+    // 32w..32w+31 of each tile; warp 8 the rel-pos tables; warps 10-11 the
+    // staged bias rows (LARGE).
     // Order: Q(0), then per tile t: Q(t+1), K/V(t, blocks). A copy instruction
     // moves 16 bytes per lane with eight lanes on one 128-byte row segment (four
     // rows per instruction), then the 32-byte tails (sixteen rows); lane l holds
     // the tokens of rows l, l+32, ... and hands them out with shuffles. Rows of
     // padded positions (token < 0) are zero-filled.
-    const int lw = warp - 4;
+    const int lw = warp - 8;
     const int kv = lw >> 1, half = lw & 1;  // kv 0: K, 1: V
     // NS x 32 rows starting at tile row r0, channel offset xcol of each token row.
     auto copy_rows = [&](auto ns_tag, uint32_t region, int R, int r0, const int* tok, const __nv_bfloat16* base,
@@ -492,7 +500,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1) sparse_attn_kernel(const Attn
       }
     }
     cp_async_wait_all();
-  } else if (warp == 8) {
+  } else if (warp == 12) {
     // =========================== UMMA issuer ===========================
     if (lane == 0) {
       const uint32_t idesc_t = make_idesc_bf16(kAttnBM, 2 * C::kNT, 0, 0);
@@ -597,71 +605,76 @@ __global__ void __launch_bounds__(kAttnThreads, 1) sparse_attn_kernel(const Attn
       mbar_wait(&bars[kBarDrain], 0);
     }
   } else {
-    // ======================== softmax warpgroup ========================
-    const uint32_t t_lane = tmem + (static_cast<uint32_t>(warp * 32) << 16);
+    // ========================= softmax warps =========================
+    // Thread (row r, half h): query row r = tid % 128 of the tile, keys 64h..64h+63
+    // of every block, O columns [h ? kOSplit : 0, h ? D : kOSplit).
+    const int r = tid & (kAttnBM - 1);
+    const int h = tid >> 7;
+    const uint32_t t_lane = tmem + (static_cast<uint32_t>((warp & 3) * 32) << 16);
+    const int oc0 = h ? C::kOSplit : 0, oc1 = h ? D : C::kOSplit;
+    float* xchg = reinterpret_cast<float*>(smem + L.xchg);  // [round & 1][half][value][row]
+    int xround = 0;
+    // Publish (max, sum) of this half and read the other half's, through a
+    // 256-thread mbarrier round (bounded wait; double-buffered by round parity).
+    auto exchange = [&](float my_max, float my_sum, float& other_max, float& other_sum) -> bool {
+      float* buf = xchg + (xround & 1) * (4 * kAttnBM);
+      buf[(h * 2 + 0) * kAttnBM + r] = my_max;
+      buf[(h * 2 + 1) * kAttnBM + r] = my_sum;
+      mbar_arrive(&bars[kBarXchg + (xround & 1)]);
+      if (!wait_or_abort(kBarXchg + (xround & 1), (xround >> 1) & 1)) return false;
+      other_max = buf[((h ^ 1) * 2 + 0) * kAttnBM + r];
+      other_sum = buf[((h ^ 1) * 2 + 1) * kAttnBM + r];
+      ++xround;
+      return true;
+    };
 
-    // A_bias of tile lt_ -> TMEM buffer lt_ & 1 (row tid): fp16 pairs, relH/scale
-    // at column j then relW/scale. Called once S of the current tile's first block
-    // is in, so every QK^T that read the buffer's previous contents has completed.
+    // A_bias of tile lt_ -> TMEM buffer lt_ & 1 (row r): fp16 pairs, relH/scale
+    // at column j (half 0 writes these), then relW/scale (half 1). Called once S
+    // of the current tile's first block is in, so every QK^T that read the
+    // buffer's previous contents has completed.
     auto stage_bias = [&](int lt_, int& tok_out) -> bool {
       const uint32_t tAB = t_lane + C::kTmAB + (lt_ & 1) * C::kABCols;
       if constexpr (SMALL) {
         const int qb = lt_ & 1;
         if (!wait_or_abort(kBarQFull + qb, (lt_ >> 1) & 1)) return false;
-        const int t = s_tok[qb * kAttnBM + tid];
+        const int t = s_tok[qb * kAttnBM + r];
         tok_out = t;
         const int qh = t >= 0 ? t / win : 0;
         const int qw = t >= 0 ? t - qh * win : 0;
+        const int qc = h ? qw : qh;
         if (!wait_or_abort(kBarPHFull, lt_ & 1)) return false;
         tc_fence_after();
-        uint8_t* row = smem + L.ab + tid * C::kABRow;  // 16 relH then 16 relW fp16
-        uint32_t rh[32], rw[32];
-        tmem_ld_32x32b_x32(t_lane + C::kTmPH, rh);
-        tmem_ld_32x32b_x32(t_lane + C::kTmPH + C::kNT, rw);
+        uint8_t* rowp = smem + L.ab + (h * kAttnBM + r) * C::kABRow;  // 16 fp16 of this half
+        uint32_t rp[32];
+        tmem_ld_32x32b_x32(t_lane + C::kTmPH + h * C::kNT, rp);
         tmem_ld_wait();
         tc_fence_before();
         mbar_arrive(&bars[kBarPHFree]);
 #pragma unroll
-        for (int j = 0; j < 16; j += 2) {  // padding columns must not hold NaN/Inf
-          *reinterpret_cast<uint32_t*>(row + j * 2) = 0u;
-          *reinterpret_cast<uint32_t*>(row + 32 + j * 2) = 0u;
-        }
+        for (int j = 0; j < 16; j += 2) *reinterpret_cast<uint32_t*>(rowp + j * 2) = 0u;  // no NaN/Inf padding
 #pragma unroll
         for (int c = 0; c < 32; ++c) {
-          const int jh = qh + win - 1 - c;
-          if (jh >= 0 && jh < win)
-            *reinterpret_cast<__half*>(row + jh * 2) = __float2half_rn(__uint_as_float(rh[c]) * a.inv_scale);
-          const int jw = qw + win - 1 - c;
-          if (jw >= 0 && jw < win)
-            *reinterpret_cast<__half*>(row + 32 + jw * 2) = __float2half_rn(__uint_as_float(rw[c]) * a.inv_scale);
+          const int jj = qc + win - 1 - c;
+          if (jj >= 0 && jj < win)
+            *reinterpret_cast<__half*>(rowp + jj * 2) = __float2half_rn(__uint_as_float(rp[c]) * a.inv_scale);
         }
-        uint32_t v[16];
+        uint32_t v[8];
 #pragma unroll
-        for (int i = 0; i < 16; ++i) v[i] = *reinterpret_cast<const uint32_t*>(row + 4 * i);
-        tmem_st_32x32b_x16(tAB, v);
+        for (int i = 0; i < 8; ++i) v[i] = *reinterpret_cast<const uint32_t*>(rowp + 4 * i);
+        tmem_st_32x32b_x8(tAB + h * (C::kBW / 2), v);
       } else {
         if (!wait_or_abort(kBarABSFull, lt_ & 1)) return false;
-        const uint8_t* hrow = smem + L.ab + tid * 128;
-        const uint8_t* wrow = hrow + kAttnBM * 128;
+        const uint8_t* hrow = smem + L.ab + h * (kAttnBM * 128) + r * 128;
         uint32_t v[32];
 #pragma unroll
         for (int c = 0; c < 8; ++c) {
-          const uint4 x = *reinterpret_cast<const uint4*>(hrow + ((c ^ (tid & 7)) << 4));
+          const uint4 x = *reinterpret_cast<const uint4*>(hrow + ((c ^ (r & 7)) << 4));
           v[4 * c] = x.x;
           v[4 * c + 1] = x.y;
           v[4 * c + 2] = x.z;
           v[4 * c + 3] = x.w;
         }
-        tmem_st_32x32b_x32(tAB, v);
-#pragma unroll
-        for (int c = 0; c < 8; ++c) {
-          const uint4 x = *reinterpret_cast<const uint4*>(wrow + ((c ^ (tid & 7)) << 4));
-          v[4 * c] = x.x;
-          v[4 * c + 1] = x.y;
-          v[4 * c + 2] = x.z;
-          v[4 * c + 3] = x.w;
-        }
-        tmem_st_32x32b_x32(tAB + 32, v);
+        tmem_st_32x32b_x32(tAB + h * 32, v);
         mbar_arrive(&bars[kBarABSFree]);
       }
       tmem_st_wait();
@@ -669,7 +682,8 @@ __global__ void __launch_bounds__(kAttnThreads, 1) sparse_attn_kernel(const Attn
       mbar_arrive(&bars[kBarABFull + (lt_ & 1)]);
       return true;
     };
-    // O / l of tile lt_, stored at the raster token (inverse permutation and head merge)
+    // This half's O columns / l of tile lt_, stored at the raster token
+    // (inverse permutation and head merge)
     auto epilogue = [&](int lt_, int g_last, int tok, float l) -> bool {
       const int tile = blockIdx.x + lt_ * gridDim.x;
       const int row = tile / a.n_tiles;
@@ -683,6 +697,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1) sparse_attn_kernel(const Attn
       const uint32_t tO = t_lane + C::kTmO + (lt_ % C::kO) * D;
 #pragma unroll
       for (int c0 = 0; c0 < D; c0 += 16) {
+        if (c0 < oc0 || c0 >= oc1) continue;
         uint32_t r16[16];
         tmem_ld_32x32b_x16(tO + c0, r16);
         tmem_ld_wait();
@@ -704,7 +719,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1) sparse_attn_kernel(const Attn
     auto query_token = [&](int lt_) -> int {
       const int tile = blockIdx.x + lt_ * gridDim.x;
       const int row = tile / a.n_tiles, qtile = tile - row * a.n_tiles;
-      const int p = qtile * kAttnBM + tid;
+      const int p = qtile * kAttnBM + r;
       return p < N ? __ldg(a.perm + static_cast<int64_t>(row) * N + p) : -1;
     };
 
@@ -715,48 +730,51 @@ __global__ void __launch_bounds__(kAttnThreads, 1) sparse_attn_kernel(const Attn
       if (!SMALL) tok_cur = query_token(0);
     }
     int pend_lt = -1, pend_g = -1, pend_tok = -1;  // deferred epilogue
-    float pend_l = 0.f;
+    float pend_l = 0.f;  // this half's share of the pending tile's row sum
     int g = 0;
     for (int lt = 0; ok && tile_exists(lt); ++lt) {
       const int tile = blockIdx.x + lt * gridDim.x;
       const int qtile = tile % a.n_tiles;
       const TileBlocks tb(a, qtile);
-      const int my_mb = 2 * qtile + (tid >= 64 ? 1 : 0);
+      const int my_mb = 2 * qtile + (r >= 64 ? 1 : 0);
       const uint32_t tO = t_lane + C::kTmO + (lt % C::kO) * D;
       if (!SMALL && tile_exists(lt + 1)) tok_next = query_token(lt + 1);
-      float m_run = -INFINITY, l_run = 0.f;
+      float m_run = -INFINITY, l_run = 0.f;  // l_run: this half's share of the row sum
       for (int j = 0; j < tb.n; ++j, ++g) {
         const int sbuf = g % C::kS;
         const int kb = tb.at(j);
         if (!(ok = wait_or_abort(kBarSFull + sbuf, (g / C::kS) & 1))) break;
         tc_fence_after();
-        const uint32_t tS = t_lane + sbuf * kAttnBN;
-        // 64-key halves of the block: enabled by the keep bar or the diagonal
-        const int m0 = 2 * kb;
-        const bool full = m0 + 1 < tb.nk && (kb + 1) * kAttnBN <= N;
-        const int kvalid = N - kb * kAttnBN;  // keys of the block inside the sequence
-        const bool on0 = full || m0 < tb.nk || (a.with_diag && m0 == my_mb);
-        const bool on1 = full || m0 + 1 < tb.nk || (a.with_diag && m0 + 1 == my_mb);
-        // pass 1: row maximum of the raw logits (scale > 0 commutes with max)
-        float mx = -INFINITY;
-#pragma unroll
-        for (int h = 0; h < 2; ++h) {
-          uint32_t s0[32], s1[32];
-          tmem_ld_32x32b_x32(tS + 64 * h, s0);
-          tmem_ld_32x32b_x32(tS + 64 * h + 32, s1);
+        const uint32_t tS = t_lane + sbuf * kAttnBN + 64 * h;
+        // this half's 64 keys: 64-key mask block 2 kb + h
+        const int mh = 2 * kb + h;
+        const bool full = 2 * kb + 1 < tb.nk && (kb + 1) * kAttnBN <= N;
+        const int kvalid = N - kb * kAttnBN - 64 * h;  // keys of this half inside the sequence
+        const bool on = full || mh < tb.nk || (a.with_diag && mh == my_mb);
+        uint32_t s[64];
+        {
+          uint32_t (&s0)[32] = *reinterpret_cast<uint32_t(*)[32]>(&s[0]);
+          uint32_t (&s1)[32] = *reinterpret_cast<uint32_t(*)[32]>(&s[32]);
+          tmem_ld_32x32b_x32(tS, s0);
+          tmem_ld_32x32b_x32(tS + 32, s1);
           tmem_ld_wait();
-          const bool on = h == 0 ? on0 : on1;
-          if (full) {
-#pragma unroll
-            for (int jj = 0; jj < 32; ++jj) mx = fmaxf(mx, fmaxf(__uint_as_float(s0[jj]), __uint_as_float(s1[jj])));
-          } else if (on) {
-#pragma unroll
-            for (int jj = 0; jj < 32; ++jj) {
-              if (64 * h + jj < kvalid) mx = fmaxf(mx, __uint_as_float(s0[jj]));
-              if (64 * h + 32 + jj < kvalid) mx = fmaxf(mx, __uint_as_float(s1[jj]));
-            }
-          }
         }
+        // row maximum of the raw logits over both halves (scale > 0 commutes with max)
+        float mx4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+        if (full) {
+#pragma unroll
+          for (int jj = 0; jj < 64; ++jj) mx4[jj & 3] = fmaxf(mx4[jj & 3], __uint_as_float(s[jj]));
+        } else if (on) {
+#pragma unroll
+          for (int jj = 0; jj < 64; ++jj)
+            if (jj < kvalid) mx4[jj & 3] = fmaxf(mx4[jj & 3], __uint_as_float(s[jj]));
+        }
+        float mx = fmaxf(fmaxf(mx4[0], mx4[1]), fmaxf(mx4[2], mx4[3]));
+        float mx_other, l_other;
+        // block 0's exchange also hands over the pending tile's row-sum shares
+        if (!(ok = exchange(mx, j == 0 ? pend_l : 0.f, mx_other, l_other))) break;
+        if (j == 0) pend_l += l_other;
+        mx = fmaxf(mx, mx_other);
         mx = mx == -INFINITY ? -INFINITY : mx * a.scale_log2;
         const float m_new = fmaxf(m_run, mx);
         float m_use = m_run;
@@ -769,7 +787,6 @@ __global__ void __launch_bounds__(kAttnThreads, 1) sparse_attn_kernel(const Attn
         }
         const float m_off = m_use == -INFINITY ? 0.f : m_use;
         const float alpha = rescale ? fast_exp2(m_run - m_use) : 1.f;
-        float sum = 0.f;
         // tcgen05.ld/st are warp-collective (.sync.aligned): the O rescale runs on
         // the whole warp when any of its rows needs it (the others scale by 1).
         if (__any_sync(0xffffffffu, rescale)) {
@@ -777,6 +794,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1) sparse_attn_kernel(const Attn
           tc_fence_after();
 #pragma unroll
           for (int c0 = 0; c0 < D; c0 += 16) {
+            if (c0 < oc0 || c0 >= oc1) continue;
             uint32_t r16[16];
             tmem_ld_32x32b_x16(tO + c0, r16);
             tmem_ld_wait();
@@ -785,41 +803,30 @@ __global__ void __launch_bounds__(kAttnThreads, 1) sparse_attn_kernel(const Attn
             tmem_st_32x32b_x16(tO + c0, r16);
           }
         }
-        // pass 2: P = exp2(s * scale log2e - m) as bf16 pairs, kept in registers
-        // and stored over the first 64 S columns once every S chunk has been read
-        uint32_t pk[64];
+        // P = exp2(s * scale log2e - m) as bf16 pairs over this half's 32 P columns
+        uint32_t pk[32];
+        float sum4[4] = {0.f, 0.f, 0.f, 0.f};
+        if (full) {
 #pragma unroll
-        for (int q4 = 0; q4 < 4; ++q4) {
-          uint32_t sq[32];
-          tmem_ld_32x32b_x32(tS + 32 * q4, sq);
-          tmem_ld_wait();
-          if (full) {
+          for (int e = 0; e < 32; ++e) {
+            const float p0 = fast_exp2(fmaf(__uint_as_float(s[2 * e]), a.scale_log2, -m_off));
+            const float p1 = fast_exp2(fmaf(__uint_as_float(s[2 * e + 1]), a.scale_log2, -m_off));
+            sum4[e & 3] += p0 + p1;
+            pk[e] = pack_bf16x2(p0, p1);
+          }
+        } else {
 #pragma unroll
-            for (int e = 0; e < 16; ++e) {
-              const float p0 = fast_exp2(fmaf(__uint_as_float(sq[2 * e]), a.scale_log2, -m_off));
-              const float p1 = fast_exp2(fmaf(__uint_as_float(sq[2 * e + 1]), a.scale_log2, -m_off));
-              sum += p0 + p1;
-              pk[16 * q4 + e] = pack_bf16x2(p0, p1);
-            }
-          } else {
-            const bool on = q4 < 2 ? on0 : on1;
-#pragma unroll
-            for (int e = 0; e < 16; ++e) {
-              const bool v0 = on && 32 * q4 + 2 * e < kvalid;
-              const bool v1 = on && 32 * q4 + 2 * e + 1 < kvalid;
-              const float p0 = v0 ? fast_exp2(fmaf(__uint_as_float(sq[2 * e]), a.scale_log2, -m_off)) : 0.f;
-              const float p1 = v1 ? fast_exp2(fmaf(__uint_as_float(sq[2 * e + 1]), a.scale_log2, -m_off)) : 0.f;
-              sum += p0 + p1;
-              pk[16 * q4 + e] = pack_bf16x2(p0, p1);
-            }
+          for (int e = 0; e < 32; ++e) {
+            const bool v0 = on && 2 * e < kvalid;
+            const bool v1 = on && 2 * e + 1 < kvalid;
+            const float p0 = v0 ? fast_exp2(fmaf(__uint_as_float(s[2 * e]), a.scale_log2, -m_off)) : 0.f;
+            const float p1 = v1 ? fast_exp2(fmaf(__uint_as_float(s[2 * e + 1]), a.scale_log2, -m_off)) : 0.f;
+            sum4[e & 3] += p0 + p1;
+            pk[e] = pack_bf16x2(p0, p1);
           }
         }
-        {
-          uint32_t (&p0)[32] = *reinterpret_cast<uint32_t(*)[32]>(&pk[0]);
-          uint32_t (&p1)[32] = *reinterpret_cast<uint32_t(*)[32]>(&pk[32]);
-          tmem_st_32x32b_x32(tS, p0);
-          tmem_st_32x32b_x32(tS + 32, p1);
-        }
+        tmem_st_32x32b_x32(t_lane + sbuf * kAttnBN + 32 * h, pk);
+        const float sum = (sum4[0] + sum4[1]) + (sum4[2] + sum4[3]);
         l_run = (j == 0 ? 0.f : l_run * alpha) + sum;
         m_run = m_use;
         tmem_st_wait();
@@ -840,13 +847,16 @@ __global__ void __launch_bounds__(kAttnThreads, 1) sparse_attn_kernel(const Attn
       pend_l = l_run;
       tok_cur = tok_next;
     }
-    if (ok && pend_lt >= 0) epilogue(pend_lt, pend_g, pend_tok, pend_l);
+    if (ok && pend_lt >= 0) {  // the last tile's row-sum shares
+      float m_unused, l_other;
+      if (exchange(0.f, pend_l, m_unused, l_other)) epilogue(pend_lt, pend_g, pend_tok, pend_l + l_other);
+    }
   }
 
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
-  if (warp == 8) tmem_dealloc(tmem, kAttnTmemCols);
+  if (warp == 12) tmem_dealloc(tmem, kAttnTmemCols);
 }
 
 // ---------------------------------------------------------------------------
