@@ -266,9 +266,9 @@ enum {
   kBarPFull = 27,    // [2]  softmax
   kBarODone = 29,    // [2]  UMMA commit after P.V
   kBarOFree = 31,    // [2]  softmax epilogue
-  kBarXchg = 33,     // [2]  softmax halves exchanged row maxima / sums
-  kBarDrain = 35,
-  kNumBars = 36
+  kBarXchg = 33,     // [2 rounds][4 lane quarters]  the two softmax warps of a quarter
+  kBarDrain = 41,
+  kNumBars = 42
 };
 
 template <int D, bool SMALL>
@@ -300,7 +300,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1) sparse_attn_kernel(const Attn
       mbar_init(&bars[kBarPFull + i], 256);
       mbar_init(&bars[kBarODone + i], 1);
       mbar_init(&bars[kBarOFree + i], 256);
-      mbar_init(&bars[kBarXchg + i], 256);
+      for (int w = 0; w < 4; ++w) mbar_init(&bars[kBarXchg + 4 * i + w], 64);
     }
     mbar_init(&bars[kBarPHFull], 1);
     mbar_init(&bars[kBarPHFree], 256);
@@ -620,8 +620,9 @@ __global__ void __launch_bounds__(kAttnThreads, 1) sparse_attn_kernel(const Attn
       float* buf = xchg + (xround & 1) * (4 * kAttnBM);
       buf[(h * 2 + 0) * kAttnBM + r] = my_max;
       buf[(h * 2 + 1) * kAttnBM + r] = my_sum;
-      mbar_arrive(&bars[kBarXchg + (xround & 1)]);
-      if (!wait_or_abort(kBarXchg + (xround & 1), (xround >> 1) & 1)) return false;
+      const int xb = kBarXchg + 4 * (xround & 1) + (warp & 3);
+      mbar_arrive(&bars[xb]);
+      if (!wait_or_abort(xb, (xround >> 1) & 1)) return false;
       other_max = buf[((h ^ 1) * 2 + 0) * kAttnBM + r];
       other_sum = buf[((h ^ 1) * 2 + 1) * kAttnBM + r];
       ++xround;
@@ -745,6 +746,11 @@ __global__ void __launch_bounds__(kAttnThreads, 1) sparse_attn_kernel(const Attn
         const int kb = tb.at(j);
         if (!(ok = wait_or_abort(kBarSFull + sbuf, (g / C::kS) & 1))) break;
         tc_fence_after();
+        // Windowed grids stage the next tile's bias operand before this block's
+        // softmax (their tiles are a single block, so the next tile's QK^T then
+        // overlaps this softmax); its buffer's previous reader, QK^T of tile
+        // lt - 1, completed before this S arrived.
+        if (SMALL && j == 0 && tile_exists(lt + 1) && !(ok = stage_bias(lt + 1, tok_next))) break;
         const uint32_t tS = t_lane + sbuf * kAttnBN + 64 * h;
         // this half's 64 keys: 64-key mask block 2 kb + h
         const int mh = 2 * kb + h;
@@ -835,7 +841,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1) sparse_attn_kernel(const Attn
 
         if (j == 0) {
           // next tile's bias operand and the previous tile's epilogue, off the critical path
-          if (tile_exists(lt + 1) && !(ok = stage_bias(lt + 1, tok_next))) break;
+          if (!SMALL && tile_exists(lt + 1) && !(ok = stage_bias(lt + 1, tok_next))) break;
           if (pend_lt >= 0 && !(ok = epilogue(pend_lt, pend_g, pend_tok, pend_l))) break;
           pend_lt = -1;
         }
