@@ -866,113 +866,134 @@ __global__ void __launch_bounds__(kAttnThreads, 1) sparse_attn_kernel(const Attn
 }
 
 // ---------------------------------------------------------------------------
-// relbias_kernel (global grids): for one 128-query tile of one (image, head)
-// row, P_H = Q Th^T and P_W = Q Tw^T on the tensor cores, then each thread
-// extracts its query's band relH[j] = P_H[qh - j + win - 1] (and relW) and
-// writes [relH / scale | relW / scale] (fp16, 64 + 64 columns, zero padding) to
-// bias_ws[row][p] in permuted query order — the operand the attention kernel
-// streams in with the query tile (sam.py:62-73, computed once per query).
+// relbias_kernel: the rel-pos bias operand of every query, once per query.
+// Persistent; per 128-query tile of an (image|window, head) row: P_H = Q Th^T
+// and P_W = Q Tw^T on the tensor cores (NT table rows), then each thread
+// extracts its query's bands relH[j] = P_H[qh - j + win - 1], relW[j] likewise
+// (sam.py:62-73) and writes [relH / scale | relW / scale] (fp16, BW + BW
+// columns, zero padding, zeros for queries past N) as one plain row of
+// bias_ws[tile][query] in permuted query order.
+// Used for the global grid (BW = 64, NT = 128, 2 win - 1 <= 127); the
+// template also covers 16-column bands (NT = 32), but windowed grids compute
+// their bands inside the attention kernel, which measured faster than a
+// separate pass for 14x14 windows.
 // ---------------------------------------------------------------------------
 constexpr int kRelThreads = 128;
 
-template <int D>
+template <int D, int BW>
+struct RelCfg {
+  static constexpr int kNT = BW == 16 ? 32 : 128;
+  static constexpr int kRowBytes = 4 * BW;           // [BW fp16 | BW fp16]
+  static constexpr int kStageStride = 4 * BW + 4;    // per-thread scratch row, odd word stride
+  static constexpr int kTmemCols = BW == 16 ? 64 : 256;
+  static constexpr int kSmem = 2 * TileGeom<D>::bytes(kNT) + TileGeom<D>::bytes(kAttnBM) +
+                               kAttnBM * kStageStride + 64 + 1024;
+};
+
+template <int D, int BW>
 __global__ void __launch_bounds__(kRelThreads) relbias_kernel(const AttnParams a) {
   using TG = TileGeom<D>;
-  constexpr int kNT = 128;
+  using RC = RelCfg<D, BW>;
+  constexpr int kNT = RC::kNT;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const uint32_t sb = smem_u32(smem);
   const uint32_t sTh = sb, sTw = sb + TG::bytes(kNT), sQ = sb + 2 * TG::bytes(kNT);
-  uint8_t* stage = smem + 3 * TG::bytes(kNT);  // [2][128 rows][128 B] swizzled bias rows
-  uint64_t* bar = reinterpret_cast<uint64_t*>(stage + 2 * kAttnBM * 128);
+  uint8_t* stage = smem + 2 * TG::bytes(kNT) + TG::bytes(kAttnBM);  // per-thread scratch rows
+  uint64_t* bar = reinterpret_cast<uint64_t*>(stage + kAttnBM * RC::kStageStride);
   uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(bar + 1);
 
   const int tid = threadIdx.x, warp = tid >> 5;
-  const int tile = blockIdx.x;
-  const int row = tile / a.n_tiles, qtile = tile - row * a.n_tiles;
-  const int seq = row / a.heads, head = row - seq * a.heads;
   const int N = a.N, win = a.win;
-  const int p = qtile * kAttnBM + tid;
-  const int t = p < N ? __ldg(a.perm + static_cast<int64_t>(row) * N + p) : -1;
 
   if (tid == 0) {
     mbar_init(bar, 1);
     fence_mbar_init();
   }
   if (warp == 0) {
-    tmem_alloc(tmem_holder, 256);
+    tmem_alloc(tmem_holder, RC::kTmemCols);
     tmem_relinquish();
   }
-  // tables (row tid) and this thread's query row
+  // tables, once per CTA (rows past 2 win - 1 zero)
   const int trows = 2 * win - 1;
-  const __nv_bfloat16* q_src =
-      t >= 0 ? a.qkv + (static_cast<int64_t>(seq) * N + t) * a.ld_qkv + head * D : nullptr;
+  if (tid < kNT) {
 #pragma unroll
-  for (int c = 0; c < TG::kChunks; ++c) {
-    cp_async16(tile_chunk_addr<D>(sTh, kNT, tid, c), tid < trows ? a.th + tid * D + c * 8 : a.th,
-               tid < trows ? 16u : 0u);
-    cp_async16(tile_chunk_addr<D>(sTw, kNT, tid, c), tid < trows ? a.tw + tid * D + c * 8 : a.tw,
-               tid < trows ? 16u : 0u);
-    cp_async16(tile_chunk_addr<D>(sQ, kAttnBM, tid, c), q_src != nullptr ? q_src + c * 8 : a.qkv,
-               q_src != nullptr ? 16u : 0u);
+    for (int c = 0; c < TG::kChunks; ++c) {
+      cp_async16(tile_chunk_addr<D>(sTh, kNT, tid, c), tid < trows ? a.th + tid * D + c * 8 : a.th,
+                 tid < trows ? 16u : 0u);
+      cp_async16(tile_chunk_addr<D>(sTw, kNT, tid, c), tid < trows ? a.tw + tid * D + c * 8 : a.tw,
+                 tid < trows ? 16u : 0u);
+    }
   }
-  cp_async_wait_all();
-  fence_proxy_async_smem();
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_holder;
-  if (tid == 0) {
-    const uint32_t idesc = make_idesc_bf16(kAttnBM, kNT, 0, 0);
+  const uint32_t t_lane = tmem + (static_cast<uint32_t>(warp * 32) << 16);
+  uint8_t* my_stage = stage + tid * RC::kStageStride;
+  bool ok = true;
+  int iter = 0;
+  for (int tile = blockIdx.x; ok && tile < a.total_tiles; tile += gridDim.x, ++iter) {
+    const int row = tile / a.n_tiles, qtile = tile - row * a.n_tiles;
+    const int seq = row / a.heads, head = row - seq * a.heads;
+    const int p = qtile * kAttnBM + tid;
+    const int t = p < N ? __ldg(a.perm + static_cast<int64_t>(row) * N + p) : -1;
+    const __nv_bfloat16* q_src =
+        t >= 0 ? a.qkv + (static_cast<int64_t>(seq) * N + t) * a.ld_qkv + head * D : nullptr;
 #pragma unroll
-    for (int ks = 0; ks < D / 16; ++ks) {
-      umma_f16_ss(tmem, kmajor_desc<D>(sQ, kAttnBM, ks), kmajor_desc<D>(sTh, kNT, ks), idesc, ks > 0);
-      umma_f16_ss(tmem + kNT, kmajor_desc<D>(sQ, kAttnBM, ks), kmajor_desc<D>(sTw, kNT, ks), idesc, ks > 0);
+    for (int c = 0; c < TG::kChunks; ++c)
+      cp_async16(tile_chunk_addr<D>(sQ, kAttnBM, tid, c), q_src != nullptr ? q_src + c * 8 : a.qkv,
+                 q_src != nullptr ? 16u : 0u);
+    cp_async_wait_all();
+    fence_proxy_async_smem();
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    if (tid == 0) {
+      const uint32_t idesc = make_idesc_bf16(kAttnBM, kNT, 0, 0);
+#pragma unroll
+      for (int ks = 0; ks < D / 16; ++ks) {
+        umma_f16_ss(tmem, kmajor_desc<D>(sQ, kAttnBM, ks), kmajor_desc<D>(sTh, kNT, ks), idesc, ks > 0);
+        umma_f16_ss(tmem + kNT, kmajor_desc<D>(sQ, kAttnBM, ks), kmajor_desc<D>(sTw, kNT, ks), idesc, ks > 0);
+      }
+      umma_commit(bar);
     }
-    umma_commit(bar);
-  }
-  const bool ok = __syncthreads_and(mbar_wait(bar, 0));
-  tc_fence_after();
-  if (ok) {
-    const int qh = t >= 0 ? t / win : 0;
-    const int qw = t >= 0 ? t - qh * win : 0;
-    uint8_t* st_h = stage;
-    uint8_t* st_w = stage + kAttnBM * 128;
-    const uint32_t t_lane = tmem + (static_cast<uint32_t>(warp * 32) << 16);
-    for (int c0 = 0; c0 < kNT; c0 += 32) {
-      uint32_t rh[32], rw[32];
-      tmem_ld_32x32b_x32(t_lane + c0, rh);
-      tmem_ld_32x32b_x32(t_lane + kNT + c0, rw);
-      tmem_ld_wait();
+    ok = __syncthreads_and(mbar_wait(bar, iter & 1));
+    tc_fence_after();
+    if (ok) {
+      const int qh = t >= 0 ? t / win : 0;
+      const int qw = t >= 0 ? t - qh * win : 0;
 #pragma unroll
-      for (int j = 0; j < 32; ++j) {
-        const int jh = qh + win - 1 - (c0 + j);
-        if (jh >= 0 && jh < win)
-          *reinterpret_cast<__half*>(st_h + bias_off<false>(tid, jh)) =
-              __float2half_rn(__uint_as_float(rh[j]) * a.inv_scale);
-        const int jw = qw + win - 1 - (c0 + j);
-        if (jw >= 0 && jw < win)
-          *reinterpret_cast<__half*>(st_w + bias_off<false>(tid, jw)) =
-              __float2half_rn(__uint_as_float(rw[j]) * a.inv_scale);
+      for (int j = 0; j < 2 * BW; j += 2) *reinterpret_cast<uint32_t*>(my_stage + j * 2) = 0u;  // zero padding
+      for (int c0 = 0; c0 < kNT; c0 += 32) {
+        uint32_t rh[32], rw[32];
+        tmem_ld_32x32b_x32(t_lane + c0, rh);
+        tmem_ld_32x32b_x32(t_lane + kNT + c0, rw);
+        tmem_ld_wait();
+#pragma unroll
+        for (int j = 0; j < 32; ++j) {
+          const int jh = qh + win - 1 - (c0 + j);
+          if (jh >= 0 && jh < win)
+            *reinterpret_cast<__half*>(my_stage + jh * 2) = __float2half_rn(__uint_as_float(rh[j]) * a.inv_scale);
+          const int jw = qw + win - 1 - (c0 + j);
+          if (jw >= 0 && jw < win)
+            *reinterpret_cast<__half*>(my_stage + 2 * BW + jw * 2) =
+                __float2half_rn(__uint_as_float(rw[j]) * a.inv_scale);
+        }
+      }
+      uint4* dst = reinterpret_cast<uint4*>(reinterpret_cast<uint8_t*>(a.bias_ws) +
+                                            (static_cast<int64_t>(tile) * kAttnBM + tid) * RC::kRowBytes);
+#pragma unroll
+      for (int i = 0; i < RC::kRowBytes / 16; ++i) {
+        const uint32_t* w = reinterpret_cast<const uint32_t*>(my_stage + 16 * i);
+        dst[i] = t >= 0 ? make_uint4(w[0], w[1], w[2], w[3]) : make_uint4(0u, 0u, 0u, 0u);
       }
     }
-    for (int j = win; j < 64; ++j) {
-      *reinterpret_cast<__half*>(st_h + bias_off<false>(tid, j)) = __float2half_rn(0.f);
-      *reinterpret_cast<__half*>(st_w + bias_off<false>(tid, j)) = __float2half_rn(0.f);
-    }
-    // this thread's row: unswizzle and store 256 B (zeros for queries past N)
-    uint4* dst = reinterpret_cast<uint4*>(a.bias_ws + (static_cast<int64_t>(row) * a.n_tiles + qtile) * kAttnBM * 128 +
-                                          static_cast<int64_t>(tid) * 128);
-#pragma unroll
-    for (int c = 0; c < 16; ++c) {
-      const uint8_t* src = stage + (c >> 3) * (kAttnBM * 128) + tid * 128 + (((c & 7) ^ (tid & 7)) << 4);
-      dst[c] = t >= 0 ? *reinterpret_cast<const uint4*>(src) : make_uint4(0u, 0u, 0u, 0u);
-    }
+    tc_fence_before();
+    __syncthreads();  // Q and TMEM reused by the next tile
+    tc_fence_after();
   }
-  tc_fence_before();
-  __syncthreads();
-  tc_fence_after();
-  if (warp == 0) tmem_dealloc(tmem, 256);
+  if (warp == 0) tmem_dealloc(tmem, RC::kTmemCols);
 }
 
 size_t sparse_attn_workspace_size(int n_seq, int heads, int win) {
@@ -984,29 +1005,29 @@ size_t sparse_attn_workspace_size(int n_seq, int heads, int win) {
 template <int D, bool SMALL>
 static int launch_attn(const AttnParams& p, cudaStream_t stream) {
   const AttnLayout<D, SMALL> L;
+  using RC = RelCfg<D, 64>;
   static bool configured[64] = {false};
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return SSAM_ERR_CUDA;
-  constexpr int kRelSmem = 3 * TileGeom<D>::bytes(128) + 2 * kAttnBM * 128 + 64 + 1024;
   if (!configured[dev]) {
     if (cudaFuncSetAttribute(sparse_attn_kernel<D, SMALL>, cudaFuncAttributeMaxDynamicSharedMemorySize, L.total) !=
         cudaSuccess)
       return SSAM_ERR_CUDA;
-    if (!SMALL && cudaFuncSetAttribute(relbias_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize, kRelSmem) !=
-                      cudaSuccess)
+    if (!SMALL && cudaFuncSetAttribute(relbias_kernel<D, 64>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       RC::kSmem) != cudaSuccess)
       return SSAM_ERR_CUDA;
     configured[dev] = true;
   }
+  const int sms = num_sms(dev);
   if (!SMALL) {
-    // two CTAs per SM at most: 2 x 256 TMEM columns
-    const int rel_smem = kRelSmem > 80 * 1024 ? kRelSmem : 80 * 1024;
-    relbias_kernel<D><<<p.total_tiles, kRelThreads, rel_smem, stream>>>(p);
+    // persistent bias pre-pass, two CTAs per SM (256 TMEM columns each)
+    const int want = sms * (512 / RC::kTmemCols);
+    relbias_kernel<D, 64><<<p.total_tiles < want ? p.total_tiles : want, kRelThreads, RC::kSmem, stream>>>(p);
     if (cudaGetLastError() != cudaSuccess) return SSAM_ERR_CUDA;
   }
   // One persistent CTA per SM (the plan exceeds half the SM's shared memory),
   // so its 512 TMEM columns are always available.
   const int smem = L.total > 116 * 1024 ? L.total : 116 * 1024;
-  const int sms = num_sms(dev);
   const int grid = p.total_tiles < sms ? p.total_tiles : sms;
   sparse_attn_kernel<D, SMALL><<<grid, kAttnThreads, smem, stream>>>(p);
   return status_from_cuda(cudaGetLastError());
