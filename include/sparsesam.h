@@ -102,6 +102,10 @@ int ssam_a_shape_mask(int N, int m_block, int n_block, int n_init, int with_diag
  *   perm  : int32 [n_seq*heads, win*win] permutation of every row.
  *   out   : bf16 [n_seq*win*win, heads*d] in raster token order, leading dim ld_out.
  *   n_init_blocks / with_diag : A-shape mask over 64-token blocks.
+ *   out_rows  : optional int32 [n_seq*N]: the output row of (sequence s,
+ *               token t) is out_rows[s*N + t] (< 0: not stored); NULL stores it
+ *               at row s*N + t. Windowed blocks pass the ssam_window_rows map,
+ *               which fuses window_unpartition (sam.py:256) into the store.
  *   workspace : ssam_sparse_attn_workspace_size() bytes (0 for windowed grids,
  *               win <= 16; global grids keep the per-query bias there).
  * d must be 64 or 80.
@@ -110,7 +114,7 @@ size_t ssam_sparse_attn_workspace_size(int n_seq, int heads, int win, int d);
 int ssam_sparse_attn_fwd(const void* qkv, int64_t ld_qkv, int n_seq, int heads, int win, int d,
                          const void* rel_pos_h, const void* rel_pos_w, const int32_t* perm,
                          int n_init_blocks, int with_diag, float scale, void* out, int64_t ld_out,
-                         void* workspace, size_t workspace_bytes, void* stream);
+                         const int32_t* out_rows, void* workspace, size_t workspace_bytes, void* stream);
 
 /* ---------------------------------------------------------------------------
  * a10 (selection). Keep set of the Residual-Consistency MLP.
@@ -136,6 +140,17 @@ int ssam_layernorm_gather(const float* x, int64_t ldx, const int32_t* src_rows, 
  * rows[(b*nwh*nww + wy*nww + wx)*ws*ws + ty*ws + tx] = b*H*W + y*W + x, or -1 in
  * the zero padding. The same map unpartitions (proj epilogue skips -1 rows). */
 int ssam_window_rows(int B, int H, int W, int ws, int32_t* rows, void* stream);
+
+/* Inverse of ssam_window_rows: win_rows[b*H*W + y*W + x] = the token's row in
+ * the window layout. Lets the windowed blocks run LN1 and the qkv GEMM on the
+ * B*H*W real tokens only, scattering qkv rows into the window layout. */
+int ssam_window_of_raster(int B, int H, int W, int ws, int32_t* win_rows, void* stream);
+
+/* out[i][0..C) = bf16(bias) for every window-layout row i with rows[i] < 0 (the
+ * padding of window_partition, sam.py:252: zero tokens after norm1, whose qkv
+ * is the Linear's bias). rows is the ssam_window_rows map. */
+int ssam_fill_pad_rows(void* out, int64_t ld, const int32_t* rows, int n_rows, int C, const float* bias,
+                       void* stream);
 
 /* ---------------------------------------------------------------------------
  * GEMM on the 5th-generation tensor cores (tcgen05 + TMEM, TMA-fed):

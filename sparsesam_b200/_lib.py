@@ -30,7 +30,7 @@ SIGNATURES: dict[str, tuple] = {
     "ssam_a_shape_mask": (c_int, [c_int, c_int, c_int, c_int, c_int, c_ptr]),
     "ssam_sparse_attn_workspace_size": (c_size, [c_int, c_int, c_int, c_int]),
     "ssam_sparse_attn_fwd": (c_int, [c_ptr, c_i64, c_int, c_int, c_int, c_int, c_ptr, c_ptr, c_ptr,
-                                     c_int, c_int, c_f32, c_ptr, c_i64, c_ptr, c_size, c_ptr]),
+                                     c_int, c_int, c_f32, c_ptr, c_i64, c_ptr, c_ptr, c_size, c_ptr]),
     "ssam_keep_select": (c_int, [c_ptr, c_int, c_int, c_int, c_int, c_ptr, c_ptr, c_ptr]),
     "ssam_layernorm_gather": (c_int, [c_ptr, c_i64, c_ptr, c_int, c_int, c_ptr, c_ptr, c_f32, c_ptr, c_i64,
                                       c_ptr]),
@@ -47,6 +47,8 @@ SIGNATURES: dict[str, tuple] = {
     "ssam_layernorm_rows": (c_int, [c_ptr, c_int, c_int, c_ptr, c_ptr, c_f32, c_ptr, c_int, c_ptr]),
     "ssam_split_bf16x2": (c_int, [c_ptr, c_int, c_int, c_ptr, c_ptr]),
     "ssam_split_bf16x3": (c_int, [c_ptr, c_int, c_int, c_ptr, c_ptr]),
+    "ssam_window_of_raster": (c_int, [c_int, c_int, c_int, c_int, c_ptr, c_ptr]),
+    "ssam_fill_pad_rows": (c_int, [c_ptr, c_i64, c_ptr, c_int, c_int, c_ptr, c_ptr]),
     "ssam_patch_im2col_split3": (c_int, [c_ptr, c_int, c_int, c_int, c_int, c_int, c_ptr, c_ptr]),
     "ssam_rc_mlp_fwd_noalloc": (c_int, [c_ptr, c_i64, c_ptr, c_int, c_int, c_int, c_ptr, c_ptr, c_f32, c_ptr, c_ptr,
                                         c_ptr, c_ptr, c_ptr]),
@@ -73,7 +75,7 @@ KERNELS_PER_CALL = {
     "ssam_layernorm_gather": 1, "ssam_window_rows": 1, "ssam_gemm_bf16": 1, "ssam_rc_mlp_fwd": 3,
     "ssam_patch_im2col": 1, "ssam_broadcast_rows": 1, "ssam_im2col3x3_nhwc": 1, "ssam_nhwc_to_nchw": 1,
     "ssam_layernorm_rows": 1, "ssam_split_bf16x2": 1, "ssam_rc_mlp_fwd_noalloc": 3,
-    "ssam_split_bf16x3": 1, "ssam_patch_im2col_split3": 1,
+    "ssam_split_bf16x3": 1, "ssam_patch_im2col_split3": 1, "ssam_window_of_raster": 1, "ssam_fill_pad_rows": 1,
 }
 launch_count = 0  # kernels enqueued through call() since import (read by bench.py)
 

@@ -196,6 +196,7 @@ struct AttnParams {
   float inv_scale;   // 1 / scale
   __nv_bfloat16* out;
   int64_t ld_out;
+  const int32_t* out_rows;  // optional output row of (sequence, token)
   int n_tiles;  // 128-query tiles per row
   int total_tiles;
   __half* bias_ws;  // LARGE: [rows][n_tiles*128][128] fp16 = relH/scale | relW/scale
@@ -692,9 +693,9 @@ __global__ void __launch_bounds__(kAttnThreads, 1) sparse_attn_kernel(const Attn
       if (g_last >= 0 && !wait_or_abort(kBarODone + (g_last & 1), (g_last >> 1) & 1)) return false;
       tc_fence_after();
       const float inv_l = l > 0.f ? 1.f / l : 0.f;
-      uint4* dst = tok >= 0 ? reinterpret_cast<uint4*>(a.out + (static_cast<int64_t>(seq) * N + tok) * a.ld_out +
-                                                       head * D)
-                            : nullptr;
+      int64_t orow = tok >= 0 ? static_cast<int64_t>(seq) * N + tok : -1;
+      if (orow >= 0 && a.out_rows != nullptr) orow = __ldg(a.out_rows + orow);
+      uint4* dst = orow >= 0 ? reinterpret_cast<uint4*>(a.out + orow * a.ld_out + head * D) : nullptr;
       const uint32_t tO = t_lane + C::kTmO + (lt_ % C::kO) * D;
 #pragma unroll
       for (int c0 = 0; c0 < D; c0 += 16) {
@@ -1035,7 +1036,8 @@ static int launch_attn(const AttnParams& p, cudaStream_t stream) {
 
 int sparse_attn_fwd(const void* qkv, int64_t ld_qkv, int n_seq, int heads, int win, int d, const void* rel_pos_h,
                     const void* rel_pos_w, const int32_t* perm, int n_init_blocks, int with_diag, float scale,
-                    void* out, int64_t ld_out, void* workspace, size_t workspace_bytes, cudaStream_t stream) {
+                    void* out, int64_t ld_out, const int32_t* out_rows, void* workspace, size_t workspace_bytes,
+                    cudaStream_t stream) {
   if (qkv == nullptr || rel_pos_h == nullptr || rel_pos_w == nullptr || perm == nullptr || out == nullptr)
     return SSAM_ERR_INVALID;
   if (n_seq <= 0 || heads <= 0 || win <= 0 || n_init_blocks < 0) return SSAM_ERR_INVALID;
@@ -1063,6 +1065,7 @@ int sparse_attn_fwd(const void* qkv, int64_t ld_qkv, int n_seq, int heads, int w
   p.scale_log2 = scale * 1.4426950408889634f;
   p.out = static_cast<__nv_bfloat16*>(out);
   p.ld_out = ld_out;
+  p.out_rows = out_rows;
   p.inv_scale = 1.0f / scale;
   p.n_tiles = (p.N + kAttnBM - 1) / kAttnBM;
   const int64_t total = static_cast<int64_t>(p.n_tiles) * n_seq * heads;

@@ -72,9 +72,11 @@ size_t ssam_sparse_attn_workspace_size(int n_seq, int heads, int win, int d) {
 
 int ssam_sparse_attn_fwd(const void* qkv, int64_t ld_qkv, int n_seq, int heads, int win, int d, const void* rel_pos_h,
                          const void* rel_pos_w, const int32_t* perm, int n_init_blocks, int with_diag, float scale,
-                         void* out, int64_t ld_out, void* workspace, size_t workspace_bytes, void* stream) {
+                         void* out, int64_t ld_out, const int32_t* out_rows, void* workspace, size_t workspace_bytes,
+                         void* stream) {
   return ssam::sparse_attn_fwd(qkv, ld_qkv, n_seq, heads, win, d, rel_pos_h, rel_pos_w, perm, n_init_blocks, with_diag,
-                               scale, out, ld_out, workspace, workspace_bytes, static_cast<cudaStream_t>(stream));
+                               scale, out, ld_out, out_rows, workspace, workspace_bytes,
+                               static_cast<cudaStream_t>(stream));
 }
 
 int ssam_keep_select(const int32_t* inv_perm_group, int B, int heads, int N, int keep_n, int32_t* idx, int32_t* rows,
@@ -125,6 +127,15 @@ int ssam_layernorm_rows(const float* x, int n_rows, int C, const float* w, const
 
 int ssam_split_bf16x2(const float* x, int n_rows, int C, void* out, void* stream) {
   return ssam::split_bf16x2(x, n_rows, C, out, static_cast<cudaStream_t>(stream));
+}
+
+int ssam_window_of_raster(int B, int H, int W, int ws, int32_t* win_rows, void* stream) {
+  return ssam::window_of_raster(B, H, W, ws, win_rows, static_cast<cudaStream_t>(stream));
+}
+
+int ssam_fill_pad_rows(void* out, int64_t ld, const int32_t* rows, int n_rows, int C, const float* bias,
+                       void* stream) {
+  return ssam::fill_pad_rows(out, ld, rows, n_rows, C, bias, static_cast<cudaStream_t>(stream));
 }
 
 int ssam_split_bf16x3(const float* x, int n_rows, int C, void* out, void* stream) {

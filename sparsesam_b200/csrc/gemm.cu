@@ -60,7 +60,9 @@ __device__ __forceinline__ void gemm_epilogue_chunk(const GemmParams& p, int row
 #pragma unroll
       for (int i = 0; i < 32; ++i) v[i] = gelu_exact(v[i]);
     }
-    uint4* dst = reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(p.out) + static_cast<int64_t>(row) * p.ldo + col0);
+    const int orow = p.out_rows != nullptr ? __ldg(p.out_rows + row) : row;
+    if (orow < 0) return;
+    uint4* dst = reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(p.out) + static_cast<int64_t>(orow) * p.ldo + col0);
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
       uint4 q;
@@ -71,7 +73,9 @@ __device__ __forceinline__ void gemm_epilogue_chunk(const GemmParams& p, int row
       dst[i] = q;
     }
   } else if constexpr (EPI == SSAM_EPI_F32) {
-    float4* dst = reinterpret_cast<float4*>(static_cast<float*>(p.out) + static_cast<int64_t>(row) * p.ldo + col0);
+    const int orow = p.out_rows != nullptr ? __ldg(p.out_rows + row) : row;
+    if (orow < 0) return;
+    float4* dst = reinterpret_cast<float4*>(static_cast<float*>(p.out) + static_cast<int64_t>(orow) * p.ldo + col0);
 #pragma unroll
     for (int i = 0; i < 8; ++i) dst[i] = make_float4(v[4 * i + 0], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
   } else {

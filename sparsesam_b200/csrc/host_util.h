@@ -37,7 +37,8 @@ int a_shape_mask(int N, int m_block, int n_block, int n_init, int with_diag, uin
 size_t sparse_attn_workspace_size(int n_seq, int heads, int win);
 int sparse_attn_fwd(const void* qkv, int64_t ld_qkv, int n_seq, int heads, int win, int d, const void* rel_pos_h,
                     const void* rel_pos_w, const int32_t* perm, int n_init_blocks, int with_diag, float scale,
-                    void* out, int64_t ld_out, void* workspace, size_t workspace_bytes, cudaStream_t stream);
+                    void* out, int64_t ld_out, const int32_t* out_rows, void* workspace, size_t workspace_bytes,
+                    cudaStream_t stream);
 int layernorm_gather(const float* x, int64_t ldx, const int32_t* src_rows, int n_rows, int C, const float* w,
                      const float* b, float eps, void* out, int64_t ld_out, cudaStream_t stream);
 int layernorm_rows(const float* x, int n_rows, int C, const float* w, const float* b, float eps, void* out,
@@ -49,6 +50,9 @@ int im2col3x3_nhwc(const void* in, int B, int H, int W, int C, void* out, cudaSt
 int nhwc_to_nchw(const float* in, int B, int HW, int C, float* out, cudaStream_t stream);
 int split_bf16x2(const float* x, int n_rows, int C, void* out, cudaStream_t stream);
 int split_bf16x3(const float* x, int n_rows, int C, void* out, cudaStream_t stream);
+int window_of_raster(int B, int H, int W, int ws, int32_t* win_rows, cudaStream_t stream);
+int fill_pad_rows(void* out, int64_t ld, const int32_t* rows, int n_rows, int C, const float* bias,
+                  cudaStream_t stream);
 int patch_im2col_split3(const float* img, int B, int Cin, int H, int W, int p, void* out, cudaStream_t stream);
 size_t rc_mlp_workspace_size(int n_rows, int C, int hidden);
 int rc_mlp_fwd(float* x, int64_t ldx, const int32_t* rows, int n_rows, int C, int hidden, const float* ln_w,

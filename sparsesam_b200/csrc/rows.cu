@@ -160,6 +160,56 @@ int window_rows(int B, int H, int W, int ws, int32_t* rows, cudaStream_t stream)
   return status_from_cuda(cudaGetLastError());
 }
 
+// Inverse map: raster row (b, y, x) -> its row in the window layout.
+__global__ void window_of_raster_kernel(int B, int H, int W, int ws, int nwh, int nww, int32_t* win_rows) {
+  const int64_t total = static_cast<int64_t>(B) * H * W;
+  const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (i >= total) return;
+  const int x = static_cast<int>(i % W);
+  const int y = static_cast<int>((i / W) % H);
+  const int b = static_cast<int>(i / (static_cast<int64_t>(W) * H));
+  const int64_t win = (static_cast<int64_t>(b) * nwh + y / ws) * nww + x / ws;
+  win_rows[i] = static_cast<int32_t>(win * ws * ws + (y % ws) * ws + (x % ws));
+}
+
+int window_of_raster(int B, int H, int W, int ws, int32_t* win_rows, cudaStream_t stream) {
+  if (B <= 0 || H <= 0 || W <= 0 || ws <= 0 || win_rows == nullptr) return SSAM_ERR_INVALID;
+  const int nwh = (H + ws - 1) / ws, nww = (W + ws - 1) / ws;
+  if (static_cast<int64_t>(B) * nwh * nww * ws * ws > INT32_MAX) return SSAM_ERR_UNSUPPORTED;
+  const int64_t total = static_cast<int64_t>(B) * H * W;
+  window_of_raster_kernel<<<static_cast<unsigned>((total + 255) / 256), 256, 0, stream>>>(B, H, W, ws, nwh, nww,
+                                                                                         win_rows);
+  return status_from_cuda(cudaGetLastError());
+}
+
+// Rows of the window layout that lie in the padding (rows[i] < 0) are set to
+// bf16(bias): SAM pads the normalised tokens with zeros, so their qkv is the
+// Linear's bias. One warp per row, 16 bytes per lane.
+__global__ void fill_pad_rows_kernel(__nv_bfloat16* __restrict__ out, int64_t ld, const int32_t* __restrict__ rows,
+                                     int n_rows, int C, const float* __restrict__ bias) {
+  const int64_t wi = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (wi >= n_rows || __ldg(rows + wi) >= 0) return;
+  uint4* dst = reinterpret_cast<uint4*>(out + wi * ld);
+  for (int c = lane * 8; c < C; c += 32 * 8) {
+    const float4 b0 = __ldg(reinterpret_cast<const float4*>(bias + c));
+    const float4 b1 = __ldg(reinterpret_cast<const float4*>(bias + c + 4));
+    dst[c / 8] = make_uint4(pack_bf16x2(b0.x, b0.y), pack_bf16x2(b0.z, b0.w), pack_bf16x2(b1.x, b1.y),
+                            pack_bf16x2(b1.z, b1.w));
+  }
+}
+
+int fill_pad_rows(void* out, int64_t ld, const int32_t* rows, int n_rows, int C, const float* bias,
+                  cudaStream_t stream) {
+  if (out == nullptr || rows == nullptr || bias == nullptr || n_rows < 0 || C <= 0) return SSAM_ERR_INVALID;
+  if (n_rows == 0) return SSAM_OK;
+  if (C % 8 || ld % 8 || !aligned16(out) || !aligned16(bias)) return SSAM_ERR_ALIGN;
+  const int64_t threads = static_cast<int64_t>(n_rows) * 32;
+  fill_pad_rows_kernel<<<static_cast<unsigned>((threads + 255) / 256), 256, 0, stream>>>(
+      static_cast<__nv_bfloat16*>(out), ld, rows, n_rows, C, bias);
+  return status_from_cuda(cudaGetLastError());
+}
+
 // ---------------------------------------------------------------------------
 // Stem / neck helpers.
 // ---------------------------------------------------------------------------

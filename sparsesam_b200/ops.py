@@ -189,9 +189,10 @@ def keep_select(inv_perm_group: torch.Tensor, B: int, heads: int, keep_n: int):
 # ---------------------------------------------------------------------------
 def sparse_attn(qkv: torch.Tensor, n_seq: int, heads: int, win: int, d: int, rel_pos_h: torch.Tensor,
                 rel_pos_w: torch.Tensor, perm: torch.Tensor, n_init_blocks: int, with_diag: bool, scale: float,
-                out: torch.Tensor | None = None) -> torch.Tensor:
-    """Block-sparse attention of every (sequence, head) row; output in raster order (n_seq*N, heads*d)."""
-    _check_cuda(qkv, rel_pos_h, rel_pos_w, perm, out)
+                out: torch.Tensor | None = None, out_rows: torch.Tensor | None = None) -> torch.Tensor:
+    """Block-sparse attention of every (sequence, head) row; output in raster order (n_seq*N, heads*d),
+    or, with `out_rows` (int32 [n_seq*N], -1 skips), (sequence, token) written to row out_rows[s*N + t]."""
+    _check_cuda(qkv, rel_pos_h, rel_pos_w, perm, out, out_rows)
     if qkv.dtype != torch.bfloat16 or rel_pos_h.dtype != torch.bfloat16 or rel_pos_w.dtype != torch.bfloat16:
         raise TypeError("qkv and rel-pos tables must be bf16")
     if perm.dtype != torch.int32 or not perm.is_contiguous():
@@ -200,7 +201,12 @@ def sparse_attn(qkv: torch.Tensor, n_seq: int, heads: int, win: int, d: int, rel
         raise ValueError("rel-pos tables must be contiguous")
     ld = _rowmajor(qkv, "qkv")
     N = win * win
+    if out_rows is not None and (out_rows.dtype != torch.int32 or out_rows.numel() < n_seq * N
+                                 or not out_rows.is_contiguous()):
+        raise ValueError("out_rows must be contiguous int32 with n_seq*N entries")
     if out is None:
+        if out_rows is not None:
+            raise ValueError("out_rows needs an explicit `out`")
         out = torch.empty(n_seq * N, heads * d, dtype=torch.bfloat16, device=qkv.device)
     ld_out = _rowmajor(out, "out")
     ws_bytes = int(_lib.load().ssam_sparse_attn_workspace_size(n_seq, heads, win, d))
@@ -208,7 +214,7 @@ def sparse_attn(qkv: torch.Tensor, n_seq: int, heads: int, win: int, d: int, rel
     t0 = KernelTimer.begin()
     _lib.call("ssam_sparse_attn_fwd", qkv.data_ptr(), ld, n_seq, heads, win, d, rel_pos_h.data_ptr(),
               rel_pos_w.data_ptr(), perm.data_ptr(), n_init_blocks, 1 if with_diag else 0, float(scale),
-              out.data_ptr(), ld_out, _ptr(ws), ws_bytes, _stream(qkv), launches=2 if ws_bytes else 1)
+              out.data_ptr(), ld_out, _ptr(out_rows), _ptr(ws), ws_bytes, _stream(qkv), launches=2 if ws_bytes else 1)
     KernelTimer.end(t0, "attention_global" if ws_bytes else "attention_window",
                     attention_flops(n_seq * heads, N, d, n_init_blocks, with_diag))
     return out
@@ -357,6 +363,26 @@ def split_bf16x3(x: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tens
     if out is None:
         out = torch.empty(n, 3 * C, dtype=torch.bfloat16, device=x.device)
     _lib.call("ssam_split_bf16x3", x2.data_ptr(), n, C, out.data_ptr(), _stream(x))
+    return out
+
+
+def window_of_raster(B: int, H: int, W: int, ws: int, device) -> torch.Tensor:
+    """int32 [B*H*W]: each raster token's row in the window layout (inverse of window_rows)."""
+    out = torch.empty(B * H * W, dtype=torch.int32, device=device)
+    _lib.call("ssam_window_of_raster", B, H, W, ws, out.data_ptr(), torch.cuda.current_stream(out.device).cuda_stream)
+    return out
+
+
+def fill_pad_rows(out: torch.Tensor, rows: torch.Tensor, bias: torch.Tensor) -> torch.Tensor:
+    """out[i] = bf16(bias) for every window-layout row i with rows[i] < 0."""
+    _check_cuda(out, rows, bias)
+    if out.dtype != torch.bfloat16 or rows.dtype != torch.int32 or bias.dtype != torch.float32:
+        raise TypeError("fill_pad_rows takes bf16 out, int32 rows, fp32 bias")
+    n, C = out.shape
+    if rows.numel() < n or bias.numel() != C:
+        raise ValueError("rows / bias do not match out")
+    _lib.call("ssam_fill_pad_rows", out.data_ptr(), _rowmajor(out, "out"), rows.data_ptr(), n, C, bias.data_ptr(),
+              _stream(out))
     return out
 
 

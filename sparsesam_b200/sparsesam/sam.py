@@ -45,6 +45,7 @@ _LN_EPS = 1e-6
 # ---------------------------------------------------------------------------
 _ZORDER: dict = {}
 _WINDOW_ROWS: dict = {}
+_WINDOW_OF_RASTER: dict = {}
 
 
 def _base_order(H: int, W: int, space: str, device) -> torch.Tensor:
@@ -61,6 +62,13 @@ def _window_rows(B: int, H: int, W: int, ws: int, device) -> torch.Tensor:
     if key not in _WINDOW_ROWS:
         _WINDOW_ROWS[key] = ops.window_rows(B, H, W, ws, device)
     return _WINDOW_ROWS[key]
+
+
+def _window_of_raster(B: int, H: int, W: int, ws: int, device) -> torch.Tensor:
+    key = (B, H, W, ws, str(device))
+    if key not in _WINDOW_OF_RASTER:
+        _WINDOW_OF_RASTER[key] = ops.window_of_raster(B, H, W, ws, device)
+    return _WINDOW_OF_RASTER[key]
 
 
 @dataclass
@@ -144,20 +152,25 @@ def _get_perm(info: dict, key: tuple, qkv: torch.Tensor, n_seq: int, heads: int,
 
 
 def _attention_core(attn, xn: torch.Tensor, n_seq: int, win: int, ratio: float, is_global: bool,
-                    n_block: int):
-    """xn: bf16 (n_seq*win*win, C) -> (o bf16 (rows, C) raster order, perm, inv_perm)."""
+                    n_block: int, qkv: torch.Tensor | None = None, out: torch.Tensor | None = None,
+                    out_rows: torch.Tensor | None = None):
+    """xn: bf16 (n_seq*win*win, C) -> (o bf16 (rows, C) raster order, perm, inv_perm).
+
+    With `qkv` given (already projected, e.g. from the real tokens only), xn is
+    not used; `out` / `out_rows` place the attention rows (see ops.sparse_attn)."""
     w = _attn_weights(attn)
     heads = attn.num_heads
-    C = xn.shape[1]
+    C = w.proj_w.shape[1]
     d = C // heads
     N = win * win
-    qkv = ops.gemm_bf16(xn, w.qkv_w, w.qkv_b)                         # sam.py:182-184
+    if qkv is None:
+        qkv = ops.gemm_bf16(xn, w.qkv_w, w.qkv_b)                     # sam.py:182-184
     info = attn._tome_info
     perm_mode = info.get("perm_mode", "z_interleave_sort")
     perm, inv_perm, _ = _get_perm(info, (win, ratio, n_block, perm_mode), qkv, n_seq, heads, win, d)
     n_init = ops.a_shape_n_init(N, n_block, ratio, is_global)          # sam.py:219-223
     o = ops.sparse_attn(qkv, n_seq, heads, win, d, w.rel_h, w.rel_w, perm, n_init, is_global,
-                        attn.scale)                                     # sam.py:206-232
+                        attn.scale, out=out, out_rows=out_rows)         # sam.py:206-232
     return o, perm, inv_perm
 
 
@@ -221,13 +234,22 @@ class ToMeSAMBlock(Block):
         bw = _block_weights(self)
         aw = _attn_weights(self.attn)
         if self.window_size > 0:
+            # norm1 and the qkv projection on the B*H*W real tokens only; the GEMM
+            # epilogue scatters qkv rows into the window layout (window_partition,
+            # sam.py:252) and the padding rows get the qkv bias, the projection of
+            # SAM's zero padding. The attention store fuses window_unpartition
+            # (sam.py:256), so proj also runs on the real tokens only.
             ws = self.window_size
             rows = _window_rows(B, H, W, ws, xr.device)
             n_win = rows.numel() // (ws * ws)
-            xn = ops.layernorm_gather(xr, bw.ln1_w, bw.ln1_b, _LN_EPS, src_rows=rows)     # norm1 + partition
-            o, _, _ = _attention_core(self.attn, xn, n_win, ws, ratio, False, _FA2_N_BLOCK_LOCAL)
-            ops.gemm_bf16(o, aw.proj_w, aw.proj_b, epilogue=ops.SSAM_EPI_ADD_F32, out=xr,
-                          out_rows=rows)                                                   # unpartition + residual
+            xn = ops.layernorm_rows(xr, bw.ln1_w, bw.ln1_b, _LN_EPS, out_bf16=True)        # norm1
+            qkv = torch.empty(rows.numel(), 3 * C, dtype=torch.bfloat16, device=xr.device)
+            ops.gemm_bf16(xn, aw.qkv_w, aw.qkv_b, out=qkv, out_rows=_window_of_raster(B, H, W, ws, xr.device))
+            ops.fill_pad_rows(qkv, rows, aw.qkv_b)
+            o = torch.empty(B * H * W, C, dtype=torch.bfloat16, device=xr.device)
+            _attention_core(self.attn, None, n_win, ws, ratio, False, _FA2_N_BLOCK_LOCAL, qkv=qkv, out=o,
+                            out_rows=rows)
+            ops.gemm_bf16(o, aw.proj_w, aw.proj_b, epilogue=ops.SSAM_EPI_ADD_F32, out=xr)     # + residual
         else:
             if H != W:
                 raise ValueError("global SparseSAM attention expects a square grid")

@@ -79,3 +79,26 @@ def test_persistent_ctas_run_many_tiles(cuda_device, d, win, n_seq, heads, is_gl
     assert err.max().item() < 3e-2, err.max().item()
     assert err.mean().item() < 3e-3
     assert ops.device_error() == 0
+
+
+def test_out_rows_places_rows(cuda_device):
+    """out_rows stores (sequence, token) rows through a map (-1 drops the row), as
+    the windowed blocks use it for window_unpartition."""
+    n_seq, heads, win, d = 4, 2, 14, 64
+    N, C = win * win, heads * d
+    g = torch.Generator().manual_seed(5)
+    qkv = torch.randn(n_seq * N, 3 * C, generator=g).to(torch.bfloat16).to(cuda_device)
+    th = (torch.randn(2 * win - 1, d, generator=g) * 0.3).to(torch.bfloat16).to(cuda_device)
+    tw = (torch.randn(2 * win - 1, d, generator=g) * 0.3).to(torch.bfloat16).to(cuda_device)
+    perm = torch.stack([torch.randperm(N, generator=g) for _ in range(n_seq * heads)]).to(torch.int32)
+    perm = perm.to(cuda_device)
+    n_init = order.a_shape_n_init(N, 64, 0.4, False)
+    base = ops.sparse_attn(qkv, n_seq, heads, win, d, th, tw, perm, n_init, False, d ** -0.5)
+    dst = torch.randperm(2 * n_seq * N, generator=g)[: n_seq * N].to(torch.int32)
+    dst[::5] = -1
+    dst = dst.to(cuda_device)
+    out = torch.zeros(2 * n_seq * N, C, device=cuda_device, dtype=torch.bfloat16)
+    ops.sparse_attn(qkv, n_seq, heads, win, d, th, tw, perm, n_init, False, d ** -0.5, out=out, out_rows=dst)
+    keep = dst >= 0
+    assert torch.equal(out[dst[keep].long()], base[keep])
+    assert ops.device_error() == 0

@@ -119,3 +119,41 @@ def test_split3_gemm_matches_fp32_linear(cuda_device):
     out = ops.gemm_bf16(ops.split_bf16x3(x), ops.split_weight3(w), None, epilogue=ops.SSAM_EPI_F32)
     ref = (x.double() @ w.double().T).float()
     assert (out - ref).abs().max().item() < 1e-4
+
+
+def test_window_of_raster_inverts_window_rows(cuda_device):
+    B, H, W, ws = 2, 64, 64, 14
+    rows = ops.window_rows(B, H, W, ws, cuda_device).cpu()
+    inv = ops.window_of_raster(B, H, W, ws, cuda_device).cpu()
+    assert inv.numel() == B * H * W
+    real = (rows >= 0).nonzero().flatten()
+    assert torch.equal(inv[rows[real].long()], real.to(torch.int32))
+    assert torch.equal(torch.sort(inv.long()).values, real)
+
+
+def test_fill_pad_rows_writes_bias_only_on_padding(cuda_device):
+    B, H, W, ws, C = 1, 20, 20, 14, 96
+    rows = ops.window_rows(B, H, W, ws, cuda_device)
+    out = torch.randn(rows.numel(), C, device=cuda_device).to(torch.bfloat16)
+    before = out.clone()
+    bias = torch.randn(C, device=cuda_device)
+    ops.fill_pad_rows(out, rows, bias)
+    pad = rows < 0
+    assert torch.equal(out[~pad], before[~pad])
+    assert torch.equal(out[pad], bias.to(torch.bfloat16).expand(int(pad.sum()), C))
+
+
+def test_gemm_bf16_scatters_rows(cuda_device):
+    M, N, K = 300, 128, 64
+    a = torch.randn(M, K, device=cuda_device).to(torch.bfloat16)
+    b = torch.randn(N, K, device=cuda_device).to(torch.bfloat16)
+    dst = torch.randperm(2 * M, device=cuda_device)[:M].to(torch.int32)
+    dst[::7] = -1
+    out = torch.zeros(2 * M, N, device=cuda_device, dtype=torch.bfloat16)
+    ops.gemm_bf16(a, b, out=out, out_rows=dst)
+    ref = (a.float() @ b.float().T).to(torch.bfloat16)
+    keep = dst >= 0
+    assert torch.allclose(out[dst[keep].long()].float(), ref[keep].float(), atol=6e-2, rtol=2e-2)
+    written = torch.zeros(2 * M, dtype=torch.bool, device=cuda_device)
+    written[dst[keep].long()] = True
+    assert (out[~written] == 0).all()
