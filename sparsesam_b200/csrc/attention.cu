@@ -180,7 +180,7 @@ struct AttnLayout {
     tok = ab + kABStage;                          // int [2][128]
     xchg = tok + 2 * kAttnBM * 4;                 // float [2 rounds][2 halves][2 values][128]
     bars = (xchg + 2 * 2 * 2 * kAttnBM * 4 + 7) & ~7;  // mbarriers
-    total = bars + 40 * 8 + 16 + 1024;            // + alignment slack
+    total = bars + 64 * 8 + 16 + 1024;            // mbarriers, TMEM address, abort flag + alignment slack
   }
 };
 
@@ -271,6 +271,7 @@ enum {
   kBarDrain = 41,
   kNumBars = 42
 };
+static_assert(kNumBars * 8 + 8 <= 64 * 8, "mbarrier region of AttnLayout too small");
 
 template <int D, bool SMALL>
 __global__ void __launch_bounds__(kAttnThreads, 1) sparse_attn_kernel(const AttnParams a) {

@@ -87,6 +87,32 @@ __device__ double block_sum_d(double v, double* red) {
 
 constexpr int kStripeMaxChPerLane = 8;  // d <= 256
 
+// x[i][j] = K[token j of group g][channel lane + 32 i] (0 past d): the group's
+// tokens are read by GS lanes and shuffled, then all CH x GS values are loaded.
+template <int GS, int CH>
+__device__ __forceinline__ void stripe_group_values(const StripeArgs& a, const __nv_bfloat16* kr, int g, int lane,
+                                                    int d, float (&x)[CH][GS]) {
+  const int tk = lane < GS ? __ldg(a.base_perm + g * GS + lane) : 0;
+  int t[GS];
+#pragma unroll
+  for (int j = 0; j < GS; ++j) t[j] = __shfl_sync(0xffffffffu, tk, j);
+#pragma unroll
+  for (int i = 0; i < CH; ++i) {
+    const int c = lane + 32 * i;
+#pragma unroll
+    for (int j = 0; j < GS; ++j)
+      x[i][j] = c < d ? __bfloat162float(kr[static_cast<int64_t>(t[j]) * a.ld + c]) : 0.f;
+  }
+}
+
+// GS > 0: group size known at compile time (SparseSAM uses 4): the tokens of a
+// group are fetched once per warp and shuffled, the group's CH x GS values are
+// loaded together (one memory round trip per group instead of one per value)
+// and kept in registers for the variance. GS == 0: any group size (up to 32),
+// values re-read per channel. The per-channel mean / variance follow
+// np.std(ddof=1): sum in token order, mean = sum / gs, squared deviations
+// rounded before they are summed (no fused multiply-add).
+template <int GS, int CH>
 __global__ void stripe_sort_kernel(const StripeArgs a) {
   extern __shared__ double sm_d[];
   double* s_std = sm_d;               // [G]
@@ -100,7 +126,7 @@ __global__ void stripe_sort_kernel(const StripeArgs a) {
   const int seq = row / a.heads, head = row - seq * a.heads;
   const __nv_bfloat16* kr = a.k + static_cast<int64_t>(seq) * a.N * a.ld + static_cast<int64_t>(head) * a.d;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
-  const int G = a.G, gs = a.gs, d = a.d, N = a.N;
+  const int G = a.G, gs = GS > 0 ? GS : a.gs, d = a.d, N = a.N;
 
   int32_t* perm = a.perm + static_cast<int64_t>(row) * N;
   int32_t* inv_perm = a.inv_perm + static_cast<int64_t>(row) * N;
@@ -110,32 +136,57 @@ __global__ void stripe_sort_kernel(const StripeArgs a) {
     for (int c = threadIdx.x; c < d; c += blockDim.x) s_S[c] = 0.0;
     __syncthreads();
     // Pass 1: per-group std and norm, per-warp partial S.
-    double Sp[kStripeMaxChPerLane];
+    double Sp[CH];
 #pragma unroll
-    for (int i = 0; i < kStripeMaxChPerLane; ++i) Sp[i] = 0.0;
+    for (int i = 0; i < CH; ++i) Sp[i] = 0.0;
     for (int g = warp; g < G; g += nw) {
-      double mean[kStripeMaxChPerLane];
+      double mean[CH];
       double std_sum = 0.0, sq = 0.0;
+      if constexpr (GS > 0) {
+        float x[CH][GS];
+        stripe_group_values<GS, CH>(a, kr, g, lane, d, x);
 #pragma unroll
-      for (int i = 0; i < kStripeMaxChPerLane; ++i) {
-        const int c = lane + 32 * i;
-        mean[i] = 0.0;
-        if (c < d) {
-          double m = 0.0;
-          for (int j = 0; j < gs; ++j) {
-            const int t = __ldg(a.base_perm + g * gs + j);
-            m += static_cast<double>(__bfloat162float(kr[static_cast<int64_t>(t) * a.ld + c]));
+        for (int i = 0; i < CH; ++i) {
+          mean[i] = 0.0;
+          if (lane + 32 * i < d) {
+            double m = 0.0;
+#pragma unroll
+            for (int j = 0; j < GS; ++j) m = __dadd_rn(m, static_cast<double>(x[i][j]));
+            m = m / GS;
+            double v = 0.0;
+#pragma unroll
+            for (int j = 0; j < GS; ++j) {
+              const double dx = __dsub_rn(static_cast<double>(x[i][j]), m);
+              v = __dadd_rn(v, __dmul_rn(dx, dx));
+            }
+            std_sum += GS > 1 ? sqrt(v / (GS - 1)) : __longlong_as_double(0x7ff8000000000000ll);
+            mean[i] = m;
+            sq += m * m;
           }
-          m /= gs;
-          double v = 0.0;  // second pass re-reads the (L1-resident) group
-          for (int j = 0; j < gs; ++j) {
-            const int t = __ldg(a.base_perm + g * gs + j);
-            const double x = static_cast<double>(__bfloat162float(kr[static_cast<int64_t>(t) * a.ld + c]));
-            v += (x - m) * (x - m);
+        }
+      } else {
+#pragma unroll
+        for (int i = 0; i < CH; ++i) {
+          const int c = lane + 32 * i;
+          mean[i] = 0.0;
+          if (c < d) {
+            double m = 0.0;
+            for (int j = 0; j < gs; ++j) {
+              const int t = __ldg(a.base_perm + g * gs + j);
+              m = __dadd_rn(m, static_cast<double>(__bfloat162float(kr[static_cast<int64_t>(t) * a.ld + c])));
+            }
+            m /= gs;
+            double v = 0.0;  // second pass re-reads the (L1-resident) group
+            for (int j = 0; j < gs; ++j) {
+              const int t = __ldg(a.base_perm + g * gs + j);
+              const double dx =
+                  __dsub_rn(static_cast<double>(__bfloat162float(kr[static_cast<int64_t>(t) * a.ld + c])), m);
+              v = __dadd_rn(v, __dmul_rn(dx, dx));
+            }
+            std_sum += gs > 1 ? sqrt(v / (gs - 1)) : __longlong_as_double(0x7ff8000000000000ll);
+            mean[i] = m;
+            sq += m * m;
           }
-          std_sum += gs > 1 ? sqrt(v / (gs - 1)) : __longlong_as_double(0x7ff8000000000000ll);
-          mean[i] = m;
-          sq += m * m;
         }
       }
       std_sum = warp_sum_d(std_sum);
@@ -147,14 +198,14 @@ __global__ void stripe_sort_kernel(const StripeArgs a) {
         s_inv[g] = inv;
       }
 #pragma unroll
-      for (int i = 0; i < kStripeMaxChPerLane; ++i) Sp[i] += mean[i] * inv;
+      for (int i = 0; i < CH; ++i) Sp[i] += mean[i] * inv;
     }
     // Reduce S over warps in a fixed warp order.
     for (int w = 0; w < nw; ++w) {
       __syncthreads();
       if (warp == w) {
 #pragma unroll
-        for (int i = 0; i < kStripeMaxChPerLane; ++i) {
+        for (int i = 0; i < CH; ++i) {
           const int c = lane + 32 * i;
           if (c < d) s_S[c] += Sp[i];
         }
@@ -164,16 +215,31 @@ __global__ void stripe_sort_kernel(const StripeArgs a) {
     // Pass 2: <n_g, S> -> dissimilarity.
     for (int g = warp; g < G; g += nw) {
       double dot = 0.0;
+      if constexpr (GS > 0) {
+        float x[CH][GS];
+        stripe_group_values<GS, CH>(a, kr, g, lane, d, x);
 #pragma unroll
-      for (int i = 0; i < kStripeMaxChPerLane; ++i) {
-        const int c = lane + 32 * i;
-        if (c < d) {
-          double m = 0.0;
-          for (int j = 0; j < gs; ++j) {
-            const int t = __ldg(a.base_perm + g * gs + j);
-            m += static_cast<double>(__bfloat162float(kr[static_cast<int64_t>(t) * a.ld + c]));
+        for (int i = 0; i < CH; ++i) {
+          const int c = lane + 32 * i;
+          if (c < d) {
+            double m = 0.0;
+#pragma unroll
+            for (int j = 0; j < GS; ++j) m = __dadd_rn(m, static_cast<double>(x[i][j]));
+            dot += (m / GS) * s_S[c];
           }
-          dot += (m / gs) * s_S[c];
+        }
+      } else {
+#pragma unroll
+        for (int i = 0; i < CH; ++i) {
+          const int c = lane + 32 * i;
+          if (c < d) {
+            double m = 0.0;
+            for (int j = 0; j < gs; ++j) {
+              const int t = __ldg(a.base_perm + g * gs + j);
+              m = __dadd_rn(m, static_cast<double>(__bfloat162float(kr[static_cast<int64_t>(t) * a.ld + c])));
+            }
+            dot += (m / gs) * s_S[c];
+          }
         }
       }
       dot = warp_sum_d(dot);
@@ -235,6 +301,19 @@ __global__ void stripe_sort_kernel(const StripeArgs a) {
   }
 }
 
+template <int GS, int CH>
+static int launch_stripe(const StripeArgs& a, int rows, int threads, size_t smem, cudaStream_t stream) {
+  static bool configured = false;
+  if (!configured) {
+    if (cudaFuncSetAttribute(stripe_sort_kernel<GS, CH>, cudaFuncAttributeMaxDynamicSharedMemorySize, 160 * 1024) !=
+        cudaSuccess)
+      return SSAM_ERR_CUDA;
+    configured = true;
+  }
+  stripe_sort_kernel<GS, CH><<<rows, threads, smem, stream>>>(a);
+  return status_from_cuda(cudaGetLastError());
+}
+
 int stripe_sort_perm(const void* k, int64_t ld, int n_seq, int heads, int H, int W, int d, int gs, int layout,
                      int ranking, const int32_t* base_perm, int32_t* perm, int32_t* inv_perm, int32_t* inv_perm_group,
                      cudaStream_t stream) {
@@ -254,15 +333,14 @@ int stripe_sort_perm(const void* k, int64_t ld, int n_seq, int heads, int H, int
   int threads = 256;
   if (G <= 64) threads = 64;
   else if (G <= 256) threads = 128;
-  static bool configured = false;
-  if (!configured) {
-    if (cudaFuncSetAttribute(stripe_sort_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 160 * 1024) !=
-        cudaSuccess)
-      return SSAM_ERR_CUDA;
-    configured = true;
+  if (gs == 4) {
+    if (d <= 32) return launch_stripe<4, 1>(a, n_seq * heads, threads, smem, stream);
+    if (d <= 64) return launch_stripe<4, 2>(a, n_seq * heads, threads, smem, stream);
+    if (d <= 96) return launch_stripe<4, 3>(a, n_seq * heads, threads, smem, stream);
+    if (d <= 128) return launch_stripe<4, 4>(a, n_seq * heads, threads, smem, stream);
+    return launch_stripe<4, kStripeMaxChPerLane>(a, n_seq * heads, threads, smem, stream);
   }
-  stripe_sort_kernel<<<n_seq * heads, threads, smem, stream>>>(a);
-  return status_from_cuda(cudaGetLastError());
+  return launch_stripe<0, kStripeMaxChPerLane>(a, n_seq * heads, threads, smem, stream);
 }
 
 // ---------------------------------------------------------------------------
