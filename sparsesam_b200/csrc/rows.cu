@@ -270,9 +270,45 @@ __global__ void patch_im2col_split3_kernel(const float* __restrict__ img, int B,
   }
 }
 
+// Same output, one block per patch (grid px, py, b) and one thread per 8-pixel
+// run of a patch row: two float4 loads, three 16-byte stores (p % 8 == 0).
+__global__ void patch_im2col_split3_v8_kernel(const float* __restrict__ img, int Cin, int H, int W, int p,
+                                              __nv_bfloat16* __restrict__ out) {
+  const int px = blockIdx.x, py = blockIdx.y, b = blockIdx.z;
+  const int gw = W / p, gh = H / p;
+  const int runs = p / 8;
+  const int K = Cin * p * p;
+  const int64_t tok = (static_cast<int64_t>(b) * gh + py) * gw + px;
+  for (int u = threadIdx.x; u < Cin * p * runs; u += blockDim.x) {
+    const int run = u % runs, ky = (u / runs) % p, cin = u / (runs * p);
+    const float4* src = reinterpret_cast<const float4*>(
+        img + ((static_cast<int64_t>(b) * Cin + cin) * H + (py * p + ky)) * W + px * p + run * 8);
+    const float4 v0 = __ldg(src), v1 = __ldg(src + 1);
+    const float f[8] = {v0.x, v0.y, v0.z, v0.w, v1.x, v1.y, v1.z, v1.w};
+    float h[8];
+#pragma unroll
+    for (int e = 0; e < 8; ++e) h[e] = __bfloat162float(__float2bfloat16_rn(f[e]));
+    const uint4 hi = make_uint4(pack_bf16x2(h[0], h[1]), pack_bf16x2(h[2], h[3]), pack_bf16x2(h[4], h[5]),
+                                pack_bf16x2(h[6], h[7]));
+    const uint4 lo = make_uint4(pack_bf16x2(f[0] - h[0], f[1] - h[1]), pack_bf16x2(f[2] - h[2], f[3] - h[3]),
+                                pack_bf16x2(f[4] - h[4], f[5] - h[5]), pack_bf16x2(f[6] - h[6], f[7] - h[7]));
+    __nv_bfloat16* dst = out + tok * (3 * static_cast<int64_t>(K)) + (cin * p + ky) * p + run * 8;
+    *reinterpret_cast<uint4*>(dst) = hi;
+    *reinterpret_cast<uint4*>(dst + K) = lo;
+    *reinterpret_cast<uint4*>(dst + 2 * K) = hi;
+  }
+}
+
 int patch_im2col_split3(const float* img, int B, int Cin, int H, int W, int p, void* out, cudaStream_t stream) {
   if (img == nullptr || out == nullptr || B <= 0 || Cin <= 0 || p <= 0 || H % p || W % p) return SSAM_ERR_INVALID;
   if (p % 2 || (reinterpret_cast<uintptr_t>(img) & 7) || (reinterpret_cast<uintptr_t>(out) & 3)) return SSAM_ERR_ALIGN;
+  if (p % 8 == 0 && W % 4 == 0 && aligned16(img) && aligned16(out) && H / p <= 65535 && B <= 65535) {
+    const int work = Cin * p * (p / 8);
+    const int threads = work >= 128 ? 128 : ((work + 31) / 32) * 32;
+    patch_im2col_split3_v8_kernel<<<dim3(W / p, H / p, B), threads, 0, stream>>>(img, Cin, H, W, p,
+                                                                                 static_cast<__nv_bfloat16*>(out));
+    return status_from_cuda(cudaGetLastError());
+  }
   const int64_t total = static_cast<int64_t>(B) * (H / p) * (W / p) * Cin * p;
   patch_im2col_split3_kernel<<<static_cast<unsigned>((total + 255) / 256), 256, 0, stream>>>(
       img, B, Cin, H, W, p, static_cast<__nv_bfloat16*>(out));
@@ -294,31 +330,32 @@ int broadcast_rows(const float* pos, int B, int T, int C, float* x, cudaStream_t
   return status_from_cuda(cudaGetLastError());
 }
 
-// 3x3 / pad 1 im2col, channels-last, (ky, kx, c) column order; 8 channels per thread.
-__global__ void im2col3x3_kernel(const __nv_bfloat16* __restrict__ in, int B, int H, int W, int C,
+// 3x3 / pad 1 im2col, channels-last, (ky, kx, c) column order. One block per
+// output pixel (grid x, y, b: no index division), 8 channels per thread and tap.
+__global__ void im2col3x3_kernel(const __nv_bfloat16* __restrict__ in, int H, int W, int C,
                                  __nv_bfloat16* __restrict__ out) {
+  const int x = blockIdx.x, y = blockIdx.y, b = blockIdx.z;
   const int c8 = C / 8;
-  const int64_t total = static_cast<int64_t>(B) * H * W * 9 * c8;
-  const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
-  if (i >= total) return;
-  const int cc = static_cast<int>(i % c8);
-  const int tap = static_cast<int>((i / c8) % 9);
-  const int64_t pix = i / (static_cast<int64_t>(c8) * 9);
-  const int x = static_cast<int>(pix % W), y = static_cast<int>((pix / W) % H);
-  const int b = static_cast<int>(pix / (static_cast<int64_t>(W) * H));
-  const int yy = y + tap / 3 - 1, xx = x + tap % 3 - 1;
-  uint4 v = make_uint4(0u, 0u, 0u, 0u);
-  if (yy >= 0 && yy < H && xx >= 0 && xx < W)
-    v = __ldg(reinterpret_cast<const uint4*>(in + ((static_cast<int64_t>(b) * H + yy) * W + xx) * C) + cc);
-  reinterpret_cast<uint4*>(out + pix * (9 * static_cast<int64_t>(C)) + tap * C)[cc] = v;
+  const int64_t pix = (static_cast<int64_t>(b) * H + y) * W + x;
+  uint4* dst = reinterpret_cast<uint4*>(out + pix * (9 * static_cast<int64_t>(C)));
+#pragma unroll
+  for (int tap = 0; tap < 9; ++tap) {
+    const int yy = y + tap / 3 - 1, xx = x + tap % 3 - 1;
+    const bool inside = yy >= 0 && yy < H && xx >= 0 && xx < W;
+    const uint4* src =
+        inside ? reinterpret_cast<const uint4*>(in + ((static_cast<int64_t>(b) * H + yy) * W + xx) * C) : nullptr;
+    for (int cc = threadIdx.x; cc < c8; cc += blockDim.x)
+      dst[tap * c8 + cc] = inside ? __ldg(src + cc) : make_uint4(0u, 0u, 0u, 0u);
+  }
 }
 
 int im2col3x3_nhwc(const void* in, int B, int H, int W, int C, void* out, cudaStream_t stream) {
   if (in == nullptr || out == nullptr || B <= 0 || H <= 0 || W <= 0 || C <= 0) return SSAM_ERR_INVALID;
+  if (H > 65535 || B > 65535) return SSAM_ERR_UNSUPPORTED;
   if (C % 8 || !aligned16(in) || !aligned16(out)) return SSAM_ERR_ALIGN;
-  const int64_t total = static_cast<int64_t>(B) * H * W * 9 * (C / 8);
-  im2col3x3_kernel<<<static_cast<unsigned>((total + 255) / 256), 256, 0, stream>>>(
-      static_cast<const __nv_bfloat16*>(in), B, H, W, C, static_cast<__nv_bfloat16*>(out));
+  const int threads = C / 8 >= 128 ? 128 : ((C / 8 + 31) / 32) * 32;
+  im2col3x3_kernel<<<dim3(W, H, B), threads, 0, stream>>>(static_cast<const __nv_bfloat16*>(in), H, W, C,
+                                                           static_cast<__nv_bfloat16*>(out));
   return status_from_cuda(cudaGetLastError());
 }
 
@@ -378,28 +415,29 @@ int split_bf16x2(const float* x, int n_rows, int C, void* out, cudaStream_t stre
 // 3-term split of fp32 rows: out[r] = [hi | lo | hi] (3 C columns), hi = bf16(x),
 // lo = bf16(x - hi); against [W_hi | W_hi | W_lo] a GEMM carries both the fp32
 // activation and the fp32 weight up to the lo*lo term.
-__global__ void split_bf16x3_kernel(const float4* __restrict__ x, int64_t n4, int c4, uint2* __restrict__ out) {
-  const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
-  if (i >= n4) return;
-  const int64_t r = i / c4;
-  const int c = static_cast<int>(i - r * c4);
-  const float4 v = __ldg(x + i);
-  const float h0 = __bfloat162float(__float2bfloat16_rn(v.x)), h1 = __bfloat162float(__float2bfloat16_rn(v.y));
-  const float h2 = __bfloat162float(__float2bfloat16_rn(v.z)), h3 = __bfloat162float(__float2bfloat16_rn(v.w));
-  const uint2 hi = make_uint2(pack_bf16x2(h0, h1), pack_bf16x2(h2, h3));
+// One block per row (no index division).
+__global__ void split_bf16x3_kernel(const float4* __restrict__ x, int c4, uint2* __restrict__ out) {
+  const int64_t r = blockIdx.x;
   uint2* row = out + r * 3 * c4;
-  row[c] = hi;
-  row[c4 + c] = make_uint2(pack_bf16x2(v.x - h0, v.y - h1), pack_bf16x2(v.z - h2, v.w - h3));
-  row[2 * c4 + c] = hi;
+  for (int c = threadIdx.x; c < c4; c += blockDim.x) {
+    const float4 v = __ldg(x + r * c4 + c);
+    const float h0 = __bfloat162float(__float2bfloat16_rn(v.x)), h1 = __bfloat162float(__float2bfloat16_rn(v.y));
+    const float h2 = __bfloat162float(__float2bfloat16_rn(v.z)), h3 = __bfloat162float(__float2bfloat16_rn(v.w));
+    const uint2 hi = make_uint2(pack_bf16x2(h0, h1), pack_bf16x2(h2, h3));
+    row[c] = hi;
+    row[c4 + c] = make_uint2(pack_bf16x2(v.x - h0, v.y - h1), pack_bf16x2(v.z - h2, v.w - h3));
+    row[2 * c4 + c] = hi;
+  }
 }
 
 int split_bf16x3(const float* x, int n_rows, int C, void* out, cudaStream_t stream) {
   if (x == nullptr || out == nullptr || n_rows < 0 || C <= 0) return SSAM_ERR_INVALID;
   if (n_rows == 0) return SSAM_OK;
   if (C % 4 || !aligned16(x) || (reinterpret_cast<uintptr_t>(out) & 7)) return SSAM_ERR_ALIGN;
-  const int64_t n4 = static_cast<int64_t>(n_rows) * (C / 4);
-  split_bf16x3_kernel<<<static_cast<unsigned>((n4 + 255) / 256), 256, 0, stream>>>(
-      reinterpret_cast<const float4*>(x), n4, C / 4, static_cast<uint2*>(out));
+  const int c4 = C / 4;
+  const int threads = c4 >= 256 ? 256 : ((c4 + 31) / 32) * 32;
+  split_bf16x3_kernel<<<n_rows, threads, 0, stream>>>(reinterpret_cast<const float4*>(x), c4,
+                                                      static_cast<uint2*>(out));
   return status_from_cuda(cudaGetLastError());
 }
 
