@@ -359,7 +359,11 @@ __global__ void keep_select_kernel(const int32_t* inv_perm_group, int heads, int
     s_key[t] = s * static_cast<uint64_t>(N) + static_cast<uint64_t>(t);
   }
   __syncthreads();
-  for (int t = threadIdx.x; t < N; t += blockDim.x) {
+  // blockIdx.y selects this CTA's slice of the tokens to rank (every CTA of an
+  // image builds all N keys: heads x N loads, cheap next to the N x N/slices compares)
+  const int per = (N + gridDim.y - 1) / gridDim.y;
+  const int t_end = min(N, (static_cast<int>(blockIdx.y) + 1) * per);
+  for (int t = blockIdx.y * per + threadIdx.x; t < t_end; t += blockDim.x) {
     const uint64_t kt = s_key[t];
     int r = 0;
     for (int u = 0; u < N; ++u) r += s_key[u] < kt;
@@ -382,7 +386,9 @@ int keep_select(const int32_t* inv_perm_group, int B, int heads, int N, int keep
       return SSAM_ERR_CUDA;
     configured = true;
   }
-  keep_select_kernel<<<B, 1024, N * sizeof(uint64_t), stream>>>(inv_perm_group, heads, N, keep_n, idx, rows);
+  const int slices = N >= 4096 ? 4 : (N >= 1024 ? 2 : 1);
+  keep_select_kernel<<<dim3(B, slices), 1024, N * sizeof(uint64_t), stream>>>(inv_perm_group, heads, N, keep_n, idx,
+                                                                              rows);
   return status_from_cuda(cudaGetLastError());
 }
 

@@ -336,10 +336,12 @@ def encoder_forward(enc, img: torch.Tensor):
     else:
         ops.gemm_bf16(cols, w.patch_w, w.patch_b, epilogue=ops.SSAM_EPI_F32, out=x)
     interm = []
-    for blk in enc.blocks:
+    n_blocks = len(enc.blocks)
+    for i, blk in enumerate(enc.blocks):
         blk._forward_residual(x, B, gh, gw)
         if blk.window_size == 0:
-            interm.append(x.view(B, gh, gw, C).clone())
+            # a snapshot, except after the last block: nothing updates x after it (the neck only reads it)
+            interm.append(x.view(B, gh, gw, C) if i == n_blocks - 1 else x.view(B, gh, gw, C).clone())
     # neck: fp32 activations and weights through the 3-term split (3x K)
     y = ops.gemm_bf16(ops.split_bf16x3(x), w.neck0_w, None, epilogue=ops.SSAM_EPI_F32)
     ya = ops.layernorm_rows(y, w.ln_a_w, w.ln_a_b, w.eps_a, out_bf16=False)
