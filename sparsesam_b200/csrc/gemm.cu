@@ -29,7 +29,9 @@ constexpr int kGemmStageBytes = kGemmABytes + kGemmBBytes;
 constexpr int kGemmThreads = 320;
 constexpr int kGemmEpiThreads = 256;
 constexpr int kGemmTmemCols = 512;
-constexpr int kGemmSmemBytes = kGemmStages * kGemmStageBytes + 1024 /*align slack*/ + 256 /*barriers*/;
+constexpr int kEpiStageBytes = 32 * 32 * 4;  // per epilogue warp: one 32-row x 32-column fp32 chunk
+constexpr int kEpiStageTotal = 8 * kEpiStageBytes;
+constexpr int kGemmSmemBytes = kGemmStages * kGemmStageBytes + 1024 /*align slack*/ + 256 /*barriers*/ + kEpiStageTotal;
 
 struct GemmParams {
   int M, N, K;
@@ -94,6 +96,80 @@ __device__ __forceinline__ void gemm_epilogue_chunk(const GemmParams& p, int row
   }
 }
 
+// Coalesced form of gemm_epilogue_chunk for one epilogue warp: lane l holds
+// row row0 + l, columns col0..col0+31 of the accumulator. The warp stages the
+// 32 x 32 chunk (bias and GELU applied) in shared memory (16-byte units XOR
+// swizzled by row) and reads it back so that eight lanes cover one row's
+// 128-byte segment: each global load / store instruction then touches four
+// rows instead of 32. Warp-collective (all 32 lanes, rows past M skipped).
+template <int EPI>
+__device__ __forceinline__ void gemm_epilogue_chunk_staged(const GemmParams& p, int row0, int lane, int col0,
+                                                           const uint32_t (&r)[32], float4* stage) {
+  float v[32];
+#pragma unroll
+  for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+  if (p.bias != nullptr) {
+    const float4* b4 = reinterpret_cast<const float4*>(p.bias + col0);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const float4 b = __ldg(b4 + i);
+      v[4 * i + 0] += b.x;
+      v[4 * i + 1] += b.y;
+      v[4 * i + 2] += b.z;
+      v[4 * i + 3] += b.w;
+    }
+  }
+  if constexpr (EPI == SSAM_EPI_GELU_BF16) {
+#pragma unroll
+    for (int i = 0; i < 32; ++i) v[i] = gelu_exact(v[i]);
+  }
+  __syncwarp();  // the previous chunk's read-back is done
+#pragma unroll
+  for (int q = 0; q < 8; ++q)
+    stage[lane * 8 + (q ^ (lane & 7))] = make_float4(v[4 * q + 0], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
+  const int row = row0 + lane;
+  const int my_orow = row < p.M ? (p.out_rows != nullptr ? __ldg(p.out_rows + row) : row) : -1;
+  __syncwarp();
+  const int c4 = lane & 7;
+  int orows[8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) orows[i] = __shfl_sync(0xffffffffu, my_orow, 4 * i + (lane >> 3));
+  if constexpr (EPI == SSAM_EPI_ADD_F32) {
+    // all eight residual loads in flight before any store
+    float4 o[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i)
+      o[i] = orows[i] >= 0 ? reinterpret_cast<const float4*>(static_cast<const float*>(p.out) +
+                                                             static_cast<int64_t>(orows[i]) * p.ldo + col0)[c4]
+                           : make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const int rr = 4 * i + (lane >> 3);
+      const float4 sv = stage[rr * 8 + (c4 ^ (rr & 7))];
+      if (orows[i] < 0) continue;
+      o[i].x += sv.x;
+      o[i].y += sv.y;
+      o[i].z += sv.z;
+      o[i].w += sv.w;
+      reinterpret_cast<float4*>(static_cast<float*>(p.out) + static_cast<int64_t>(orows[i]) * p.ldo + col0)[c4] = o[i];
+    }
+  } else {
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const int rr = 4 * i + (lane >> 3);
+      const float4 sv = stage[rr * 8 + (c4 ^ (rr & 7))];
+      if (orows[i] < 0) continue;
+      if constexpr (EPI == SSAM_EPI_BF16 || EPI == SSAM_EPI_GELU_BF16) {
+        uint2* dst = reinterpret_cast<uint2*>(static_cast<__nv_bfloat16*>(p.out) + static_cast<int64_t>(orows[i]) * p.ldo + col0);
+        dst[c4] = make_uint2(pack_bf16x2(sv.x, sv.y), pack_bf16x2(sv.z, sv.w));
+      } else {
+        float4* dst = reinterpret_cast<float4*>(static_cast<float*>(p.out) + static_cast<int64_t>(orows[i]) * p.ldo + col0);
+        dst[c4] = sv;
+      }
+    }
+  }
+}
+
 template <int EPI>
 __global__ void __launch_bounds__(kGemmThreads, 1)
     gemm_bf16_tn_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
@@ -109,6 +185,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   uint64_t* drain_bar = tempty_bar + 2;           // [1]
   uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(drain_bar + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
+  // epilogue warp w (2..9): 4 KB chunk staging after the 256-byte barrier block
+  float4* const epi_stage = reinterpret_cast<float4*>(smem + kGemmStages * kGemmStageBytes + 256) +
+                            (threadIdx.x >> 5 >= 2 ? (threadIdx.x >> 5) - 2 : 0) * (kEpiStageBytes / 16);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -247,7 +326,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         uint32_t r[32];
         tmem_ld_32x32b_x32(t_row + static_cast<uint32_t>(c), r);
         tmem_ld_wait();
-        if (row < p.M) gemm_epilogue_chunk<EPI>(p, row, col0, r);
+        gemm_epilogue_chunk_staged<EPI>(p, row - lane, lane, col0, r, epi_stage);
       }
       tc_fence_before();
       mbar_arrive(&tempty_bar[acc]);
@@ -276,7 +355,10 @@ constexpr int kPairStages = 6;
 constexpr int kPairABytes = 128 * kGemmBK * 2;  // 16 KB
 constexpr int kPairBBytes = 128 * kGemmBK * 2;  // 16 KB (half of the 256-column B tile)
 constexpr int kPairStageBytes = kPairABytes + kPairBBytes;
-constexpr int kPairSmemBytes = kPairStages * kPairStageBytes + 1024 + 256;
+constexpr int kPairSmemBytes = kPairStages * kPairStageBytes + 1024 + 256 + kEpiStageTotal;
+static_assert((2 * kPairStages + 5) * 8 + 8 <= 256 && (2 * kGemmStages + 5) * 8 + 8 <= 256,
+              "mbarrier block overlaps the epilogue staging");
+static_assert(kPairSmemBytes <= 227 * 1024 && kGemmSmemBytes <= 227 * 1024, "shared memory per CTA");
 
 template <int EPI>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGemmThreads, 1)
@@ -293,6 +375,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGemmThreads, 1)
   uint64_t* drain_bar = tempty_bar + 2;           // [1]
   uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(drain_bar + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
+  // epilogue warp w (2..9): 4 KB chunk staging after the 256-byte barrier block
+  float4* const epi_stage = reinterpret_cast<float4*>(smem + kPairStages * kPairStageBytes + 256) +
+                            (threadIdx.x >> 5 >= 2 ? (threadIdx.x >> 5) - 2 : 0) * (kEpiStageBytes / 16);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -433,7 +518,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGemmThreads, 1)
         uint32_t r[32];
         tmem_ld_32x32b_x32(t_row + static_cast<uint32_t>(c), r);
         tmem_ld_wait();
-        if (row < p.M) gemm_epilogue_chunk<EPI>(p, row, col0, r);
+        gemm_epilogue_chunk_staged<EPI>(p, row - lane, lane, col0, r, epi_stage);
       }
       tc_fence_before();
       __syncwarp();
