@@ -170,6 +170,67 @@ __device__ __forceinline__ void gemm_epilogue_chunk_staged(const GemmParams& p, 
   }
 }
 
+// Pair-kernel epilogue through the bulk-copy engine: lane l stages its row's
+// 32 outputs in its own shared-memory row and one cp.async.bulk moves them
+// (fp32 residual add: cp.reduce.async.bulk .add.f32, done at L2, so the SM never
+// waits for the residual). Each lane reuses only its own row, so the only wait is
+// for its previous copy to have read it.
+template <int EPI>
+__device__ __forceinline__ void gemm_epilogue_chunk_bulk(const GemmParams& p, int row, int col0, const uint32_t (&r)[32],
+                                                         uint8_t* srow) {
+  float v[32];
+#pragma unroll
+  for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+  if (p.bias != nullptr) {
+    const float4* b4 = reinterpret_cast<const float4*>(p.bias + col0);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const float4 b = __ldg(b4 + i);
+      v[4 * i + 0] += b.x;
+      v[4 * i + 1] += b.y;
+      v[4 * i + 2] += b.z;
+      v[4 * i + 3] += b.w;
+    }
+  }
+  if constexpr (EPI == SSAM_EPI_GELU_BF16) {
+#pragma unroll
+    for (int i = 0; i < 32; ++i) v[i] = gelu_exact(v[i]);
+  }
+  const int orow = row < p.M ? (p.out_rows != nullptr ? __ldg(p.out_rows + row) : row) : -1;
+  asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
+  if constexpr (EPI == SSAM_EPI_BF16 || EPI == SSAM_EPI_GELU_BF16) {
+    uint4* sp = reinterpret_cast<uint4*>(srow);
+#pragma unroll
+    for (int q = 0; q < 4; ++q)
+      sp[q] = make_uint4(pack_bf16x2(v[8 * q + 0], v[8 * q + 1]), pack_bf16x2(v[8 * q + 2], v[8 * q + 3]),
+                         pack_bf16x2(v[8 * q + 4], v[8 * q + 5]), pack_bf16x2(v[8 * q + 6], v[8 * q + 7]));
+  } else {
+    float4* sp = reinterpret_cast<float4*>(srow);
+#pragma unroll
+    for (int q = 0; q < 8; ++q) sp[q] = make_float4(v[4 * q + 0], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
+  }
+  fence_proxy_async_smem();
+  if (orow >= 0) {
+    if constexpr (EPI == SSAM_EPI_BF16 || EPI == SSAM_EPI_GELU_BF16) {
+      asm volatile("cp.async.bulk.global.shared::cta.bulk_group [%0], [%1], 64;" ::"l"(
+                       static_cast<__nv_bfloat16*>(p.out) + static_cast<int64_t>(orow) * p.ldo + col0),
+                   "r"(smem_u32(srow))
+                   : "memory");
+    } else if constexpr (EPI == SSAM_EPI_F32) {
+      asm volatile("cp.async.bulk.global.shared::cta.bulk_group [%0], [%1], 128;" ::"l"(
+                       static_cast<float*>(p.out) + static_cast<int64_t>(orow) * p.ldo + col0),
+                   "r"(smem_u32(srow))
+                   : "memory");
+    } else {
+      asm volatile("cp.reduce.async.bulk.global.shared::cta.bulk_group.add.f32 [%0], [%1], 128;" ::"l"(
+                       static_cast<float*>(p.out) + static_cast<int64_t>(orow) * p.ldo + col0),
+                   "r"(smem_u32(srow))
+                   : "memory");
+    }
+  }
+  asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+}
+
 template <int EPI>
 __global__ void __launch_bounds__(kGemmThreads, 1)
     gemm_bf16_tn_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
@@ -351,32 +412,45 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
 // MMA compared with the 1-SM kernel.
 // ===========================================================================
 constexpr int kPairBM = 256;  // rows per CTA pair (128 per CTA)
-constexpr int kPairStages = 6;
+constexpr int kPairRowStride = 144;  // bulk epilogue: per-lane output row staging (128 B + 16 B pad)
 constexpr int kPairABytes = 128 * kGemmBK * 2;  // 16 KB
 constexpr int kPairBBytes = 128 * kGemmBK * 2;  // 16 KB (half of the 256-column B tile)
 constexpr int kPairStageBytes = kPairABytes + kPairBBytes;
-constexpr int kPairSmemBytes = kPairStages * kPairStageBytes + 1024 + 256 + kEpiStageTotal;
-static_assert((2 * kPairStages + 5) * 8 + 8 <= 256 && (2 * kGemmStages + 5) * 8 + 8 <= 256,
-              "mbarrier block overlaps the epilogue staging");
-static_assert(kPairSmemBytes <= 227 * 1024 && kGemmSmemBytes <= 227 * 1024, "shared memory per CTA");
+// fp32 outputs leave through the bulk-copy engine (per-row staging, 36 KB: one
+// operand stage fewer); bf16 outputs through the coalesced chunk staging (32 KB).
+template <int EPI>
+struct PairCfg {
+  static constexpr bool kBulk = EPI == SSAM_EPI_ADD_F32 || EPI == SSAM_EPI_F32;
+  static constexpr int kStages = kBulk ? 5 : 6;
+  static constexpr int kEpiBytes = kBulk ? 8 * 32 * kPairRowStride : kEpiStageTotal;
+  static constexpr int kSmemBytes = kStages * kPairStageBytes + 1024 + 256 + kEpiBytes;
+  static_assert((2 * kStages + 5) * 8 + 8 <= 256, "mbarrier block overlaps the epilogue staging");
+  static_assert(kSmemBytes <= 227 * 1024, "shared memory per CTA");
+};
+static_assert((2 * kGemmStages + 5) * 8 + 8 <= 256, "mbarrier block overlaps the epilogue staging");
+static_assert(kGemmSmemBytes <= 227 * 1024, "shared memory per CTA");
 
 template <int EPI>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGemmThreads, 1)
     gemm_bf16_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                           const GemmParams p) {
+  using PC = PairCfg<EPI>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sA = smem;
-  uint8_t* sB = smem + kPairStages * kPairABytes;
-  uint64_t* full_bar = reinterpret_cast<uint64_t*>(smem + kPairStages * kPairStageBytes);
-  uint64_t* empty_bar = full_bar + kPairStages;
-  uint64_t* tfull_bar = empty_bar + kPairStages;  // [2]
+  uint8_t* sB = smem + PC::kStages * kPairABytes;
+  uint64_t* full_bar = reinterpret_cast<uint64_t*>(smem + PC::kStages * kPairStageBytes);
+  uint64_t* empty_bar = full_bar + PC::kStages;
+  uint64_t* tfull_bar = empty_bar + PC::kStages;  // [2]
   uint64_t* tempty_bar = tfull_bar + 2;           // [2] (used on the leader)
   uint64_t* drain_bar = tempty_bar + 2;           // [1]
   uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(drain_bar + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
   // epilogue warp w (2..9): 4 KB chunk staging after the 256-byte barrier block
-  float4* const epi_stage = reinterpret_cast<float4*>(smem + kPairStages * kPairStageBytes + 256) +
+  uint8_t* const epi_row = smem + PC::kStages * kPairStageBytes + 256 +
+                          ((threadIdx.x >> 5 >= 2 ? (threadIdx.x >> 5) - 2 : 0) * 32 + (threadIdx.x & 31)) *
+                              kPairRowStride;
+  float4* const epi_stage = reinterpret_cast<float4*>(smem + PC::kStages * kPairStageBytes + 256) +
                             (threadIdx.x >> 5 >= 2 ? (threadIdx.x >> 5) - 2 : 0) * (kEpiStageBytes / 16);
 
   const int warp = threadIdx.x >> 5;
@@ -391,7 +465,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGemmThreads, 1)
   const int kblocks = (p.K + kGemmBK - 1) / kGemmBK;
 
   if (threadIdx.x == 0) {
-    for (int s = 0; s < kPairStages; ++s) {
+    for (int s = 0; s < PC::kStages; ++s) {
       mbar_init(&full_bar[s], 1);
       mbar_init(&empty_bar[s], 1);
     }
@@ -434,14 +508,14 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGemmThreads, 1)
           tma_load_2d_pair(sB + stage * kPairBBytes, &tmB, bar, kb * kGemmBK, nb * kGemmBN + rank * 128);
           issued_mask |= 1u << stage;
           issued_parity = (issued_parity & ~(1u << stage)) | (phase << stage);
-          if (++stage == kPairStages) {
+          if (++stage == PC::kStages) {
             stage = 0;
             phase ^= 1;
           }
         }
       }
       if (*abort_flag && leader) {
-        for (int s = 0; s < kPairStages; ++s)
+        for (int s = 0; s < PC::kStages; ++s)
           if (issued_mask & (1u << s)) mbar_wait(&full_bar[s], (issued_parity >> s) & 1u);
       }
     }
@@ -477,7 +551,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGemmThreads, 1)
             umma_f16_ss_pair(d_tmem, ad, bd, idesc, (kb | k) != 0 ? 1u : 0u);
           }
           umma_commit_pair(&empty_bar[stage], 0x3);
-          if (++stage == kPairStages) {
+          if (++stage == PC::kStages) {
             stage = 0;
             phase ^= 1;
           }
@@ -518,12 +592,17 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGemmThreads, 1)
         uint32_t r[32];
         tmem_ld_32x32b_x32(t_row + static_cast<uint32_t>(c), r);
         tmem_ld_wait();
-        gemm_epilogue_chunk_staged<EPI>(p, row - lane, lane, col0, r, epi_stage);
+        if constexpr (PC::kBulk) {
+          gemm_epilogue_chunk_bulk<EPI>(p, row, col0, r, epi_row);
+        } else {
+          gemm_epilogue_chunk_staged<EPI>(p, row - lane, lane, col0, r, epi_stage);
+        }
       }
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive_cluster(acc ? tempty1 : tempty0);  // one release per warp
     }
+    if constexpr (PC::kBulk) asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");  // copies done
   }
 
   tc_fence_before();
@@ -539,7 +618,7 @@ static int launch_gemm_pair(const CUtensorMap& ta, const CUtensorMap& tb, const 
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return SSAM_ERR_CUDA;
   if (!configured[dev]) {
     if (cudaFuncSetAttribute(gemm_bf16_pair_kernel<EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             kPairSmemBytes) != cudaSuccess)
+                             PairCfg<EPI>::kSmemBytes) != cudaSuccess)
       return SSAM_ERR_CUDA;
     configured[dev] = true;
   }
@@ -548,7 +627,7 @@ static int launch_gemm_pair(const CUtensorMap& ta, const CUtensorMap& tb, const 
   const int tiles = m_tiles * n_tiles;
   const int max_pairs = num_sms(dev) / 2;
   const int pairs = tiles < max_pairs ? tiles : max_pairs;
-  gemm_bf16_pair_kernel<EPI><<<2 * pairs, kGemmThreads, kPairSmemBytes, stream>>>(ta, tb, p);
+  gemm_bf16_pair_kernel<EPI><<<2 * pairs, kGemmThreads, PairCfg<EPI>::kSmemBytes, stream>>>(ta, tb, p);
   return cudaGetLastError() == cudaSuccess ? SSAM_OK : SSAM_ERR_CUDA;
 }
 
