@@ -868,30 +868,55 @@ __global__ void __launch_bounds__(kAttnThreads, 1) sparse_attn_kernel(const Attn
 }
 
 // ---------------------------------------------------------------------------
-// relbias_kernel: the rel-pos bias operand of every query, once per query.
-// Persistent; per 128-query tile of an (image|window, head) row: P_H = Q Th^T
-// and P_W = Q Tw^T on the tensor cores (NT table rows), then each thread
-// extracts its query's bands relH[j] = P_H[qh - j + win - 1], relW[j] likewise
-// (sam.py:62-73) and writes [relH / scale | relW / scale] (fp16, BW + BW
-// columns, zero padding, zeros for queries past N) as one plain row of
-// bias_ws[tile][query] in permuted query order.
-// Used for the global grid (BW = 64, NT = 128, 2 win - 1 <= 127); the
-// template also covers 16-column bands (NT = 32), but windowed grids compute
-// their bands inside the attention kernel, which measured faster than a
-// separate pass for 14x14 windows.
+// Global-grid bias pre-pass (below). Windowed grids compute their 16-column
+// bands inside the attention kernel, which measured faster than a separate
+// pass for 14x14 windows.
 // ---------------------------------------------------------------------------
 constexpr int kRelThreads = 128;
 
 template <int D, int BW>
 struct RelCfg {
-  static constexpr int kNT = BW == 16 ? 32 : 128;
+  static_assert(BW == 64, "the bias pre-pass serves the global grid (64-wide bands)");
+  static constexpr int kNT = 128;                    // table rows (2 win - 1 <= 127)
   static constexpr int kRowBytes = 4 * BW;           // [BW fp16 | BW fp16]
-  static constexpr int kStageStride = 4 * BW + 4;    // per-thread scratch row, odd word stride
-  static constexpr int kTmemCols = BW == 16 ? 64 : 256;
+  static constexpr int kStageStride = 2 * kNT + 16;  // per-thread fp16 row of P (+16 B: conflict-free 16-byte ops)
+  static constexpr int kTmemCols = 256;
   static constexpr int kSmem = 2 * TileGeom<D>::bytes(kNT) + TileGeom<D>::bytes(kAttnBM) +
                                kAttnBM * kStageStride + 64 + 1024;
 };
 
+// Band of one table: the 32 output words (fp16 pairs) relX[j] = S[qc + win - 1 - j]
+// (j < win, zero above) for the fp16 row S (kNT entries) staged at `srow`.
+// With base = qc + win - 64 the band is the reversed window S[base .. base + 63]:
+// it is read as 33 consecutive words from word base >> 1 (the words before the
+// row only feed entries that are masked) and re-paired with byte permutes.
+__device__ __forceinline__ void relbias_band(const uint8_t* srow, int qc, int win, uint32_t (&out)[32]) {
+  const int base = qc + win - 64;
+  const int w0 = base >> 1;  // arithmetic shift: floor
+  const uint32_t* sw = reinterpret_cast<const uint32_t*>(srow) + w0;
+  uint32_t u[33];
+#pragma unroll
+  for (int i = 0; i < 33; ++i) u[i] = sw[i];
+  const bool odd = base & 1;
+#pragma unroll
+  for (int k = 0; k < 32; ++k) {
+    // word k = (relX[2k], relX[2k+1]) = (S[base + 63 - 2k], S[base + 62 - 2k])
+    uint32_t w = odd ? __byte_perm(u[32 - k], u[31 - k], 0x7610) : __byte_perm(u[31 - k], 0u, 0x1032);
+    if (2 * k >= win) w = 0u;
+    else if (2 * k + 1 >= win) w &= 0xffffu;
+    out[k] = w;
+  }
+}
+
+// relbias_kernel: the rel-pos bias operand of every query, once per query.
+// Persistent, two CTAs per SM, tables loaded once per CTA; per 128-query tile of
+// an (image, head) row: P_H = Q Th^T and P_W = Q Tw^T on the tensor cores, each
+// thread stages its query's P row as fp16 (relX / scale) in shared memory and
+// extracts its bands relH[j] = P_H[qh - j + win - 1], relW likewise
+// (sam.py:62-73); the tile's 128 output rows ([relH | relW], 256 B each, in
+// permuted query order, zero rows for queries past N) are contiguous in
+// bias_ws, so each warp copies its 32 rows out with coalesced 16-byte stores.
+// The next tile's Q rows load while the current tile's bands are extracted.
 template <int D, int BW>
 __global__ void __launch_bounds__(kRelThreads) relbias_kernel(const AttnParams a) {
   using TG = TileGeom<D>;
@@ -901,11 +926,11 @@ __global__ void __launch_bounds__(kRelThreads) relbias_kernel(const AttnParams a
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const uint32_t sb = smem_u32(smem);
   const uint32_t sTh = sb, sTw = sb + TG::bytes(kNT), sQ = sb + 2 * TG::bytes(kNT);
-  uint8_t* stage = smem + 2 * TG::bytes(kNT) + TG::bytes(kAttnBM);  // per-thread scratch rows
+  uint8_t* stage = smem + 2 * TG::bytes(kNT) + TG::bytes(kAttnBM);  // per-thread rows
   uint64_t* bar = reinterpret_cast<uint64_t*>(stage + kAttnBM * RC::kStageStride);
   uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(bar + 1);
 
-  const int tid = threadIdx.x, warp = tid >> 5;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int N = a.N, win = a.win;
 
   if (tid == 0) {
@@ -927,6 +952,27 @@ __global__ void __launch_bounds__(kRelThreads) relbias_kernel(const AttnParams a
                  tid < trows ? 16u : 0u);
     }
   }
+  // this thread's query token of a tile, and its Q row into sQ
+  auto tile_token = [&](int tile) -> int {
+    const int row = tile / a.n_tiles, qtile = tile - row * a.n_tiles;
+    const int p = qtile * kAttnBM + tid;
+    return p < N ? __ldg(a.perm + static_cast<int64_t>(row) * N + p) : -1;
+  };
+  auto load_q = [&](int tile, int t) {
+    const int row = tile / a.n_tiles;
+    const int seq = row / a.heads, head = row - seq * a.heads;
+    const __nv_bfloat16* q_src =
+        t >= 0 ? a.qkv + (static_cast<int64_t>(seq) * N + t) * a.ld_qkv + head * D : nullptr;
+#pragma unroll
+    for (int c = 0; c < TG::kChunks; ++c)
+      cp_async16(tile_chunk_addr<D>(sQ, kAttnBM, tid, c), q_src != nullptr ? q_src + c * 8 : a.qkv,
+                 q_src != nullptr ? 16u : 0u);
+  };
+  int t_cur = -1;
+  if (static_cast<int>(blockIdx.x) < a.total_tiles) {
+    t_cur = tile_token(blockIdx.x);
+    load_q(blockIdx.x, t_cur);
+  }
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
@@ -936,20 +982,10 @@ __global__ void __launch_bounds__(kRelThreads) relbias_kernel(const AttnParams a
   bool ok = true;
   int iter = 0;
   for (int tile = blockIdx.x; ok && tile < a.total_tiles; tile += gridDim.x, ++iter) {
-    const int row = tile / a.n_tiles, qtile = tile - row * a.n_tiles;
-    const int seq = row / a.heads, head = row - seq * a.heads;
-    const int p = qtile * kAttnBM + tid;
-    const int t = p < N ? __ldg(a.perm + static_cast<int64_t>(row) * N + p) : -1;
-    const __nv_bfloat16* q_src =
-        t >= 0 ? a.qkv + (static_cast<int64_t>(seq) * N + t) * a.ld_qkv + head * D : nullptr;
-#pragma unroll
-    for (int c = 0; c < TG::kChunks; ++c)
-      cp_async16(tile_chunk_addr<D>(sQ, kAttnBM, tid, c), q_src != nullptr ? q_src + c * 8 : a.qkv,
-                 q_src != nullptr ? 16u : 0u);
     cp_async_wait_all();
     fence_proxy_async_smem();
     tc_fence_before();
-    __syncthreads();
+    __syncthreads();  // Q (and, the first time, the tables) of every thread are in
     tc_fence_after();
     if (tid == 0) {
       const uint32_t idesc = make_idesc_bf16(kAttnBM, kNT, 0, 0);
@@ -962,39 +998,64 @@ __global__ void __launch_bounds__(kRelThreads) relbias_kernel(const AttnParams a
     }
     ok = __syncthreads_and(mbar_wait(bar, iter & 1));
     tc_fence_after();
+    // sQ is free again: the next tile's Q rows load during the extraction
+    const int t = t_cur;
+    const int next = tile + static_cast<int>(gridDim.x);
+    if (ok && next < a.total_tiles) {
+      t_cur = tile_token(next);
+      load_q(next, t_cur);
+    }
     if (ok) {
       const int qh = t >= 0 ? t / win : 0;
       const int qw = t >= 0 ? t - qh * win : 0;
+      uint32_t bh[32], bw[32];
 #pragma unroll
-      for (int j = 0; j < 2 * BW; j += 2) *reinterpret_cast<uint32_t*>(my_stage + j * 2) = 0u;  // zero padding
-      for (int c0 = 0; c0 < kNT; c0 += 32) {
-        uint32_t rh[32], rw[32];
-        tmem_ld_32x32b_x32(t_lane + c0, rh);
-        tmem_ld_32x32b_x32(t_lane + kNT + c0, rw);
-        tmem_ld_wait();
+      for (int tab = 0; tab < 2; ++tab) {
+        // P row of this table -> fp16 (x 1/scale) in my_stage
 #pragma unroll
-        for (int j = 0; j < 32; ++j) {
-          const int jh = qh + win - 1 - (c0 + j);
-          if (jh >= 0 && jh < win)
-            *reinterpret_cast<__half*>(my_stage + jh * 2) = __float2half_rn(__uint_as_float(rh[j]) * a.inv_scale);
-          const int jw = qw + win - 1 - (c0 + j);
-          if (jw >= 0 && jw < win)
-            *reinterpret_cast<__half*>(my_stage + 2 * BW + jw * 2) =
-                __float2half_rn(__uint_as_float(rw[j]) * a.inv_scale);
+        for (int c0 = 0; c0 < kNT; c0 += 32) {
+          uint32_t rr[32];
+          tmem_ld_32x32b_x32(t_lane + tab * kNT + c0, rr);
+          tmem_ld_wait();
+          uint32_t hw[16];
+#pragma unroll
+          for (int i = 0; i < 16; ++i) {
+            const __half2 h2 = __floats2half2_rn(__uint_as_float(rr[2 * i]) * a.inv_scale,
+                                                 __uint_as_float(rr[2 * i + 1]) * a.inv_scale);
+            hw[i] = *reinterpret_cast<const uint32_t*>(&h2);
+          }
+          uint4* sp = reinterpret_cast<uint4*>(my_stage + c0 * 2);
+#pragma unroll
+          for (int i = 0; i < 4; ++i) sp[i] = make_uint4(hw[4 * i], hw[4 * i + 1], hw[4 * i + 2], hw[4 * i + 3]);
         }
+        if (tab == 0) relbias_band(my_stage, qh, win, bh);
+        else relbias_band(my_stage, qw, win, bw);
       }
-      uint4* dst = reinterpret_cast<uint4*>(reinterpret_cast<uint8_t*>(a.bias_ws) +
-                                            (static_cast<int64_t>(tile) * kAttnBM + tid) * RC::kRowBytes);
+      // output row [relH | relW] (zero for queries past N) back into my_stage
+      uint4* sp = reinterpret_cast<uint4*>(my_stage);
 #pragma unroll
-      for (int i = 0; i < RC::kRowBytes / 16; ++i) {
-        const uint32_t* w = reinterpret_cast<const uint32_t*>(my_stage + 16 * i);
-        dst[i] = t >= 0 ? make_uint4(w[0], w[1], w[2], w[3]) : make_uint4(0u, 0u, 0u, 0u);
+      for (int i = 0; i < 8; ++i)
+        sp[i] = t >= 0 ? make_uint4(bh[4 * i], bh[4 * i + 1], bh[4 * i + 2], bh[4 * i + 3]) : make_uint4(0u, 0u, 0u, 0u);
+#pragma unroll
+      for (int i = 0; i < 8; ++i)
+        sp[8 + i] =
+            t >= 0 ? make_uint4(bw[4 * i], bw[4 * i + 1], bw[4 * i + 2], bw[4 * i + 3]) : make_uint4(0u, 0u, 0u, 0u);
+      __syncwarp();
+      // the warp's 32 rows are contiguous in bias_ws: 16 lanes per 256-byte row
+      uint4* dst = reinterpret_cast<uint4*>(reinterpret_cast<uint8_t*>(a.bias_ws) +
+                                            (static_cast<int64_t>(tile) * kAttnBM + warp * 32) * RC::kRowBytes);
+#pragma unroll
+      for (int i = 0; i < 16; ++i) {
+        const int rr = 2 * i + (lane >> 4), c16 = lane & 15;
+        dst[rr * 16 + c16] =
+            *reinterpret_cast<const uint4*>(stage + (warp * 32 + rr) * RC::kStageStride + c16 * 16);
       }
     }
     tc_fence_before();
-    __syncthreads();  // Q and TMEM reused by the next tile
+    __syncthreads();  // TMEM and the staging rows are reused by the next tile
     tc_fence_after();
   }
+  cp_async_wait_all();
   if (warp == 0) tmem_dealloc(tmem, RC::kTmemCols);
 }
 
