@@ -141,6 +141,7 @@ template <int D, bool SMALL>
 struct AttnCfg {
   static constexpr int kS = 2;                    // S / P buffers in TMEM
   static constexpr int kStages = 2;               // K / V / one-hot stages (3 measured slower for windows)
+  static_assert(kStages == kS && kS == 2, "one commit per block frees S, K / V stage and O: indices g % 2");
   static constexpr int kBW = SMALL ? 16 : 64;     // bias columns per table (>= win)
   static constexpr int kNT = 32;                  // rows per table (SMALL), stacked Th ; Tw
   static constexpr int kABCols = kBW;             // 2 x kBW fp16 = kBW columns
@@ -254,18 +255,18 @@ enum {
   kBarQFull = 1,     // [2]  loader lanes (cp.async)
   kBarQEmpty = 3,    // [2]  UMMA commit after the tile's last QK^T
   kBarKFull = 5,     // [3]  K loader lanes (cp.async)
-  kBarKEmpty = 8,    // [3]  UMMA commit after QK^T
+  kBarKEmpty = 8,    // [3]  unused: S-full (QK^T done) frees the K stage
   kBarVFull = 11,    // [3]  V loader lanes (cp.async)
-  kBarVEmpty = 14,   // [3]  UMMA commit after P.V
+  kBarVEmpty = 14,   // [3]  unused: O-done (P.V done) frees the V stage
   kBarPHFull = 17,   //      UMMA commit (SMALL)
   kBarPHFree = 18,   //      softmax (SMALL)
   kBarABFull = 19,   // [2]  softmax: A_bias of the tile is in TMEM
   kBarABSFull = 21,  //      LARGE: bias rows staged (cp.async)
   kBarABSFree = 22,  //      LARGE: softmax copied the staged rows
   kBarSFull = 23,    // [2]  UMMA commit after QK^T
-  kBarSFree = 25,    // [2]  UMMA commit after P.V (P lives in the S columns)
+  kBarSFree = 25,    // [2]  unused: O-done frees the S block (P lives in its columns)
   kBarPFull = 27,    // [2]  softmax
-  kBarODone = 29,    // [2]  UMMA commit after P.V
+  kBarODone = 29,    // [2]  UMMA commit after P.V of block g (index g & 1)
   kBarOFree = 31,    // [2]  softmax epilogue
   kBarXchg = 33,     // [2 rounds][4 lane quarters]  the two softmax warps of a quarter
   kBarDrain = 41,
@@ -466,7 +467,9 @@ __global__ void __launch_bounds__(kAttnThreads, 1) sparse_attn_kernel(const Attn
         if (j + 1 < tb.n) fetch(j + 1);  // the next block's tokens, one block ahead
         const int stage = g % C::kStages;
         const int full_bar = (kv == 0 ? kBarKFull : kBarVFull) + stage;
-        if (!(ok = wait_or_abort((kv == 0 ? kBarKEmpty : kBarVEmpty) + stage, ((g / C::kStages) & 1) ^ 1))) break;
+        // K stage free once QK^T of block g - kStages completed (its S-full commit), V
+        // stage once P.V of that block did (its O-done commit)
+        if (!(ok = wait_or_abort((kv == 0 ? kBarSFull : kBarODone) + stage, ((g / C::kStages) & 1) ^ 1))) break;
         const uint32_t sK = sb + L.kv + stage * LAY::kStage;
         if (kv == 0) {  // one-hot rows of this lane's two keys
           uint8_t* oh_h = smem + L.kv + stage * LAY::kStage + 2 * TG::bytes(kAttnBN);
@@ -536,7 +539,8 @@ __global__ void __launch_bounds__(kAttnThreads, 1) sparse_attn_kernel(const Attn
         }
         const int st = c.g % C::kStages, sbuf = c.g % C::kS;
         if (!wait_or_abort(kBarKFull + st, (c.g / C::kStages) & 1)) return false;
-        if (!wait_or_abort(kBarSFree + sbuf, ((c.g / C::kS) & 1) ^ 1)) return false;
+        // S block free once P.V of block g - kS (which reads P from it) completed
+        if (!wait_or_abort(kBarODone + sbuf, ((c.g / C::kS) & 1) ^ 1)) return false;
         tc_fence_after();
         fence_proxy_async_smem();
         const uint32_t sQ = sb + L.q + (c.lt & 1) * TG::bytes(kAttnBM);
@@ -560,8 +564,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1) sparse_attn_kernel(const Attn
               umma_f16_ts(tS, ab + ks * 8, make_smem_desc(oh + ks * 32, 16, 1024, kSw128), idesc_b, 1u);
           }
         }
-        umma_commit(&bars[kBarSFull + sbuf]);
-        umma_commit(&bars[kBarKEmpty + st]);
+        umma_commit(&bars[kBarSFull + sbuf]);  // also frees K stage st (kS == kStages)
         if (c.j == c.tb.n - 1) umma_commit(&bars[kBarQEmpty + (c.lt & 1)]);
         return true;
       };
@@ -582,9 +585,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1) sparse_attn_kernel(const Attn
         for (int ks = 0; ks < kAttnBN / 16; ++ks)
           umma_f16_ts(tO, tP + ks * 8, make_smem_desc(sV + ks * 512, kAttnBN * 32, 256, kSw32), idesc_o,
                       (c.j > 0 || ks > 0) ? 1u : 0u);
-        umma_commit(&bars[kBarODone + (c.g & 1)]);
-        umma_commit(&bars[kBarVEmpty + st]);
-        umma_commit(&bars[kBarSFree + sbuf]);
+        umma_commit(&bars[kBarODone + (c.g & 1)]);  // also frees V stage st and S block sbuf
         return true;
       };
 
