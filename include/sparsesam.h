@@ -156,7 +156,9 @@ int ssam_fill_pad_rows(void* out, int64_t ld, const int32_t* rows, int n_rows, i
  * GEMM on the 5th-generation tensor cores (tcgen05 + TMEM, TMA-fed):
  *   acc[r, n] = sum_k A[r, k] * B[n, k]        (A: M x K, B: N x K, bf16, K-major)
  * then the epilogue selected by `epilogue` (SSAM_EPI_*). `bias` may be NULL.
- * out_rows is only read by SSAM_EPI_ADD_F32 (NULL = identity).
+ * out_rows (NULL = identity) maps accumulator row r to output row out_rows[r]
+ * for every epilogue; rows < 0 are skipped (window partition of qkv, keep-set
+ * scatter of lin2). Output rows may repeat only with SSAM_EPI_ADD_F32.
  * Used for Attention.qkv / Attention.proj (sam.py:182, 233), MLPBlock lin1/lin2
  * (sam.py:283, 286), patch embedding and the neck convolutions.
  * Requirements: lda, ldb multiples of 8; K multiple of 8; N multiple of 32.

@@ -63,8 +63,9 @@ def gemm_bf16(a: torch.Tensor, b: torch.Tensor, bias: torch.Tensor | None = None
     """acc = a @ b.T (a: M x K bf16, b: N x K bf16) with a fused epilogue.
 
     SSAM_EPI_BF16 / SSAM_EPI_GELU_BF16 write bf16 `out` (M x N, allocated when
-    None). SSAM_EPI_ADD_F32 accumulates into the fp32 `out` rows given by
-    `out_rows` (int32, -1 skips the row).
+    None), SSAM_EPI_F32 fp32 `out`; SSAM_EPI_ADD_F32 accumulates into the fp32
+    `out`. With `out_rows` (int32) accumulator row r goes to out[out_rows[r]]
+    (-1 skips the row) for every epilogue.
     """
     _check_cuda(a, b, bias, out, out_rows)
     if a.dtype != torch.bfloat16 or b.dtype != torch.bfloat16:
@@ -84,8 +85,6 @@ def gemm_bf16(a: torch.Tensor, b: torch.Tensor, bias: torch.Tensor | None = None
     elif epilogue == SSAM_EPI_ADD_F32:
         if out is None or out.dtype != torch.float32:
             raise ValueError("SSAM_EPI_ADD_F32 needs an fp32 `out`")
-        if out_rows is not None and (out_rows.dtype != torch.int32 or out_rows.numel() < M):
-            raise ValueError("out_rows must be int32 with at least M entries")
         if out_rows is None and out.shape[0] < M:
             raise ValueError("out has fewer than M rows")
     else:
@@ -93,6 +92,8 @@ def gemm_bf16(a: torch.Tensor, b: torch.Tensor, bias: torch.Tensor | None = None
             out = torch.empty(M, N, device=a.device, dtype=torch.bfloat16)
         elif out.dtype != torch.bfloat16 or out.shape[0] < M:
             raise ValueError("out must be bf16 with at least M rows")
+    if out_rows is not None and (out_rows.dtype != torch.int32 or out_rows.numel() < M):
+        raise ValueError("out_rows must be int32 with at least M entries")
     ldo = _rowmajor(out, "out")
     t0 = KernelTimer.begin()
     _lib.call("ssam_gemm_bf16", a.data_ptr(), lda, b.data_ptr(), ldb, M, N, K, _ptr(bias), epilogue,
