@@ -1012,20 +1012,21 @@ __global__ void __launch_bounds__(kRelThreads) relbias_kernel(const AttnParams a
       uint32_t bh[32], bw[32];
 #pragma unroll
       for (int tab = 0; tab < 2; ++tab) {
-        // P row of this table -> fp16 (x 1/scale) in my_stage
+        // P row of this table -> fp16 (x 1/scale) in my_stage; all four loads in flight before the wait
+        uint32_t rr[kNT / 32][32];
 #pragma unroll
-        for (int c0 = 0; c0 < kNT; c0 += 32) {
-          uint32_t rr[32];
-          tmem_ld_32x32b_x32(t_lane + tab * kNT + c0, rr);
-          tmem_ld_wait();
+        for (int q = 0; q < kNT / 32; ++q) tmem_ld_32x32b_x32(t_lane + tab * kNT + 32 * q, rr[q]);
+        tmem_ld_wait();
+#pragma unroll
+        for (int q = 0; q < kNT / 32; ++q) {
           uint32_t hw[16];
 #pragma unroll
           for (int i = 0; i < 16; ++i) {
-            const __half2 h2 = __floats2half2_rn(__uint_as_float(rr[2 * i]) * a.inv_scale,
-                                                 __uint_as_float(rr[2 * i + 1]) * a.inv_scale);
+            const __half2 h2 = __floats2half2_rn(__uint_as_float(rr[q][2 * i]) * a.inv_scale,
+                                                 __uint_as_float(rr[q][2 * i + 1]) * a.inv_scale);
             hw[i] = *reinterpret_cast<const uint32_t*>(&h2);
           }
-          uint4* sp = reinterpret_cast<uint4*>(my_stage + c0 * 2);
+          uint4* sp = reinterpret_cast<uint4*>(my_stage + q * 64);
 #pragma unroll
           for (int i = 0; i < 4; ++i) sp[i] = make_uint4(hw[4 * i], hw[4 * i + 1], hw[4 * i + 2], hw[4 * i + 3]);
         }
