@@ -11,20 +11,24 @@
 // and the result of permuted row p is written to raster token perm[p]
 // (the inverse permutation and the head merge are fused into the store).
 //
-// Persistent, warp-specialised CTA (one per SM), 416 threads:
+// Persistent, warp-specialised CTA (one per SM), 480 threads (15 warps):
 //   warps 0-7   softmax: warps w and w+4 share TMEM lane quarter w % 4 (query
 //               rows 32(w%4)..+31 of the tile) and split each 128-key block
 //               into two 64-key halves; the row maxima are exchanged through
 //               shared memory. They also place the next tile's rel-pos bias
 //               operand in TMEM and run the deferred epilogue, split the same way;
-//   warps 8-11  loaders: coalesced cp.async gathers of the permuted K (with the
-//               one-hot key-position operand), V and Q rows (eight lanes per
-//               128-byte row segment) and, for global grids, the bias rows;
-//   warp 12     UMMA issuer: S = Q K^T + A_bias onehot^T (A_bias from TMEM),
+//   warps 8-13  loaders: coalesced cp.async gathers (eight lanes per 128-byte row
+//               segment) of the permuted K rows with the one-hot key-position
+//               operand (warps 8-11, 32 rows each; they also copy the Q rows),
+//               the V rows (warps 12-13, 64 rows each) and, for global grids,
+//               the bias rows (warps 12-13);
+//   warp 14     UMMA issuer: S = Q K^T + A_bias onehot^T (A_bias from TMEM),
 //               O += P V (P from TMEM, V as one N = D operand); for windowed
 //               grids also [P_H | P_W] = Q [Th ; Tw]^T of the next tile.
-// Every tcgen05.mma occupies the tensor pipe for about 100 cycles up to N = 128,
-// so the blocks are 128 keys wide and P.V is one MMA per 16 keys.
+// Blocks are 128 keys wide (one N = 128 MMA per 16 channels of QK^T) and P.V
+// is one MMA per 16 keys. The loaders are latency-bound gathers, so the key rows
+// are spread over four warps, and the copy loop is kept rolled (one body shared
+// by every loader role): the kernel's hot code is instruction-cache sensitive.
 // O is rescaled lazily: only when a row maximum grows by more than 2^8 is the
 // TMEM row read, scaled and written back; otherwise the stale maximum is kept
 // (probabilities stay below 2^8 and the final 1/l normalisation is consistent).
@@ -41,7 +45,11 @@ namespace ssam {
 constexpr int kAttnBM = 128;   // queries per tile
 constexpr int kAttnBN = 128;   // keys per block
 constexpr int kMaskBlk = 64;   // the reference's mask granularity (64-token blocks)
-constexpr int kAttnThreads = 416;
+constexpr int kAttnKW = 4;      // K loader warps (128 / kAttnKW key rows each)
+constexpr int kAttnVW = 2;      // V loader warps
+constexpr int kAttnLW = kAttnKW + kAttnVW;  // loader warps 8 .. 8 + kAttnLW - 1
+constexpr int kAttnMmaWarp = 8 + kAttnLW;
+constexpr int kAttnThreads = 32 * (kAttnMmaWarp + 1);
 constexpr int kAttnTmemCols = 512;
 constexpr float kRescaleThreshold = 8.0f;  // log2 units
 
@@ -295,7 +303,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1) sparse_attn_kernel(const Attn
   if (tid == 0) {
     mbar_init(&bars[kBarTab], 64);
     for (int i = 0; i < 2; ++i) {
-      mbar_init(&bars[kBarQFull + i], 256);
+      mbar_init(&bars[kBarQFull + i], 4 * 64);
       mbar_init(&bars[kBarQEmpty + i], 1);
       mbar_init(&bars[kBarABFull + i], 256);
       mbar_init(&bars[kBarSFull + i], 1);
@@ -307,19 +315,19 @@ __global__ void __launch_bounds__(kAttnThreads, 1) sparse_attn_kernel(const Attn
     }
     mbar_init(&bars[kBarPHFull], 1);
     mbar_init(&bars[kBarPHFree], 256);
-    mbar_init(&bars[kBarABSFull], 128);
+    mbar_init(&bars[kBarABSFull], kAttnVW * 64);
     mbar_init(&bars[kBarABSFree], 256);
     for (int s = 0; s < C::kStages; ++s) {
-      mbar_init(&bars[kBarKFull + s], 128);
+      mbar_init(&bars[kBarKFull + s], kAttnKW * 64);
       mbar_init(&bars[kBarKEmpty + s], 1);
-      mbar_init(&bars[kBarVFull + s], 128);
+      mbar_init(&bars[kBarVFull + s], kAttnVW * 64);
       mbar_init(&bars[kBarVEmpty + s], 1);
     }
     mbar_init(&bars[kBarDrain], 1);
     *abort_flag = 0;
     fence_mbar_init();
   }
-  if (warp == 12) {
+  if (warp == kAttnMmaWarp) {
     tmem_alloc(tmem_holder, kAttnTmemCols);
     tmem_relinquish();
   }
@@ -341,50 +349,63 @@ __global__ void __launch_bounds__(kAttnThreads, 1) sparse_attn_kernel(const Attn
   };
   auto tile_exists = [&](int lt_) { return static_cast<int>(blockIdx.x) + lt_ * static_cast<int>(gridDim.x) < a.total_tiles; };
 
-  if (warp >= 8 && warp < 12) {
+  if (warp >= 8 && warp < kAttnMmaWarp) {
     // =========================== loader warps ===========================
-    // Warp 8 + h (h = 0, 1): K rows 64h..64h+63 of each block with their one-hot
-    // rows; warp 10 + h: the V rows. Warp 8 + w also copies Q rows
-    // 32w..32w+31 of each tile; warp 8 the rel-pos tables; warps 10-11 the
-    // staged bias rows (LARGE).
+    // Warp 8 + w (w < kAttnKW): K rows 32w..32w+31 of each block with their
+    // one-hot rows, and Q rows 32w..32w+31 of each tile; warp 8 also the rel-pos
+    // tables. Warp 8 + kAttnKW + h: V rows 64h..64h+63 of each block and (LARGE)
+    // the staged bias rows 64h..64h+63 of each tile.
     // Order: Q(0), then per tile t: Q(t+1), K/V(t, blocks). A copy instruction
     // moves 16 bytes per lane with eight lanes on one 128-byte row segment (four
     // rows per instruction), then the 32-byte tails (sixteen rows); lane l holds
     // the tokens of rows l, l+32, ... and hands them out with shuffles. Rows of
     // padded positions (token < 0) are zero-filled.
     const int lw = warp - 8;
-    const int kv = lw >> 1, half = lw & 1;  // kv 0: K, 1: V
-    // NS x 32 rows starting at tile row r0, channel offset xcol of each token row.
-    auto copy_rows = [&](auto ns_tag, uint32_t region, int R, int r0, const int* tok, const __nv_bfloat16* base,
+    const int kv = lw < kAttnKW ? 0 : 1;  // 0: K, 1: V
+    const int part = kv == 0 ? lw : lw - kAttnKW;
+    constexpr int kKRows = kAttnBN / kAttnKW, kVRows = kAttnBN / kAttnVW;
+    const int my_rows = kv == 0 ? kKRows : kVRows;
+    const int row0 = part * my_rows;   // this warp's first key row of a block
+    const bool q_warp = lw < 4;        // Q rows 32 lw .. 32 lw + 31 of each tile
+    // nrows (a multiple of 32, at most 128) rows starting at tile row r0, channel
+    // offset xcol of each token row; tok[s] holds the token of row r0 + 32 s + lane.
+    // One 32-row group per iteration (kept rolled: the loop body is shared by all
+    // loader roles, which keeps the kernel's hot code small).
+    auto copy_rows = [&](uint32_t region, int R, int r0, int nrows, const int (&tok)[4], const __nv_bfloat16* base,
                          int xcol) {
-      constexpr int NS = decltype(ns_tag)::value;
       const int c = lane & 7;
+      const int ct = 8 + (lane & 1);
+#pragma unroll 1
+      for (int s = 0; s < nrows / 32; ++s) {
+        const int tk = s == 0 ? tok[0] : s == 1 ? tok[1] : s == 2 ? tok[2] : tok[3];
+        const int rb = r0 + 32 * s;
 #pragma unroll
-      for (int i = 0; i < NS * 8; ++i) {  // 4 rows per instruction
-        const int rr = 4 * i + (lane >> 3);
-        const int t = __shfl_sync(0xffffffffu, tok[i >> 3], rr & 31);
-        const __nv_bfloat16* src = t >= 0 ? base + static_cast<int64_t>(t) * a.ld_qkv + xcol + c * 8 : a.qkv;
-        cp_async16(tile_chunk_addr<D>(region, R, r0 + rr, c), src, t >= 0 ? 16u : 0u);
-      }
-      if constexpr (D > 64) {
-        const int ct = 8 + (lane & 1);
+        for (int i = 0; i < 8; ++i) {  // 4 rows per instruction
+          const int rr = 4 * i + (lane >> 3);
+          const int t = __shfl_sync(0xffffffffu, tk, rr);
+          const __nv_bfloat16* src = t >= 0 ? base + static_cast<int64_t>(t) * a.ld_qkv + xcol + c * 8 : a.qkv;
+          cp_async16(tile_chunk_addr<D>(region, R, rb + rr, c), src, t >= 0 ? 16u : 0u);
+        }
+        if constexpr (D > 64) {
 #pragma unroll
-        for (int i = 0; i < NS * 2; ++i) {  // 16 rows per instruction
-          const int rr = 16 * i + (lane >> 1);
-          const int t = __shfl_sync(0xffffffffu, tok[i >> 1], rr & 31);
-          const __nv_bfloat16* src = t >= 0 ? base + static_cast<int64_t>(t) * a.ld_qkv + xcol + ct * 8 : a.qkv;
-          cp_async16(tile_chunk_addr<D>(region, R, r0 + rr, ct), src, t >= 0 ? 16u : 0u);
+          for (int i = 0; i < 2; ++i) {  // 16 rows per instruction
+            const int rr = 16 * i + (lane >> 1);
+            const int t = __shfl_sync(0xffffffffu, tk, rr);
+            const __nv_bfloat16* src = t >= 0 ? base + static_cast<int64_t>(t) * a.ld_qkv + xcol + ct * 8 : a.qkv;
+            cp_async16(tile_chunk_addr<D>(region, R, rb + rr, ct), src, t >= 0 ? 16u : 0u);
+          }
         }
       }
     };
-    using One = std::integral_constant<int, 1>;
-    using Two = std::integral_constant<int, 2>;
+    constexpr int kMaxKV = (kKRows > kVRows ? kKRows : kVRows) / 32;  // tokens per lane
 
     // previous one-hot entries (kh | kw << 16, -1: none) of this K-loader lane's
     // two rows in each stage
-    int oh_prev[C::kStages][2];
+    int oh_prev[C::kStages][kKRows / 32];
 #pragma unroll
-    for (int s2 = 0; s2 < C::kStages; ++s2) oh_prev[s2][0] = oh_prev[s2][1] = -1;
+    for (int s2 = 0; s2 < C::kStages; ++s2)
+#pragma unroll
+      for (int i = 0; i < kKRows / 32; ++i) oh_prev[s2][i] = -1;
     if (lw == 0) {
       // one-hot regions start at zero
       for (int s2 = 0; s2 < C::kStages; ++s2) {
@@ -412,26 +433,28 @@ __global__ void __launch_bounds__(kAttnThreads, 1) sparse_attn_kernel(const Attn
       const int row = tile / a.n_tiles, qtile = tile - row * a.n_tiles;
       const int seq = row / a.heads, head = row - seq * a.heads;
       const int32_t* perm = a.perm + static_cast<int64_t>(row) * N;
-      int qt[1];  // row 32 lw + lane of the tile
-      {
-        const int p = qtile * kAttnBM + 32 * lw + lane;
-        qt[0] = p < N ? __ldg(perm + p) : -1;
-      }
       const int qb = lt_ & 1;
-      if (!wait_or_abort(kBarQEmpty + qb, ((lt_ >> 1) & 1) ^ 1)) return false;
-      if constexpr (SMALL) s_tok[qb * kAttnBM + 32 * lw + lane] = qt[0];
-      copy_rows(One{}, sb + L.q + qb * TG::bytes(kAttnBM), kAttnBM, 32 * lw, qt,
-                a.qkv + static_cast<int64_t>(seq) * N * a.ld_qkv, head * D);
-      mbar_arrive(&bars[kBarQFull + qb]);
-      cp_async_arrive_noinc(&bars[kBarQFull + qb]);
-      if (!SMALL && kv == 1) {  // bias rows 64h..64h+63 of the tile (256 B each), two rows per instruction
+      if (q_warp) {
+        int qt[4] = {-1, -1, -1, -1};  // row 32 lw + lane of the tile in qt[0]
+        {
+          const int p = qtile * kAttnBM + 32 * lw + lane;
+          qt[0] = p < N ? __ldg(perm + p) : -1;
+        }
+        if (!wait_or_abort(kBarQEmpty + qb, ((lt_ >> 1) & 1) ^ 1)) return false;
+        if constexpr (SMALL) s_tok[qb * kAttnBM + 32 * lw + lane] = qt[0];
+        copy_rows(sb + L.q + qb * TG::bytes(kAttnBM), kAttnBM, 32 * lw, 32, qt,
+                  a.qkv + static_cast<int64_t>(seq) * N * a.ld_qkv, head * D);
+        mbar_arrive(&bars[kBarQFull + qb]);
+        cp_async_arrive_noinc(&bars[kBarQFull + qb]);
+      }
+      if (!SMALL && kv == 1) {  // bias rows row0 .. row0 + kVRows - 1 of the tile (256 B each), two rows per instruction
         if (!wait_or_abort(kBarABSFree, (lt_ & 1) ^ 1)) return false;
         const uint8_t* src = reinterpret_cast<const uint8_t*>(
             a.bias_ws + (static_cast<int64_t>(row) * a.n_tiles + qtile) * kAttnBM * 128);
         const int c = lane & 15;
 #pragma unroll 8
-        for (int i = 0; i < kAttnBM / 4; ++i) {
-          const int r = 64 * half + 2 * i + (lane >> 4);
+        for (int i = 0; i < kVRows / 2; ++i) {
+          const int r = row0 + 2 * i + (lane >> 4);
           cp_async16(sb + L.ab + (c >> 3) * (kAttnBM * 128) + r * 128 + (((c & 7) ^ (r & 7)) << 4),
                      src + r * 256 + c * 16, 16u);
         }
@@ -453,17 +476,17 @@ __global__ void __launch_bounds__(kAttnThreads, 1) sparse_attn_kernel(const Attn
       const __nv_bfloat16* base = a.qkv + static_cast<int64_t>(seq) * N * a.ld_qkv;
       const int xcol = (kv == 0 ? a.C : 2 * a.C) + head * D;
       const TileBlocks tb(a, qtile);
-      int nt[2];  // tokens of keys 64 half + lane + 32 i of the next block
+      int nt[4] = {-1, -1, -1, -1};  // tokens of keys row0 + lane + 32 i of the next block
       auto fetch = [&](int jb) {
-        const int kp = tb.at(jb) * kAttnBN + 64 * half + lane;
+        const int kp = tb.at(jb) * kAttnBN + row0 + lane;
 #pragma unroll
-        for (int i = 0; i < 2; ++i) nt[i] = kp + 32 * i < N ? __ldg(perm + kp + 32 * i) : -1;
+        for (int i = 0; i < kMaxKV; ++i) nt[i] = (32 * i < my_rows && kp + 32 * i < N) ? __ldg(perm + kp + 32 * i) : -1;
       };
       if (tb.n > 0) fetch(0);
       for (int j = 0; j < tb.n; ++j, ++g) {
-        int t[2];
+        int t[4] = {-1, -1, -1, -1};
 #pragma unroll
-        for (int i = 0; i < 2; ++i) t[i] = nt[i];
+        for (int i = 0; i < kMaxKV; ++i) t[i] = nt[i];
         if (j + 1 < tb.n) fetch(j + 1);  // the next block's tokens, one block ahead
         const int stage = g % C::kStages;
         const int full_bar = (kv == 0 ? kBarKFull : kBarVFull) + stage;
@@ -478,8 +501,8 @@ __global__ void __launch_bounds__(kAttnThreads, 1) sparse_attn_kernel(const Attn
           for (int s2 = 0; s2 < C::kStages; ++s2) {
             if (s2 != stage) continue;  // keeps oh_prev in registers
 #pragma unroll
-            for (int i = 0; i < 2; ++i) {
-              const int r = 64 * half + lane + 32 * i;
+            for (int i = 0; i < kKRows / 32; ++i) {
+              const int r = row0 + lane + 32 * i;
               int info = -1;
               if (t[i] >= 0) {
                 const int kh = t[i] / win;
@@ -499,13 +522,13 @@ __global__ void __launch_bounds__(kAttnThreads, 1) sparse_attn_kernel(const Attn
           }
           fence_proxy_async_smem();  // one-hot rows (generic stores) -> UMMA reads
         }
-        copy_rows(Two{}, kv == 0 ? sK : sK + TG::bytes(kAttnBN), kAttnBN, 64 * half, t, base, xcol);
+        copy_rows(kv == 0 ? sK : sK + TG::bytes(kAttnBN), kAttnBN, row0, my_rows, t, base, xcol);
         mbar_arrive(&bars[full_bar]);
         cp_async_arrive_noinc(&bars[full_bar]);
       }
     }
     cp_async_wait_all();
-  } else if (warp == 12) {
+  } else if (warp == kAttnMmaWarp) {
     // =========================== UMMA issuer ===========================
     if (lane == 0) {
       const uint32_t idesc_t = make_idesc_bf16(kAttnBM, 2 * C::kNT, 0, 0);
@@ -865,7 +888,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1) sparse_attn_kernel(const Attn
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
-  if (warp == 12) tmem_dealloc(tmem, kAttnTmemCols);
+  if (warp == kAttnMmaWarp) tmem_dealloc(tmem, kAttnTmemCols);
 }
 
 // ---------------------------------------------------------------------------
