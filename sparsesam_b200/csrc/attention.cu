@@ -11,18 +11,18 @@
 // and the result of permuted row p is written to raster token perm[p]
 // (the inverse permutation and the head merge are fused into the store).
 //
-// Persistent, warp-specialised CTA (one per SM), 480 threads (15 warps):
+// Persistent, warp-specialised CTA (one per SM), 512 threads (16 warps):
 //   warps 0-7   softmax: warps w and w+4 share TMEM lane quarter w % 4 (query
 //               rows 32(w%4)..+31 of the tile) and split each 128-key block
 //               into two 64-key halves; the row maxima are exchanged through
 //               shared memory. They also place the next tile's rel-pos bias
 //               operand in TMEM and run the deferred epilogue, split the same way;
-//   warps 8-13  loaders: coalesced cp.async gathers (eight lanes per 128-byte row
+//   warps 8-14  loaders: coalesced cp.async gathers (eight lanes per 128-byte row
 //               segment) of the permuted K rows with the one-hot key-position
-//               operand (warps 8-11, 32 rows each; they also copy the Q rows),
-//               the V rows (warps 12-13, 64 rows each) and, for global grids,
-//               the bias rows (warps 12-13);
-//   warp 14     UMMA issuer: S = Q K^T + A_bias onehot^T (A_bias from TMEM),
+//               operand (warps 8-11, 32 rows each), the V rows (warps 12-13,
+//               64 rows each; for global grids also the bias rows) and the Q
+//               rows (warp 14);
+//   warp 15     UMMA issuer: S = Q K^T + A_bias onehot^T (A_bias from TMEM),
 //               O += P V (P from TMEM, V as one N = D operand); for windowed
 //               grids also [P_H | P_W] = Q [Th ; Tw]^T of the next tile.
 // Blocks are 128 keys wide (one N = 128 MMA per 16 channels of QK^T) and P.V
@@ -47,7 +47,7 @@ constexpr int kAttnBN = 128;   // keys per block
 constexpr int kMaskBlk = 64;   // the reference's mask granularity (64-token blocks)
 constexpr int kAttnKW = 4;      // K loader warps (128 / kAttnKW key rows each)
 constexpr int kAttnVW = 2;      // V loader warps
-constexpr int kAttnLW = kAttnKW + kAttnVW;  // loader warps 8 .. 8 + kAttnLW - 1
+constexpr int kAttnLW = kAttnKW + kAttnVW + 1;  // loader warps 8 .. 8 + kAttnLW - 1 (last: Q rows)
 constexpr int kAttnMmaWarp = 8 + kAttnLW;
 constexpr int kAttnThreads = 32 * (kAttnMmaWarp + 1);
 constexpr int kAttnTmemCols = 512;
@@ -303,7 +303,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1) sparse_attn_kernel(const Attn
   if (tid == 0) {
     mbar_init(&bars[kBarTab], 64);
     for (int i = 0; i < 2; ++i) {
-      mbar_init(&bars[kBarQFull + i], 4 * 64);
+      mbar_init(&bars[kBarQFull + i], 64);
       mbar_init(&bars[kBarQEmpty + i], 1);
       mbar_init(&bars[kBarABFull + i], 256);
       mbar_init(&bars[kBarSFull + i], 1);
@@ -352,21 +352,22 @@ __global__ void __launch_bounds__(kAttnThreads, 1) sparse_attn_kernel(const Attn
   if (warp >= 8 && warp < kAttnMmaWarp) {
     // =========================== loader warps ===========================
     // Warp 8 + w (w < kAttnKW): K rows 32w..32w+31 of each block with their
-    // one-hot rows, and Q rows 32w..32w+31 of each tile; warp 8 also the rel-pos
-    // tables. Warp 8 + kAttnKW + h: V rows 64h..64h+63 of each block and (LARGE)
-    // the staged bias rows 64h..64h+63 of each tile.
-    // Order: Q(0), then per tile t: Q(t+1), K/V(t, blocks). A copy instruction
+    // one-hot rows; warp 8 also the rel-pos tables. Warp 8 + kAttnKW + h: V rows
+    // 64h..64h+63 of each block and (LARGE) the staged bias rows 64h..64h+63 of
+    // each tile. The last loader warp: the 128 Q rows of each tile, as soon as
+    // the tile's Q buffer is free.
+    // K / V warps: per tile t, (LARGE) the bias rows of t+1, then K/V(t, blocks). A copy instruction
     // moves 16 bytes per lane with eight lanes on one 128-byte row segment (four
     // rows per instruction), then the 32-byte tails (sixteen rows); lane l holds
     // the tokens of rows l, l+32, ... and hands them out with shuffles. Rows of
     // padded positions (token < 0) are zero-filled.
     const int lw = warp - 8;
-    const int kv = lw < kAttnKW ? 0 : 1;  // 0: K, 1: V
+    const int kv = lw < kAttnKW ? 0 : (lw < kAttnKW + kAttnVW ? 1 : 2);  // 0: K, 1: V, 2: Q
     const int part = kv == 0 ? lw : lw - kAttnKW;
     constexpr int kKRows = kAttnBN / kAttnKW, kVRows = kAttnBN / kAttnVW;
     const int my_rows = kv == 0 ? kKRows : kVRows;
     const int row0 = part * my_rows;   // this warp's first key row of a block
-    const bool q_warp = lw < 4;        // Q rows 32 lw .. 32 lw + 31 of each tile
+    const bool q_warp = kv == 2;       // all Q rows of each tile
     // nrows (a multiple of 32, at most 128) rows starting at tile row r0, channel
     // offset xcol of each token row; tok[s] holds the token of row r0 + 32 s + lane.
     // One 32-row group per iteration (kept rolled: the loop body is shared by all
@@ -435,14 +436,18 @@ __global__ void __launch_bounds__(kAttnThreads, 1) sparse_attn_kernel(const Attn
       const int32_t* perm = a.perm + static_cast<int64_t>(row) * N;
       const int qb = lt_ & 1;
       if (q_warp) {
-        int qt[4] = {-1, -1, -1, -1};  // row 32 lw + lane of the tile in qt[0]
-        {
-          const int p = qtile * kAttnBM + 32 * lw + lane;
-          qt[0] = p < N ? __ldg(perm + p) : -1;
+        int qt[4];  // rows 32 i + lane of the tile
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const int p = qtile * kAttnBM + 32 * i + lane;
+          qt[i] = p < N ? __ldg(perm + p) : -1;
         }
         if (!wait_or_abort(kBarQEmpty + qb, ((lt_ >> 1) & 1) ^ 1)) return false;
-        if constexpr (SMALL) s_tok[qb * kAttnBM + 32 * lw + lane] = qt[0];
-        copy_rows(sb + L.q + qb * TG::bytes(kAttnBM), kAttnBM, 32 * lw, 32, qt,
+        if constexpr (SMALL) {
+#pragma unroll
+          for (int i = 0; i < 4; ++i) s_tok[qb * kAttnBM + 32 * i + lane] = qt[i];
+        }
+        copy_rows(sb + L.q + qb * TG::bytes(kAttnBM), kAttnBM, 0, 128, qt,
                   a.qkv + static_cast<int64_t>(seq) * N * a.ld_qkv, head * D);
         mbar_arrive(&bars[kBarQFull + qb]);
         cp_async_arrive_noinc(&bars[kBarQFull + qb]);
@@ -466,8 +471,11 @@ __global__ void __launch_bounds__(kAttnThreads, 1) sparse_attn_kernel(const Attn
 
     int g = 0;
     bool ok = true;
-    if (tile_exists(0)) ok = load_q(0);
-    for (int lt = 0; ok && tile_exists(lt) && !*abort_flag; ++lt) {
+    if (kv == 2) {  // Q warp: every tile as soon as its Q buffer is free
+      for (int lt = 0; ok && tile_exists(lt) && !*abort_flag; ++lt) ok = load_q(lt);
+    }
+    if (kv < 2 && tile_exists(0)) ok = load_q(0);
+    for (int lt = 0; kv < 2 && ok && tile_exists(lt) && !*abort_flag; ++lt) {
       if (tile_exists(lt + 1) && !(ok = load_q(lt + 1))) break;
       const int tile = blockIdx.x + lt * gridDim.x;
       const int row = tile / a.n_tiles, qtile = tile - row * a.n_tiles;
