@@ -9,10 +9,11 @@ Every step runs through the C ABI of libsparsesam_b200.so (sparsesam_b200.ops);
 there is no CPU path — a patched encoder must live on a CUDA device.
 
 Per block (sam.py:242-290), on an fp32 residual stream x (B*H*W, C):
-  windowed  : LN1 gathered into zero-padded windows -> qkv GEMM -> Stripe-Sort
+  windowed  : LN1 on the real tokens -> qkv GEMM scattering rows into the
+              window layout (padding rows = the qkv bias) -> Stripe-Sort
               permutation (first windowed block of the forward) -> block-sparse
-              rel-pos attention (inverse permutation fused) -> proj GEMM whose
-              epilogue unpartitions the windows and adds into x
+              rel-pos attention storing raster rows (inverse permutation and
+              window unpartition fused) -> proj GEMM adding into x
   global    : the same on the full grid, with the diagonal blocks enabled
   MLP       : Residual-Consistency MLP on the keep set (windowed blocks after the
               first global block, ratio < 1, mlp_merge) or the dense MLP; both
