@@ -812,9 +812,16 @@ __global__ void __launch_bounds__(kAttnThreads, 1) sparse_attn_kernel(const Attn
           tmem_ld_32x32b_x32(tS + 32, s1);
           tmem_ld_wait();
         }
+        // LARGE: masked keys (off mask blocks, keys past N) -> -inf, so that one code
+        // path serves every block (exp2(-inf) = 0); measured faster than two paths
+        // for the global grid, slower for windows (whose blocks are all full)
+        if (!SMALL && !full) {
+#pragma unroll
+          for (int jj = 0; jj < 64; ++jj) s[jj] = (on && jj < kvalid) ? s[jj] : 0xff800000u;
+        }
         // row maximum of the raw logits over both halves (scale > 0 commutes with max)
         float mx4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
-        if (full) {
+        if (!SMALL || full) {
 #pragma unroll
           for (int jj = 0; jj < 64; ++jj) mx4[jj & 3] = fmaxf(mx4[jj & 3], __uint_as_float(s[jj]));
         } else if (on) {
@@ -859,7 +866,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1) sparse_attn_kernel(const Attn
         // P = exp2(s * scale log2e - m) as bf16 pairs over this half's 32 P columns
         uint32_t pk[32];
         float sum4[4] = {0.f, 0.f, 0.f, 0.f};
-        if (full) {
+        if (!SMALL || full) {
 #pragma unroll
           for (int e = 0; e < 32; ++e) {
             const float p0 = fast_exp2(fmaf(__uint_as_float(s[2 * e]), a.scale_log2, -m_off));
