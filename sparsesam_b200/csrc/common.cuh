@@ -305,21 +305,24 @@ __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
 
 // GELU(x) = 0.5 x (1 + erf(x / sqrt 2)) with erf from Abramowitz & Stegun,
 // Handbook of Mathematical Functions (1964), formula 7.1.26:
-//   erf(u) = 1 - (a1 t + a2 t^2 + a3 t^3 + a4 t^4 + a5 t^5) exp(-u^2),
-//   t = 1 / (1 + p u), u >= 0, |error| <= 1.5e-7; odd symmetry for u < 0.
-// About 14 instructions (one rcp.approx, one ex2.approx), far below the bf16
-// rounding of the GEMM output that consumes it.
+//   erf(u) = 1 - q(u),  q(u) = (a1 t + a2 t^2 + a3 t^3 + a4 t^4 + a5 t^5) exp(-u^2),
+//   t = 1 / (1 + p u), u >= 0, |error| <= 1.5e-7.
+// With u = |x| / sqrt 2: GELU(x) = x - |x| q / 2 for x >= 0 and -|x| q / 2 for
+// x < 0, i.e. max(x, 0) - |x| q / 2 (the 1/2 folded into the coefficients).
+// 15 instructions (one rcp.approx, one ex2.approx), far below the bf16 rounding
+// of the GEMM output that consumes it.
 __device__ __forceinline__ float gelu_exact(float x) {
-  const float u = fabsf(x) * 0.70710678118654752440f;
+  const float ax = fabsf(x);
+  const float u = ax * 0.70710678118654752440f;
   float t;
   asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(t) : "f"(fmaf(0.3275911f, u, 1.0f)));
-  const float poly =
-      fmaf(fmaf(fmaf(fmaf(1.061405429f, t, -1.453152027f), t, 1.421413741f), t, -0.284496736f), t, 0.254829592f) * t;
+  // a_i / 2
+  const float half_poly =
+      fmaf(fmaf(fmaf(fmaf(0.5307027145f, t, -0.7265760135f), t, 0.7107068705f), t, -0.142248368f), t, 0.127414796f) *
+      t;
   float e;
-  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(e) : "f"(-u * u * 1.4426950408889634f));
-  const float erf_u = copysignf(fmaf(-poly, e, 1.0f), x);
-  const float hx = 0.5f * x;
-  return fmaf(hx, erf_u, hx);
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(e) : "f"(u * u * -1.4426950408889634f));
+  return fmaf(-ax, half_poly * e, fmaxf(x, 0.f));
 }
 
 }  // namespace ssam
