@@ -403,7 +403,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
 // ===========================================================================
 // 2-SM variant: a cluster of two CTAs computes a 256x256 tile with
 // tcgen05.mma.cta_group::2 (M=256, N=256, K=16). CTA r of the pair loads rows
-// [r*128, r*128+128) of the A tile and of the B tile (6 stages x 32 KB) and owns
+// [r*128, r*128+128) of the A tile and of the B tile (PairCfg<EPI>::kStages x 32 KB) and owns
 // accumulator rows [r*128, r*128+128) in its TMEM. Both CTAs' TMA loads
 // complete on the leader's (rank 0) full barrier; the leader's commits are
 // multicast to both CTAs' empty / tmem-full barriers; both CTAs' epilogue
