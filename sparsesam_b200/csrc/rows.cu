@@ -103,6 +103,10 @@ static int launch_layernorm(const float* x, int64_t ldx, const int32_t* src_rows
       layernorm_rows_kernel<4, OUT_BF16><<<grid, block, 0, stream>>>(x, ldx, src_rows, n_rows, C, w, b, eps, out,
                                                                      ld_out);
       break;
+    case 9: case 10:  // ViT-H (C = 1280): exactly 10 float4 per lane
+      layernorm_rows_kernel<10, OUT_BF16><<<grid, block, 0, stream>>>(x, ldx, src_rows, n_rows, C, w, b, eps, out,
+                                                                      ld_out);
+      break;
     case 5: case 6: case 7:
       layernorm_rows_kernel<8, OUT_BF16><<<grid, block, 0, stream>>>(x, ldx, src_rows, n_rows, C, w, b, eps, out,
                                                                      ld_out);

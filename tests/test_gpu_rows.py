@@ -131,8 +131,8 @@ def test_window_of_raster_inverts_window_rows(cuda_device):
     assert torch.equal(torch.sort(inv.long()).values, real)
 
 
-def test_fill_pad_rows_writes_bias_only_on_padding(cuda_device):
-    B, H, W, ws, C = 1, 20, 20, 14, 96
+@pytest.mark.parametrize("B,H,W,ws,C", [(1, 20, 20, 14, 96), (2, 64, 64, 14, 3840), (3, 9, 13, 7, 264)])
+def test_fill_pad_rows_writes_bias_only_on_padding(cuda_device, B, H, W, ws, C):
     rows = ops.window_rows(B, H, W, ws, cuda_device)
     out = torch.randn(rows.numel(), C, device=cuda_device).to(torch.bfloat16)
     before = out.clone()
