@@ -201,6 +201,14 @@ int ssam_nhwc_to_nchw(const float* in, int B, int HW, int C, float* out, void* s
 int ssam_layernorm_rows(const float* x, int n_rows, int C, const float* w, const float* b, float eps,
                         void* out, int out_bf16, void* stream);
 
+/* Row LayerNorm fp32 -> bf16 that also stores its input rows unchanged to
+ * copy (fp32 [n_rows, C], 16-byte aligned). The encoder keeps its intermediate
+ * embedding after a global-attention block (the token grid the SAM-HQ encoder
+ * returns beside the features) this way: the next block's norm1 reads the
+ * residual stream anyway, so the snapshot costs its writes only. */
+int ssam_layernorm_rows_copy(const float* x, int n_rows, int C, const float* w, const float* b, float eps,
+                             void* out_bf16, float* copy, void* stream);
+
 /* ---------------------------------------------------------------------------
  * ssam_rc_mlp_fwd for callers that cannot allocate device memory at call time
  * (a host with a fixed, pre-reserved device memory budget, or a foreign-language

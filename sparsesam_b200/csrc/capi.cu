@@ -125,6 +125,11 @@ int ssam_layernorm_rows(const float* x, int n_rows, int C, const float* w, const
   return ssam::layernorm_rows(x, n_rows, C, w, b, eps, out, out_bf16, static_cast<cudaStream_t>(stream));
 }
 
+int ssam_layernorm_rows_copy(const float* x, int n_rows, int C, const float* w, const float* b, float eps,
+                             void* out_bf16, float* copy, void* stream) {
+  return ssam::layernorm_rows_copy(x, n_rows, C, w, b, eps, out_bf16, copy, static_cast<cudaStream_t>(stream));
+}
+
 int ssam_split_bf16x2(const float* x, int n_rows, int C, void* out, void* stream) {
   return ssam::split_bf16x2(x, n_rows, C, out, static_cast<cudaStream_t>(stream));
 }

@@ -43,6 +43,8 @@ int layernorm_gather(const float* x, int64_t ldx, const int32_t* src_rows, int n
                      const float* b, float eps, void* out, int64_t ld_out, cudaStream_t stream);
 int layernorm_rows(const float* x, int n_rows, int C, const float* w, const float* b, float eps, void* out,
                    int out_bf16, cudaStream_t stream);
+int layernorm_rows_copy(const float* x, int n_rows, int C, const float* w, const float* b, float eps, void* out,
+                        float* copy, cudaStream_t stream);
 int window_rows(int B, int H, int W, int ws, int32_t* rows, cudaStream_t stream);
 int patch_im2col(const float* img, int B, int Cin, int H, int W, int p, void* out, cudaStream_t stream);
 int broadcast_rows(const float* pos, int B, int T, int C, float* x, cudaStream_t stream);

@@ -12,11 +12,12 @@ namespace ssam {
 // LayerNorm over rows, optionally gathered through src_rows (-1 -> zero row).
 // One warp per output row; the row lives in registers as float4 chunks.
 // Matches torch.nn.LayerNorm: biased variance, (x - mean) * rsqrt(var + eps).
+// COPY: the input row is also stored unchanged to copy[r] (fp32, C wide).
 // ---------------------------------------------------------------------------
-template <int CHUNKS, bool OUT_BF16>
+template <int CHUNKS, bool OUT_BF16, bool COPY = false>
 __global__ void layernorm_rows_kernel(const float* __restrict__ x, int64_t ldx, const int32_t* __restrict__ src_rows,
                                       int n_rows, int C, const float* __restrict__ w, const float* __restrict__ b,
-                                      float eps, void* __restrict__ out, int64_t ld_out) {
+                                      float eps, void* __restrict__ out, int64_t ld_out, float* __restrict__ copy) {
   const int warps_per_block = blockDim.x >> 5;
   const int r = blockIdx.x * warps_per_block + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
@@ -43,6 +44,13 @@ __global__ void layernorm_rows_kernel(const float* __restrict__ x, int64_t ldx, 
     const int c = lane + 32 * i;
     v[i] = c < nc4 ? __ldg(xr + c) : make_float4(0.f, 0.f, 0.f, 0.f);
     s += (v[i].x + v[i].y) + (v[i].z + v[i].w);
+  }
+  if constexpr (COPY) {
+#pragma unroll
+    for (int i = 0; i < CHUNKS; ++i) {
+      const int c = lane + 32 * i;
+      if (c < nc4) reinterpret_cast<float4*>(copy + static_cast<int64_t>(r) * C)[c] = v[i];
+    }
   }
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
@@ -81,17 +89,18 @@ __global__ void layernorm_rows_kernel(const float* __restrict__ x, int64_t ldx, 
   }
 }
 
-template <bool OUT_BF16>
+template <bool OUT_BF16, bool COPY = false>
 static int launch_layernorm(const float* x, int64_t ldx, const int32_t* src_rows, int n_rows, int C, const float* w,
-                            const float* b, float eps, void* out, int64_t ld_out, cudaStream_t stream) {
+                            const float* b, float eps, void* out, int64_t ld_out, cudaStream_t stream,
+                            float* copy = nullptr) {
   const int nc4 = C / 4;
   const int chunks = (nc4 + 31) / 32;
   const int wpb = 8;
   const dim3 grid((n_rows + wpb - 1) / wpb), block(32 * wpb);
 #define SSAM_LN_CASE(K)                                                                                           \
   case K:                                                                                                         \
-    layernorm_rows_kernel<K, OUT_BF16><<<grid, block, 0, stream>>>(x, ldx, src_rows, n_rows, C, w, b, eps, out, \
-                                                                   ld_out);                                       \
+    layernorm_rows_kernel<K, OUT_BF16, COPY><<<grid, block, 0, stream>>>(x, ldx, src_rows, n_rows, C, w, b, eps, out, \
+                                                                   ld_out, copy);                                 \
     break;
   switch (chunks) {
     SSAM_LN_CASE(1)
@@ -100,21 +109,21 @@ static int launch_layernorm(const float* x, int64_t ldx, const int32_t* src_rows
     SSAM_LN_CASE(8)
     SSAM_LN_CASE(16)
     case 3:
-      layernorm_rows_kernel<4, OUT_BF16><<<grid, block, 0, stream>>>(x, ldx, src_rows, n_rows, C, w, b, eps, out,
-                                                                     ld_out);
+      layernorm_rows_kernel<4, OUT_BF16, COPY><<<grid, block, 0, stream>>>(x, ldx, src_rows, n_rows, C, w, b, eps, out,
+                                                                     ld_out, copy);
       break;
     case 9: case 10:  // ViT-H (C = 1280): exactly 10 float4 per lane
-      layernorm_rows_kernel<10, OUT_BF16><<<grid, block, 0, stream>>>(x, ldx, src_rows, n_rows, C, w, b, eps, out,
-                                                                      ld_out);
+      layernorm_rows_kernel<10, OUT_BF16, COPY><<<grid, block, 0, stream>>>(x, ldx, src_rows, n_rows, C, w, b, eps, out,
+                                                                      ld_out, copy);
       break;
     case 5: case 6: case 7:
-      layernorm_rows_kernel<8, OUT_BF16><<<grid, block, 0, stream>>>(x, ldx, src_rows, n_rows, C, w, b, eps, out,
-                                                                     ld_out);
+      layernorm_rows_kernel<8, OUT_BF16, COPY><<<grid, block, 0, stream>>>(x, ldx, src_rows, n_rows, C, w, b, eps, out,
+                                                                     ld_out, copy);
       break;
     default:
       if (chunks > 16) return SSAM_ERR_UNSUPPORTED;
-      layernorm_rows_kernel<16, OUT_BF16><<<grid, block, 0, stream>>>(x, ldx, src_rows, n_rows, C, w, b, eps, out,
-                                                                      ld_out);
+      layernorm_rows_kernel<16, OUT_BF16, COPY><<<grid, block, 0, stream>>>(x, ldx, src_rows, n_rows, C, w, b, eps, out,
+                                                                      ld_out, copy);
   }
 #undef SSAM_LN_CASE
   return status_from_cuda(cudaGetLastError());
@@ -136,6 +145,16 @@ int layernorm_rows(const float* x, int n_rows, int C, const float* w, const floa
   if (C % 4 || !aligned16(x) || !aligned16(w) || !aligned16(b) || !aligned16(out)) return SSAM_ERR_ALIGN;
   return out_bf16 ? launch_layernorm<true>(x, C, nullptr, n_rows, C, w, b, eps, out, C, stream)
                   : launch_layernorm<false>(x, C, nullptr, n_rows, C, w, b, eps, out, C, stream);
+}
+
+int layernorm_rows_copy(const float* x, int n_rows, int C, const float* w, const float* b, float eps, void* out,
+                        float* copy, cudaStream_t stream) {
+  if (x == nullptr || w == nullptr || b == nullptr || out == nullptr || copy == nullptr || n_rows < 0 || C <= 0)
+    return SSAM_ERR_INVALID;
+  if (n_rows == 0) return SSAM_OK;
+  if (C % 4 || !aligned16(x) || !aligned16(w) || !aligned16(b) || !aligned16(out) || !aligned16(copy))
+    return SSAM_ERR_ALIGN;
+  return launch_layernorm<true, true>(x, C, nullptr, n_rows, C, w, b, eps, out, C, stream, copy);
 }
 
 // ---------------------------------------------------------------------------

@@ -330,14 +330,24 @@ def nhwc_to_nchw(x: torch.Tensor, B: int, H: int, W: int, C: int, out: torch.Ten
 
 
 def layernorm_rows(x: torch.Tensor, w: torch.Tensor, b: torch.Tensor, eps: float, out_bf16: bool,
-                   out: torch.Tensor | None = None) -> torch.Tensor:
-    _check_cuda(x, w, b, out)
+                   out: torch.Tensor | None = None, copy_out: torch.Tensor | None = None) -> torch.Tensor:
+    """Row LayerNorm of fp32 x (rows, C). `copy_out` (fp32, x's shape; bf16 output only)
+    also receives x unchanged, read once for both."""
+    _check_cuda(x, w, b, out, copy_out)
     x2 = x.reshape(-1, x.shape[-1])
     n, C = x2.shape
     if out is None:
         out = torch.empty(n, C, dtype=torch.bfloat16 if out_bf16 else torch.float32, device=x.device)
-    _lib.call("ssam_layernorm_rows", x2.data_ptr(), n, C, w.data_ptr(), b.data_ptr(), float(eps), out.data_ptr(),
-              1 if out_bf16 else 0, _stream(x))
+    if copy_out is None:
+        _lib.call("ssam_layernorm_rows", x2.data_ptr(), n, C, w.data_ptr(), b.data_ptr(), float(eps),
+                  out.data_ptr(), 1 if out_bf16 else 0, _stream(x))
+        return out
+    if not out_bf16:
+        raise ValueError("copy_out is supported with the bf16 output")
+    if copy_out.dtype != torch.float32 or not copy_out.is_contiguous() or copy_out.numel() != n * C:
+        raise ValueError("copy_out must be a contiguous fp32 tensor with x's number of elements")
+    _lib.call("ssam_layernorm_rows_copy", x2.data_ptr(), n, C, w.data_ptr(), b.data_ptr(), float(eps),
+              out.data_ptr(), copy_out.data_ptr(), _stream(x))
     return out
 
 

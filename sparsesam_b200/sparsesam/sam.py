@@ -227,8 +227,12 @@ class ToMeSAMBlock(Block):
         self._forward_residual(xr.view(B * H * W, C), B, H, W)
         return xr.view(B, H, W, C).to(x.dtype)
 
-    def _forward_residual(self, xr: torch.Tensor, B: int, H: int, W: int) -> None:
-        """In-place block update of the fp32 residual stream xr (B*H*W, C)."""
+    def _forward_residual(self, xr: torch.Tensor, B: int, H: int, W: int,
+                          snapshot: torch.Tensor | None = None) -> None:
+        """In-place block update of the fp32 residual stream xr (B*H*W, C).
+
+        `snapshot` (xr's shape) receives xr as it enters the block (the encoder's
+        intermediate embedding of the previous, global block), written by norm1."""
         info = self._tome_info
         ratio = info["ratio"].pop(0) if isinstance(info["ratio"], list) else info["ratio"]
         C = xr.shape[1]
@@ -243,7 +247,8 @@ class ToMeSAMBlock(Block):
             ws = self.window_size
             rows = _window_rows(B, H, W, ws, xr.device)
             n_win = rows.numel() // (ws * ws)
-            xn = ops.layernorm_rows(xr, bw.ln1_w, bw.ln1_b, _LN_EPS, out_bf16=True)        # norm1
+            xn = ops.layernorm_rows(xr, bw.ln1_w, bw.ln1_b, _LN_EPS, out_bf16=True,
+                                    copy_out=snapshot)                                      # norm1
             qkv = torch.empty(rows.numel(), 3 * C, dtype=torch.bfloat16, device=xr.device)
             ops.gemm_bf16(xn, aw.qkv_w, aw.qkv_b, out=qkv, out_rows=_window_of_raster(B, H, W, ws, xr.device))
             ops.fill_pad_rows(qkv, rows, aw.qkv_b)
@@ -254,6 +259,8 @@ class ToMeSAMBlock(Block):
         else:
             if H != W:
                 raise ValueError("global SparseSAM attention expects a square grid")
+            if snapshot is not None:
+                snapshot.copy_(xr)
             xn = ops.layernorm_gather(xr, bw.ln1_w, bw.ln1_b, _LN_EPS)
             o, _, _ = _attention_core(self.attn, xn, B, H, ratio, True, _FA2_N_BLOCK_GLOBAL)
             ops.gemm_bf16(o, aw.proj_w, aw.proj_b, epilogue=ops.SSAM_EPI_ADD_F32, out=xr)
@@ -338,11 +345,17 @@ def encoder_forward(enc, img: torch.Tensor):
         ops.gemm_bf16(cols, w.patch_w, w.patch_b, epilogue=ops.SSAM_EPI_F32, out=x)
     interm = []
     n_blocks = len(enc.blocks)
+    pending = None  # the snapshot of x after a global block, written by the next block's norm1
     for i, blk in enumerate(enc.blocks):
-        blk._forward_residual(x, B, gh, gw)
+        blk._forward_residual(x, B, gh, gw, snapshot=pending)
+        pending = None
         if blk.window_size == 0:
-            # a snapshot, except after the last block: nothing updates x after it (the neck only reads it)
-            interm.append(x.view(B, gh, gw, C) if i == n_blocks - 1 else x.view(B, gh, gw, C).clone())
+            # after the last block x itself (nothing updates it; the neck only reads it)
+            if i == n_blocks - 1:
+                interm.append(x.view(B, gh, gw, C))
+            else:
+                pending = torch.empty_like(x)
+                interm.append(pending.view(B, gh, gw, C))
     # neck: fp32 activations and weights through the 3-term split (3x K)
     y = ops.gemm_bf16(ops.split_bf16x3(x), w.neck0_w, None, epilogue=ops.SSAM_EPI_F32)
     ya = ops.layernorm_rows(y, w.ln_a_w, w.ln_a_b, w.eps_a, out_bf16=False)

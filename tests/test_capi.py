@@ -68,6 +68,8 @@ def test_invalid_arguments_rejected_on_host():
         _lib.SSAM_ERR_INVALID
     assert lib.ssam_stripe_sort_perm(16, 64, 1, 1, 3, 3, 64, 4, 0, 0, 16, 16, 16, 16, nul) == _lib.SSAM_ERR_INVALID
     assert lib.ssam_keep_select(16, 1, 1, 16, 17, 16, nul, nul) == _lib.SSAM_ERR_INVALID
+    assert lib.ssam_layernorm_rows_copy(16, 4, 64, 16, 16, 1e-6, 16, nul, nul) == _lib.SSAM_ERR_INVALID
+    assert lib.ssam_layernorm_rows_copy(16, 4, 64, 16, 16, 1e-6, 16, 24, nul) == _lib.SSAM_ERR_ALIGN
     assert lib.ssam_stripe_sort_perm(16, 64, 1, 1, 4, 4, 64, 4, 7, 0, 16, 16, 16, 16, nul) == _lib.SSAM_ERR_INVALID
 
 

@@ -157,3 +157,18 @@ def test_gemm_bf16_scatters_rows(cuda_device):
     written = torch.zeros(2 * M, dtype=torch.bool, device=cuda_device)
     written[dst[keep].long()] = True
     assert (out[~written] == 0).all()
+
+
+@pytest.mark.parametrize("rows,C", [(1000, 1280), (37, 768), (5, 96)])
+def test_layernorm_rows_copy_out(cuda_device, rows, C):
+    """norm1 with the snapshot: the bf16 output equals the plain LayerNorm's and the
+    copy holds the input rows bit for bit."""
+    g = torch.Generator().manual_seed(3)
+    x = (torch.randn(rows, C, generator=g) * 3 + 1).to(cuda_device)
+    w = torch.randn(C, generator=g).to(cuda_device)
+    b = torch.randn(C, generator=g).to(cuda_device)
+    ref = ops.layernorm_rows(x, w, b, 1e-6, out_bf16=True)
+    snap = torch.full_like(x, float("nan"))
+    out = ops.layernorm_rows(x, w, b, 1e-6, out_bf16=True, copy_out=snap)
+    assert torch.equal(out, ref)
+    assert torch.equal(snap, x)
