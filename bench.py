@@ -150,6 +150,27 @@ def cpu_baseline(sample_images: int = 1) -> dict:
                       f" {dt:.1f} s"}
 
 
+def shard_seed(rank: int) -> int:
+    """Seed of rank `rank`'s image shard: every rank encodes its own images."""
+    return 1000 + rank
+
+
+def max_over_ranks(ms: float, world: int, device) -> float:
+    """The slowest rank's time (the job ends when its last rank does); `world` 1: ms."""
+    if world <= 1:
+        return ms
+    import torch
+    import torch.distributed as dist
+    t = torch.tensor([ms], device=device, dtype=torch.float64)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def job_throughput(per_rank_batch: int, world: int, steps: int, ms: float) -> float:
+    """Images/s of the whole job: every rank's images over the slowest rank's time."""
+    return per_rank_batch * world * steps / (ms * 1e-3)
+
+
 def run_reference(args) -> None:
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
@@ -195,13 +216,15 @@ def run_ours(args) -> None:
     dev = torch.device("cuda", local)
     if world > 1:
         from datetime import timedelta
+        # NCCL's own log lines (with NCCL_DEBUG set) go to stderr: stdout carries the one JSON line
+        os.environ.setdefault("NCCL_DEBUG_FILE", "/dev/stderr")
         dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=dev)
 
     batch = args.batch
     enc = host.build_image_encoder(ARCH, seed=0, device=dev).eval()
     registry.apply_sam(enc, "sparsesam", ratio=RATIO)
     # each rank owns its own shard of images (seeded by rank)
-    x_host = host.synthetic_images(batch, seed=1000 + rank, img_size=IMG).pin_memory()
+    x_host = host.synthetic_images(batch, seed=shard_seed(rank), img_size=IMG).pin_memory()
     x_dev = x_host.to(dev)
     feat_host = torch.empty(batch, 256, IMG // 16, IMG // 16, dtype=torch.float32).pin_memory()
 
@@ -219,12 +242,7 @@ def run_ours(args) -> None:
         e.record()
         torch.cuda.synchronize()
         barrier()
-        ms = s.elapsed_time(e)
-        if world > 1:
-            t = torch.tensor([ms], device=dev)
-            dist.all_reduce(t, op=dist.ReduceOp.MAX)
-            ms = float(t.item())
-        return ms
+        return max_over_ranks(s.elapsed_time(e), world, dev)
 
     with torch.no_grad():
         def step_device():
@@ -299,9 +317,8 @@ def run_ours(args) -> None:
     gemm_ms_step = sum(t for _, t in g) / args.steps
     attn_ms_step = sum(t for _, t in a) / args.steps
 
-    imgs_total = batch * world * args.steps
-    value = imgs_total / (ms * 1e-3)
-    e2e = imgs_total / (ms_e2e * 1e-3)
+    value = job_throughput(batch, world, args.steps, ms)
+    e2e = job_throughput(batch, world, args.steps, ms_e2e)
     flops_img = encoder_flops(ARCH, RATIO)
     enc_tflops = flops_img * value / world / 1e12          # per GPU
     if rank != 0:
