@@ -100,3 +100,26 @@ def test_perm_cache_is_per_forward(cuda_device):
     assert pa.keys() == pb.keys()
     assert any(not torch.equal(pa[k], pb[k]) for k in pa)
     assert enc.tome_info["ratio"] == 0.4
+
+
+def test_full_size_vit_h_batch_properties(cuda_device):
+    """BASELINE's bench configuration (SAM ViT-H, 1024^2, batch 64, d = 0.3), too
+    large for the CPU oracle, through properties that hold at any size: images
+    are independent, so an image's features and intermediate embeddings in the
+    batch-64 forward equal those of a batch-4 forward of the same images bit for
+    bit (every GEMM takes the 2-SM kernel at both sizes), and a second batch-64
+    forward repeats the first exactly."""
+    enc = host.build_image_encoder("vit_h", seed=0, device=cuda_device).eval()
+    registry.apply_sam(enc, "sparsesam", ratio=0.3)
+    imgs = host.synthetic_images(64, seed=7).to(cuda_device)
+    pick = [0, 21, 42, 63]
+    with torch.no_grad():
+        f64, i64 = enc(imgs)
+        f64b, _ = enc(imgs)
+        f4, i4 = enc(imgs[pick].contiguous())
+    assert torch.isfinite(f64).all()
+    assert torch.equal(f64, f64b)
+    assert torch.equal(f64[pick], f4)
+    assert len(i64) == len(i4) == 4
+    for a, b in zip(i64, i4):
+        assert torch.equal(a[pick], b)
