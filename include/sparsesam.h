@@ -54,6 +54,13 @@ const char* ssam_status_string(int status);
  * (SSAM_OK when no kernel raised one). `reset` != 0 clears it. */
 int ssam_device_error(int reset);
 
+/* Diagnostic for integrators (no counterpart in the reference): enqueues one
+ * small kernel whose bounded wait nothing satisfies, so it gives up after about
+ * two seconds, raises SSAM_ERR_TIMEOUT on the device flag and returns, the same
+ * path every kernel of this library takes when a wait runs out. A following
+ * ssam_device_error() reports SSAM_ERR_TIMEOUT; the context stays usable. */
+int ssam_check_wait_timeout(void* stream);
+
 /* ---------------------------------------------------------------------------
  * a1. Morton (Z-curve) raster->Z permutation of an H x W grid.
  * Replaces algos/sparsesam/z_utils.py:35-49 (encode), :65-85 (_compute_z_order),

@@ -6,6 +6,21 @@
 
 using ssam::status_from_cuda;
 
+namespace ssam {
+// One CTA waits on an mbarrier phase that nothing completes: the bounded wait
+// gives up (~2 s), raises SSAM_ERR_TIMEOUT on the device flag and returns.
+__global__ void wait_timeout_check_kernel() {
+  __shared__ __align__(8) uint64_t bar;
+  if (threadIdx.x == 0) {
+    mbar_init(&bar, 1);
+    fence_mbar_init();
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) mbar_wait(&bar, 0);
+  __syncthreads();
+}
+}  // namespace ssam
+
 extern "C" {
 
 int ssam_version(void) { return 100; }
@@ -38,6 +53,11 @@ int ssam_device_error(int reset) {
     if (cudaMemcpyToSymbol(ssam::g_device_error, &zero, sizeof(int)) != cudaSuccess) return SSAM_ERR_CUDA;
   }
   return v;
+}
+
+int ssam_check_wait_timeout(void* stream) {
+  ssam::wait_timeout_check_kernel<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>();
+  return status_from_cuda(cudaGetLastError());
 }
 
 int ssam_gemm_bf16(const void* A, int64_t lda, const void* B, int64_t ldb, int M, int N, int K, const float* bias,
