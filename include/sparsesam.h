@@ -69,13 +69,21 @@ int ssam_check_wait_timeout(void* stream);
  * ------------------------------------------------------------------------- */
 int ssam_zorder(int H, int W, int32_t* perm, int32_t* inv_perm, void* stream);
 
+/* Hilbert-curve raster->Hilbert permutation of an H x W grid, the base order of
+ * the "hilbert" perm_mode space. Replaces algos/sparsesam/hilbert_utils.py:
+ * 55-76 (_forward_hilbert_transform), :28-33 (_transposed_to_h), :108-129
+ * (_compute_hilbert_order) and :132-147 (get_hilbert_order / _inverse), as
+ * called at sam.py:131-132. Same outputs as ssam_zorder. */
+int ssam_hilbert_order(int H, int W, int32_t* perm, int32_t* inv_perm, void* stream);
+
 /* ---------------------------------------------------------------------------
  * a2. Stripe-Sort permutation of every (sequence, head) row of K.
  * Replaces algos/sparsesam/sam.py:105-164 (tile_stride_matching), as called at
  * sam.py:193-204.
  *   K of row r = s*heads + h, token t, channel c is read at
  *     k[(s*H*W + t)*ld + h*d + c]            (bf16; `k` already points at K)
- *   base_perm : int32[H*W] space-filling order (ssam_zorder output for "z").
+ *   base_perm : int32[H*W] space-filling order (ssam_zorder output for "z",
+ *               ssam_hilbert_order for "hilbert").
  *   Outputs (int32, [rows, H*W]): perm (interleave or naive layout), inv_perm,
  *   inv_perm_group. Group scores are computed in fp64; ties in the descending
  *   group ranking are broken by lowest group index.

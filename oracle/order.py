@@ -32,6 +32,47 @@ def zorder(H: int, W: int) -> tuple[np.ndarray, np.ndarray]:
     return perm, inv
 
 
+def hilbert_keys(H: int, W: int) -> np.ndarray:
+    """Hilbert index of every raster cell, row as axis 0 and column as axis 1.
+
+    Skilling's transpose algorithm (J. Skilling, "Programming the Hilbert
+    curve", AIP Conf. Proc. 707, 2004) as the reference applies it: the axes to
+    transposed form (algos/sparsesam/hilbert_utils.py:55-76), then the bits
+    interleaved with axis 0 the higher of each pair (:28-33), over
+    p = max(1, ceil(log2(max(H, W)))) bits (:118)."""
+    p = max(1, math.ceil(math.log2(max(H, W))))
+    r, c = np.meshgrid(np.arange(H, dtype=np.int64), np.arange(W, dtype=np.int64), indexing="ij")
+    x0, x1 = r.ravel().copy(), c.ravel().copy()
+    top = 1 << (p - 1)
+    q = top
+    while q > 1:                                     # undo excess work, axis 0 then axis 1
+        low = q - 1
+        x0 = np.where((x0 & q) != 0, x0 ^ low, x0)
+        hi = (x1 & q) != 0
+        t = (x0 ^ x1) & low
+        x0, x1 = np.where(hi, x0 ^ low, x0 ^ t), np.where(hi, x1, x1 ^ t)
+        q >>= 1
+    x1 = x1 ^ x0                                     # Gray encode
+    t = np.zeros_like(x0)
+    q = top
+    while q > 1:
+        t = np.where((x1 & q) != 0, t ^ (q - 1), t)
+        q >>= 1
+    x0, x1 = x0 ^ t, x1 ^ t
+    h = np.zeros_like(x0)
+    for i in range(p):
+        h |= ((x0 >> (p - 1 - i)) & 1) << (2 * p - 1 - 2 * i)
+        h |= ((x1 >> (p - 1 - i)) & 1) << (2 * p - 2 - 2 * i)
+    return h
+
+
+def hilbert_order(H: int, W: int) -> tuple[np.ndarray, np.ndarray]:
+    """(perm, inv_perm) of the Hilbert curve (hilbert_utils.py:108-129); keys are unique."""
+    perm = np.argsort(hilbert_keys(H, W), kind="stable")
+    inv = np.argsort(perm, kind="stable")
+    return perm, inv
+
+
 def stripe_sort(k: np.ndarray, H: int, W: int, group_size: int = 4,
                 perm_mode: str = "z_interleave_sort",
                 base_perm: np.ndarray | None = None):
@@ -46,9 +87,7 @@ def stripe_sort(k: np.ndarray, H: int, W: int, group_size: int = 4,
     assert N % group_size == 0
     G, gs = N // group_size, group_size
     if base_perm is None:
-        if space != "z":
-            raise NotImplementedError("pass base_perm for non-Z spaces")
-        base_perm = zorder(H, W)[0]
+        base_perm = zorder(H, W)[0] if space == "z" else hilbert_order(H, W)[0]   # sam.py:128-132
     k = np.asarray(k, dtype=np.float64)
     R = k.shape[0]
     xg = k[:, base_perm, :].reshape(R, G, gs, -1)

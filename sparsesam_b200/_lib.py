@@ -29,6 +29,7 @@ SIGNATURES: dict[str, tuple] = {
     "ssam_a_shape_n_init": (c_int, [c_int, c_int, c_f64, c_int]),
     "ssam_a_shape_mask": (c_int, [c_int, c_int, c_int, c_int, c_int, c_ptr]),
     "ssam_check_wait_timeout": (c_int, [c_ptr]),
+    "ssam_hilbert_order": (c_int, [c_int, c_int, c_ptr, c_ptr, c_ptr]),
     "ssam_sparse_attn_workspace_size": (c_size, [c_int, c_int, c_int, c_int]),
     "ssam_sparse_attn_fwd": (c_int, [c_ptr, c_i64, c_int, c_int, c_int, c_int, c_ptr, c_ptr, c_ptr,
                                      c_int, c_int, c_f32, c_ptr, c_i64, c_ptr, c_ptr, c_size, c_ptr]),
@@ -74,7 +75,7 @@ _lib: ctypes.CDLL | None = None
 # Kernels each entry point enqueues (for launch accounting); host-only calls are 0.
 KERNELS_PER_CALL = {
     "ssam_zorder": 1, "ssam_stripe_sort_perm": 1, "ssam_sparse_attn_fwd": 1, "ssam_keep_select": 1,
-    "ssam_check_wait_timeout": 1,
+    "ssam_check_wait_timeout": 1, "ssam_hilbert_order": 1,
     "ssam_layernorm_gather": 1, "ssam_window_rows": 1, "ssam_gemm_bf16": 1, "ssam_rc_mlp_fwd": 3,
     "ssam_patch_im2col": 1, "ssam_broadcast_rows": 1, "ssam_im2col3x3_nhwc": 1, "ssam_nhwc_to_nchw": 1,
     "ssam_layernorm_rows": 1, "ssam_layernorm_rows_copy": 1, "ssam_split_bf16x2": 1, "ssam_rc_mlp_fwd_noalloc": 3,

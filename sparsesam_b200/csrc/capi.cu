@@ -66,6 +66,10 @@ int ssam_gemm_bf16(const void* A, int64_t lda, const void* B, int64_t ldb, int M
                          static_cast<cudaStream_t>(stream));
 }
 
+int ssam_hilbert_order(int H, int W, int32_t* perm, int32_t* inv_perm, void* stream) {
+  return ssam::hilbert_order(H, W, perm, inv_perm, static_cast<cudaStream_t>(stream));
+}
+
 int ssam_zorder(int H, int W, int32_t* perm, int32_t* inv_perm, void* stream) {
   return ssam::zorder(H, W, perm, inv_perm, static_cast<cudaStream_t>(stream));
 }

@@ -41,6 +41,7 @@ int sparse_attn_fwd(const void* qkv, int64_t ld_qkv, int n_seq, int heads, int w
                     cudaStream_t stream);
 int layernorm_gather(const float* x, int64_t ldx, const int32_t* src_rows, int n_rows, int C, const float* w,
                      const float* b, float eps, void* out, int64_t ld_out, cudaStream_t stream);
+int hilbert_order(int H, int W, int32_t* perm, int32_t* inv_perm, cudaStream_t stream);
 int layernorm_rows(const float* x, int n_rows, int C, const float* w, const float* b, float eps, void* out,
                    int out_bf16, cudaStream_t stream);
 int layernorm_rows_copy(const float* x, int n_rows, int C, const float* w, const float* b, float eps, void* out,

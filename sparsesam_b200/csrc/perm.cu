@@ -47,9 +47,68 @@ int zorder(int H, int W, int32_t* perm, int32_t* inv_perm, cudaStream_t stream) 
 }
 
 // ---------------------------------------------------------------------------
+// Hilbert order, the `hilbert` perm_mode space (algos/sparsesam/hilbert_utils.py:
+// 55-76 _forward_hilbert_transform, :28-33 _transposed_to_h, :108-129 grid order).
+// Skilling's transpose algorithm (J. Skilling, "Programming the Hilbert curve",
+// AIP Conf. Proc. 707, 2004) in two dimensions, row = axis 0, column = axis 1,
+// over p = max(1, ceil(log2(max(H, W)))) bits; the index interleaves the
+// transposed bits with axis 0 the higher of each pair. Keys are unique, so the
+// rank of a cell is the number of smaller keys.
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ uint32_t hilbert_key(uint32_t r, uint32_t c, int p) {
+  uint32_t x0 = r, x1 = c;
+  const uint32_t top = 1u << (p - 1);
+  for (uint32_t q = top; q > 1; q >>= 1) {  // undo excess work: axis 0, then axis 1
+    const uint32_t low = q - 1;
+    if (x0 & q) x0 ^= low;
+    if (x1 & q) {
+      x0 ^= low;
+    } else {
+      const uint32_t t = (x0 ^ x1) & low;
+      x0 ^= t;
+      x1 ^= t;
+    }
+  }
+  x1 ^= x0;  // Gray encode
+  uint32_t t = 0;
+  for (uint32_t q = top; q > 1; q >>= 1)
+    if (x1 & q) t ^= q - 1;
+  x0 ^= t;
+  x1 ^= t;
+  uint32_t h = 0;
+  for (int i = 0; i < p; ++i) {
+    h |= ((x0 >> (p - 1 - i)) & 1u) << (2 * p - 1 - 2 * i);
+    h |= ((x1 >> (p - 1 - i)) & 1u) << (2 * p - 2 - 2 * i);
+  }
+  return h;
+}
+
+__global__ void hilbert_kernel(int H, int W, int num_bits, int32_t* perm, int32_t* inv_perm) {
+  const int N = H * W;
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= N) return;
+  const uint32_t ki = hilbert_key(i / W, i % W, num_bits);
+  int rank = 0;
+  for (int j = 0; j < N; ++j) rank += hilbert_key(j / W, j % W, num_bits) < ki;
+  perm[rank] = i;
+  if (inv_perm != nullptr) inv_perm[i] = rank;
+}
+
+int hilbert_order(int H, int W, int32_t* perm, int32_t* inv_perm, cudaStream_t stream) {
+  if (H <= 0 || W <= 0 || perm == nullptr || H * W > kMaxTokens) return SSAM_ERR_INVALID;
+  int m = H > W ? H : W;
+  int num_bits = 0;
+  while ((1 << num_bits) < m) ++num_bits;  // ceil(log2(m))
+  if (num_bits < 1) num_bits = 1;
+  const int N = H * W;
+  hilbert_kernel<<<(N + 255) / 256, 256, 0, stream>>>(H, W, num_bits, perm, inv_perm);
+  return status_from_cuda(cudaGetLastError());
+}
+
+// ---------------------------------------------------------------------------
 // a2. Stripe-Sort permutation (algos/sparsesam/sam.py:105-164, tile_stride_matching).
 // One CTA per (sequence, head) row:
-//   1. groups of `gs` consecutive tokens in base order (Z curve);
+//   1. groups of `gs` consecutive tokens in base order (Z or Hilbert curve);
 //   2. grp_std = mean over channels of the unbiased std over the group;
 //      grp_mean normalised to unit L2 norm (eps 1e-12);
 //   3. avg_sim_g = (sum_j <n_g, n_j> - 1) / max(G-1, 1) computed as

@@ -118,6 +118,15 @@ def zorder(H: int, W: int, device) -> tuple[torch.Tensor, torch.Tensor]:
     return perm, inv
 
 
+def hilbert_order(H: int, W: int, device) -> tuple[torch.Tensor, torch.Tensor]:
+    """Hilbert-curve order of an H x W grid: (perm, inv_perm), int32 on `device`."""
+    perm = torch.empty(H * W, dtype=torch.int32, device=device)
+    inv = torch.empty_like(perm)
+    _lib.call("ssam_hilbert_order", H, W, perm.data_ptr(), inv.data_ptr(),
+              torch.cuda.current_stream(perm.device).cuda_stream)
+    return perm, inv
+
+
 _LAYOUTS = {"interleave": 0, "naive": 1}
 _RANKINGS = {"sort": 0, "nosort": 1}
 

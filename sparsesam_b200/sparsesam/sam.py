@@ -44,18 +44,17 @@ _LN_EPS = 1e-6
 # ---------------------------------------------------------------------------
 # Device-side caches (static per grid / device)
 # ---------------------------------------------------------------------------
-_ZORDER: dict = {}
+_BASE_ORDER: dict = {}
 _WINDOW_ROWS: dict = {}
 _WINDOW_OF_RASTER: dict = {}
 
 
 def _base_order(H: int, W: int, space: str, device) -> torch.Tensor:
     key = (H, W, space, str(device))
-    if key not in _ZORDER:
-        if space != "z":
-            raise NotImplementedError(f"perm space {space!r} is not implemented on the B200 path")
-        _ZORDER[key] = ops.zorder(H, W, device)[0]
-    return _ZORDER[key]
+    if key not in _BASE_ORDER:
+        order = ops.zorder if space == "z" else ops.hilbert_order   # sam.py:128-132
+        _BASE_ORDER[key] = order(H, W, device)[0]
+    return _BASE_ORDER[key]
 
 
 def _window_rows(B: int, H: int, W: int, ws: int, device) -> torch.Tensor:

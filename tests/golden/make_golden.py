@@ -1,6 +1,7 @@
 """Generate the golden fixtures by running the reference's own SparseSAM code on CPU.
 
 Usage:  python tests/golden/make_golden.py --reference <path to a hchautran/SparseSAM checkout>
+        [--only hilbert]   (write golden_hilbert.npz alone)
 
 What runs is the reference's unmodified algos/sparsesam/sam.py and z_utils.py.
 Three things are supplied around it, because the reference cannot run on a CPU
@@ -20,6 +21,8 @@ Outputs (next to this script):
                     window / global inputs and four perm modes, A-shape n_init table
   golden_e2e.npz    a small SparseSAM-patched encoder forward (features,
                     intermediate embeddings, permutations, keep sets, dense control)
+  golden_hilbert.npz  the reference's Hilbert orders (hilbert_utils.py) for seven
+                    grids and tile_stride_matching in three Hilbert perm modes
 """
 from __future__ import annotations
 
@@ -175,6 +178,25 @@ def make_order(ref_sam, ref_z) -> dict:
     return out
 
 
+def make_hilbert(ref_sam) -> dict:
+    import algos.sparsesam.hilbert_utils as ref_h  # noqa: E402
+    out = {}
+    for H, W in ((4, 4), (14, 14), (64, 64), (16, 16), (7, 9), (1, 5), (2, 2)):
+        out[f"horder_{H}x{W}"] = ref_h.get_hilbert_order(H, W).numpy().astype(np.int32)
+        out[f"hinv_{H}x{W}"] = ref_h.get_hilbert_inverse(H, W).numpy().astype(np.int32)
+    g = torch.Generator().manual_seed(4321)
+    cases = {"win": (bf16_round(torch.randn(6, 196, 64, generator=g)), 14),
+             "glob": (bf16_round(torch.randn(2, 4096, 16, generator=g)), 64)}
+    for name, (k, win) in cases.items():
+        out[f"k_{name}"] = bf16_bits(k)
+        for mode in ("hilbert_interleave_sort", "hilbert_naive_sort", "hilbert_interleave_nosort"):
+            p, ip, ipg = ref_sam.tile_stride_matching(k, win, win, ratio=E2E_RATIO, perm_mode=mode)
+            out[f"{name}_{mode}_perm"] = p.numpy().astype(np.int16)
+            out[f"{name}_{mode}_inv"] = ip.numpy().astype(np.int16)
+            out[f"{name}_{mode}_invg"] = ipg.numpy().astype(np.int16)
+    return out
+
+
 def make_e2e(ref_sam) -> dict:
     out = {}
     img = host.synthetic_images(1, seed=E2E_SEED, img_size=E2E_CFG["img_size"])
@@ -213,11 +235,14 @@ def make_e2e(ref_sam) -> dict:
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", required=True, help="path of a hchautran/SparseSAM checkout")
+    ap.add_argument("--only", choices=("all", "hilbert"), default="all")
     args = ap.parse_args()
     torch.manual_seed(0)
     ref_sam, ref_z = load_reference(os.path.abspath(args.reference))
-    np.savez_compressed(os.path.join(HERE, "golden_order.npz"), **make_order(ref_sam, ref_z))
-    np.savez_compressed(os.path.join(HERE, "golden_e2e.npz"), **make_e2e(ref_sam))
+    if args.only == "all":
+        np.savez_compressed(os.path.join(HERE, "golden_order.npz"), **make_order(ref_sam, ref_z))
+        np.savez_compressed(os.path.join(HERE, "golden_e2e.npz"), **make_e2e(ref_sam))
+    np.savez_compressed(os.path.join(HERE, "golden_hilbert.npz"), **make_hilbert(ref_sam))
     print("wrote", os.listdir(HERE))
 
 

@@ -30,14 +30,14 @@ def _forced(enc):
     return {k: tuple(t.long().cpu() for t in v) for k, v in pc.items() if isinstance(k[0], int) and len(v) == 3}
 
 
-def _run_gpu(enc, img, cuda_device, ratio, mlp_merge=True):
+def _run_gpu(enc, img, cuda_device, ratio, mlp_merge=True, perm_mode="z_interleave_sort"):
     enc = enc.to(cuda_device)
     # registry.apply_sam treats ratio >= 1 as a no-op (registry.py:65-66); the
     # dense control goes through apply_patch directly, as the reference's ablation does.
     if ratio < 1:
-        registry.apply_sam(enc, "sparsesam", ratio=ratio, mlp_merge=mlp_merge)
+        registry.apply_sam(enc, "sparsesam", ratio=ratio, mlp_merge=mlp_merge, perm_mode=perm_mode)
     else:
-        apply_patch(enc, ratio=ratio, mlp_merge=mlp_merge)
+        apply_patch(enc, ratio=ratio, mlp_merge=mlp_merge, perm_mode=perm_mode)
     # keep the permutations: the patched forward resets perm_cache on entry
     feats, interm = enc(img.to(cuda_device))
     torch.cuda.synchronize()
@@ -57,6 +57,20 @@ def test_small_encoder(cuda_device, ratio):
     enc_ref = e2e_encoder()
     feats, interm, forced = _run_gpu(e2e_encoder(), img, cuda_device, ratio)
     rf, ri = oenc.encoder_forward(enc_ref, img, ratio, forced_perms=forced)
+    _check(feats, rf, "features")
+    for a, b in zip(interm, ri):
+        _check(a, b, "interm")
+
+
+@pytest.mark.parametrize("perm_mode", ["hilbert_interleave_sort", "hilbert_naive_nosort"])
+def test_small_encoder_hilbert(cuda_device, perm_mode):
+    """The Hilbert perm_mode space end to end (sam.py:128-132): the patched
+    encoder runs in that space and its features match the fp32 oracle run on the
+    GPU's permutations (whose bit-exactness test_gpu_order.py checks)."""
+    img = host.synthetic_images(2, seed=0, img_size=256)
+    feats, interm, forced = _run_gpu(e2e_encoder(), img, cuda_device, E2E_RATIO, perm_mode=perm_mode)
+    assert forced and all(k[3] == perm_mode for k in forced)
+    rf, ri = oenc.encoder_forward(e2e_encoder(), img, E2E_RATIO, perm_mode=perm_mode, forced_perms=forced)
     _check(feats, rf, "features")
     for a, b in zip(interm, ri):
         _check(a, b, "interm")

@@ -5,10 +5,11 @@ import torch
 
 from oracle import order
 from sparsesam_b200 import ops
-from tests._golden import MODES, bf16_bits_to_f32, load
+from tests._golden import HILBERT_GRIDS, HILBERT_MODES, MODES, bf16_bits_to_f32, load
 
 pytestmark = pytest.mark.gpu
 GO = load("golden_order.npz")
+GH = load("golden_hilbert.npz")
 
 
 @pytest.mark.parametrize("H,W", [(4, 4), (14, 14), (64, 64), (16, 16), (7, 9), (1, 5)])
@@ -26,7 +27,7 @@ def _gpu_perm(k_rows_f32: np.ndarray, win: int, mode: str, cuda_device, heads=1)
     buf = torch.from_numpy(k_rows_f32).view(n_seq, heads, N, d).permute(0, 2, 1, 3).reshape(n_seq * N, heads * d)
     buf = buf.to(cuda_device, torch.bfloat16).contiguous()
     space, layout, ranking = ops.parse_perm_mode(mode)
-    base = ops.zorder(win, win, cuda_device)[0]
+    base = (ops.zorder if space == "z" else ops.hilbert_order)(win, win, cuda_device)[0]
     p, ip, ipg = ops.stripe_sort_perm(buf, n_seq, heads, win, win, d, base, layout=layout, ranking=ranking)
     return p.cpu().numpy(), ip.cpu().numpy(), ipg.cpu().numpy()
 
@@ -40,6 +41,27 @@ def test_stripe_sort_golden_inputs(cuda_device, case, win, mode):
     np.testing.assert_array_equal(p, op)
     np.testing.assert_array_equal(ip, oip)
     np.testing.assert_array_equal(ipg, oipg)
+
+
+@pytest.mark.parametrize("H,W", list(HILBERT_GRIDS) + [(128, 128), (3, 1)])
+def test_hilbert_order(cuda_device, H, W):
+    p, inv = ops.hilbert_order(H, W, cuda_device)
+    op, oinv = order.hilbert_order(H, W)
+    np.testing.assert_array_equal(p.cpu().numpy(), op)
+    np.testing.assert_array_equal(inv.cpu().numpy(), oinv)
+    if (H, W) in HILBERT_GRIDS:  # the reference's own orders
+        np.testing.assert_array_equal(p.cpu().numpy(), GH[f"horder_{H}x{W}"])
+
+
+@pytest.mark.parametrize("case,win", [("win", 14), ("glob", 64)])
+@pytest.mark.parametrize("mode", HILBERT_MODES)
+def test_stripe_sort_hilbert_matches_reference(cuda_device, case, win, mode):
+    """Hilbert base order: the GPU permutations equal the reference's own outputs."""
+    k = bf16_bits_to_f32(GH[f"k_{case}"])
+    p, ip, ipg = _gpu_perm(k, win, mode, cuda_device)
+    np.testing.assert_array_equal(p, GH[f"{case}_{mode}_perm"].astype(np.int64))
+    np.testing.assert_array_equal(ip, GH[f"{case}_{mode}_inv"].astype(np.int64))
+    np.testing.assert_array_equal(ipg, GH[f"{case}_{mode}_invg"].astype(np.int64))
 
 
 @pytest.mark.parametrize("heads,d", [(16, 80), (16, 64), (12, 64)])

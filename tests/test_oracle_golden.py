@@ -6,10 +6,12 @@ import torch
 from oracle import encoder as oenc
 from oracle import order
 from oracle.attention import sparse_attention
-from tests._golden import E2E_RATIO, MODES, bf16_bits_to_f32, e2e_encoder, group_order, load
+from tests._golden import (E2E_RATIO, HILBERT_GRIDS, HILBERT_MODES, MODES, bf16_bits_to_f32, e2e_encoder,
+                           group_order, load)
 
 GO = load("golden_order.npz")
 GE = load("golden_e2e.npz")
+GH = load("golden_hilbert.npz")
 
 
 def test_zorder_kat():
@@ -19,6 +21,25 @@ def test_zorder_kat():
         p, inv = order.zorder(H, W)
         np.testing.assert_array_equal(p, GO[f"zorder_{H}x{W}"])
         np.testing.assert_array_equal(inv, GO[f"zinv_{H}x{W}"])
+
+
+def test_hilbert_order_matches_reference():
+    # 4x4 Hilbert order (known answer from the reference's hilbert_utils.py)
+    assert order.hilbert_order(4, 4)[0].tolist() == [0, 4, 5, 1, 2, 3, 7, 6, 10, 11, 15, 14, 13, 9, 8, 12]
+    for H, W in HILBERT_GRIDS:
+        p, inv = order.hilbert_order(H, W)
+        np.testing.assert_array_equal(p, GH[f"horder_{H}x{W}"])
+        np.testing.assert_array_equal(inv, GH[f"hinv_{H}x{W}"])
+
+
+@pytest.mark.parametrize("case,win", [("win", 14), ("glob", 64)])
+@pytest.mark.parametrize("mode", HILBERT_MODES)
+def test_stripe_sort_hilbert_matches_reference(case, win, mode):
+    k = bf16_bits_to_f32(GH[f"k_{case}"])
+    p, ip, ipg = order.stripe_sort(k, win, win, perm_mode=mode)
+    np.testing.assert_array_equal(p, GH[f"{case}_{mode}_perm"].astype(np.int64))
+    np.testing.assert_array_equal(ip, GH[f"{case}_{mode}_inv"].astype(np.int64))
+    np.testing.assert_array_equal(ipg, GH[f"{case}_{mode}_invg"].astype(np.int64))
 
 
 CASES = [("win", 14, 64), ("winpad", 14, 64), ("glob", 64, 16)]
