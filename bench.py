@@ -221,8 +221,13 @@ def run_ours(args) -> None:
         dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=dev)
 
     batch = args.batch
-    enc = host.build_image_encoder(ARCH, seed=0, device=dev).eval()
-    registry.apply_sam(enc, "sparsesam", ratio=RATIO)
+    arch, ratio = args.arch, args.ratio
+    enc = host.build_image_encoder(arch, seed=0, device=dev).eval()
+    if ratio < 1.0:
+        registry.apply_sam(enc, "sparsesam", ratio=ratio)
+    else:  # the dense control: apply_sam treats ratio >= 1 as no patch (registry.py:65-66)
+        from sparsesam_b200.sparsesam.sam import apply_patch
+        apply_patch(enc, ratio=1.0)
     # each rank owns its own shard of images (seeded by rank)
     x_host = host.synthetic_images(batch, seed=shard_seed(rank), img_size=IMG).pin_memory()
     x_dev = x_host.to(dev)
@@ -319,7 +324,7 @@ def run_ours(args) -> None:
 
     value = job_throughput(batch, world, args.steps, ms)
     e2e = job_throughput(batch, world, args.steps, ms_e2e)
-    flops_img = encoder_flops(ARCH, RATIO)
+    flops_img = encoder_flops(arch, ratio)
     enc_tflops = flops_img * value / world / 1e12          # per GPU
     if rank != 0:
         if world > 1:
@@ -331,12 +336,15 @@ def run_ours(args) -> None:
         with open(tpath) as f:
             traffic = json.load(f).get("bytes_per_launch")
     line = {
-        "metric": METRIC, "value": value, "unit": "images/s", "n_gpus": world, "steps": args.steps,
+        "metric": METRIC if (arch, ratio) == (ARCH, RATIO) else
+        f"SAM {arch} encoder images/sec @1024², d={ratio}, bf16, B200; % TC peak",
+        "value": value, "unit": "images/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-        "config": {"workload": f"SAM ViT-H image encoder (configs[4]), 1024x1024, SparseSAM density {RATIO}, "
+        "config": {"workload": f"SAM {arch} image encoder ({dict(vit_h='configs[4]', vit_l='configs[3]', vit_b='configs[0]')[arch]}), "
+                               f"1024x1024, SparseSAM density {ratio}, "
                                f"{batch} images per GPU, seed-0 random weights",
-                   "global_batch": batch * world, "per_gpu_batch": batch, "ratio": RATIO,
+                   "global_batch": batch * world, "per_gpu_batch": batch, "ratio": ratio,
                    "parallelism": f"dp{world} (independent image shards, no collective)",
                    "l2": "inputs larger than L2 (805 MB of images and GBs of activations per step)"},
         "e2e": {"value": e2e, "unit": "images/s", "h2d_bytes_per_step": x_host.numel() * 4,
@@ -369,6 +377,8 @@ def main() -> None:
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
     ap.add_argument("--batch", type=int, default=PER_GPU_BATCH)
+    ap.add_argument("--ratio", type=float, default=RATIO, help="SparseSAM density (1.0: dense control)")
+    ap.add_argument("--arch", choices=("vit_h", "vit_l", "vit_b"), default=ARCH)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()
     if args.warmup < 3 and args.impl == "ours":
