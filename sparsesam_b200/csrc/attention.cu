@@ -351,10 +351,12 @@ __global__ void __launch_bounds__(kAttnThreads, 1) sparse_attn_kernel(const Attn
 
   // Fast path: one try_wait (usually the phase has completed); the abort flag is
   // read only when the wait has to sleep.
+  // (the bounded wait stays a call here: inlining its first test measured slower
+  // for this kernel, whose loader and softmax paths sit at the register limit)
   auto wait_or_abort = [&](int bar, uint32_t parity) -> bool {
     if (mbar_try_wait(&bars[bar], parity)) return true;
     if (*abort_flag) return false;
-    if (!mbar_wait(&bars[bar], parity)) {
+    if (!mbar_wait_slow(&bars[bar], parity)) {
       *abort_flag = 1;
       return false;
     }
@@ -649,7 +651,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1) sparse_attn_kernel(const Attn
         cp.advance(a);
       }
       umma_commit(&bars[kBarDrain]);
-      mbar_wait(&bars[kBarDrain], 0);
+      mbar_wait_slow(&bars[kBarDrain], 0);
     }
   } else {
     // ========================= softmax warps =========================
@@ -1048,7 +1050,7 @@ __global__ void __launch_bounds__(kRelThreads) relbias_kernel(const AttnParams a
       }
       umma_commit(bar);
     }
-    ok = __syncthreads_and(mbar_wait(bar, iter & 1));
+    ok = __syncthreads_and(mbar_wait_slow(bar, iter & 1));
     tc_fence_after();
     // sQ is free again: the next tile's Q rows load during the extraction
     const int t = t_cur;

@@ -403,7 +403,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
 // ===========================================================================
 // 2-SM variant: a cluster of two CTAs computes a 256x256 tile with
 // tcgen05.mma.cta_group::2 (M=256, N=256, K=16). CTA r of the pair loads rows
-// [r*128, r*128+128) of the A tile and of the B tile (PairCfg<EPI>::kStages x 32 KB) and owns
+// [r*128, r*128+128) of the A tile and of the B tile (PairCfg<EPI>::kStages stages of
+// kSub 64-wide K sub-tiles, 32 KB each) and owns
 // accumulator rows [r*128, r*128+128) in its TMEM. Both CTAs' TMA loads
 // complete on the leader's (rank 0) full barrier; the leader's commits are
 // multicast to both CTAs' empty / tmem-full barriers; both CTAs' epilogue
@@ -416,14 +417,21 @@ constexpr int kPairRowStride = 144;  // bulk epilogue: per-lane output row stagi
 constexpr int kPairABytes = 128 * kGemmBK * 2;  // 16 KB
 constexpr int kPairBBytes = 128 * kGemmBK * 2;  // 16 KB (half of the 256-column B tile)
 constexpr int kPairStageBytes = kPairABytes + kPairBBytes;
-// fp32 outputs leave through the bulk-copy engine (per-row staging, 36 KB: one
-// operand stage fewer); bf16 outputs through the coalesced chunk staging (32 KB).
+// fp32 outputs leave through the bulk-copy engine (per-row staging, 36 KB: five
+// 32 KB stages); bf16 outputs through the coalesced chunk staging (32 KB), with
+// three 64 KB stages of two K sub-tiles each, so that one barrier round trip of
+// the UMMA thread feeds eight MMAs instead of four (batch-64 qkv 2.14 -> 2.08 ms,
+// fc1 0.951 -> 0.926 ms in a sustained loop). A sub-tile past K is zero-filled by TMA.
 template <int EPI>
 struct PairCfg {
   static constexpr bool kBulk = EPI == SSAM_EPI_ADD_F32 || EPI == SSAM_EPI_F32;
-  static constexpr int kStages = kBulk ? 5 : 6;
+  static constexpr int kSub = kBulk ? 1 : 2;  // 64-wide K sub-tiles per stage
+  static constexpr int kStages = kBulk ? 5 : 3;
+  static constexpr int kStageABytes = kSub * kPairABytes;
+  static constexpr int kStageBBytes = kSub * kPairBBytes;
+  static constexpr int kStageBytes = kStageABytes + kStageBBytes;
   static constexpr int kEpiBytes = kBulk ? 8 * 32 * kPairRowStride : kEpiStageTotal;
-  static constexpr int kSmemBytes = kStages * kPairStageBytes + 1024 + 256 + kEpiBytes;
+  static constexpr int kSmemBytes = kStages * kStageBytes + 1024 + 256 + kEpiBytes;
   static_assert((2 * kStages + 5) * 8 + 8 <= 256, "mbarrier block overlaps the epilogue staging");
   static_assert(kSmemBytes <= 227 * 1024, "shared memory per CTA");
 };
@@ -438,8 +446,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGemmThreads, 1)
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sA = smem;
-  uint8_t* sB = smem + PC::kStages * kPairABytes;
-  uint64_t* full_bar = reinterpret_cast<uint64_t*>(smem + PC::kStages * kPairStageBytes);
+  uint8_t* sB = smem + PC::kStages * PC::kStageABytes;
+  uint64_t* full_bar = reinterpret_cast<uint64_t*>(smem + PC::kStages * PC::kStageBytes);
   uint64_t* empty_bar = full_bar + PC::kStages;
   uint64_t* tfull_bar = empty_bar + PC::kStages;  // [2]
   uint64_t* tempty_bar = tfull_bar + 2;           // [2] (used on the leader)
@@ -447,10 +455,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGemmThreads, 1)
   uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(drain_bar + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
   // epilogue warp w (2..9): 4 KB chunk staging after the 256-byte barrier block
-  uint8_t* const epi_row = smem + PC::kStages * kPairStageBytes + 256 +
+  uint8_t* const epi_row = smem + PC::kStages * PC::kStageBytes + 256 +
                           ((threadIdx.x >> 5 >= 2 ? (threadIdx.x >> 5) - 2 : 0) * 32 + (threadIdx.x & 31)) *
                               kPairRowStride;
-  float4* const epi_stage = reinterpret_cast<float4*>(smem + PC::kStages * kPairStageBytes + 256) +
+  float4* const epi_stage = reinterpret_cast<float4*>(smem + PC::kStages * PC::kStageBytes + 256) +
                             (threadIdx.x >> 5 >= 2 ? (threadIdx.x >> 5) - 2 : 0) * (kEpiStageBytes / 16);
 
   const int warp = threadIdx.x >> 5;
@@ -463,6 +471,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGemmThreads, 1)
   const int n_tiles = (p.N + kGemmBN - 1) / kGemmBN;
   const int num_tiles = m_tiles * n_tiles;
   const int kblocks = (p.K + kGemmBK - 1) / kGemmBK;
+  const int ksteps = (kblocks + PC::kSub - 1) / PC::kSub;  // stages per tile (a sub-tile past K reads zeros)
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < PC::kStages; ++s) {
@@ -497,15 +506,19 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGemmThreads, 1)
       for (int tile = pair; tile < num_tiles && !*abort_flag; tile += n_pairs) {
         const int mb = tile / n_tiles;
         const int nb = tile - mb * n_tiles;
-        for (int kb = 0; kb < kblocks; ++kb) {
+        for (int ks = 0; ks < ksteps; ++ks) {
           if (!mbar_wait(&empty_bar[stage], phase ^ 1)) {
             *abort_flag = 1;
             break;
           }
           const uint32_t bar = mapa_shared(smem_u32(&full_bar[stage]), 0);
-          if (leader) mbar_arrive_expect_tx(&full_bar[stage], 2 * kPairStageBytes);
-          tma_load_2d_pair(sA + stage * kPairABytes, &tmA, bar, kb * kGemmBK, mb * kPairBM + rank * 128);
-          tma_load_2d_pair(sB + stage * kPairBBytes, &tmB, bar, kb * kGemmBK, nb * kGemmBN + rank * 128);
+          if (leader) mbar_arrive_expect_tx(&full_bar[stage], 2 * PC::kStageBytes);
+#pragma unroll
+          for (int s = 0; s < PC::kSub; ++s) {
+            const int kx = (ks * PC::kSub + s) * kGemmBK;
+            tma_load_2d_pair(sA + stage * PC::kStageABytes + s * kPairABytes, &tmA, bar, kx, mb * kPairBM + rank * 128);
+            tma_load_2d_pair(sB + stage * PC::kStageBBytes + s * kPairBBytes, &tmB, bar, kx, nb * kGemmBN + rank * 128);
+          }
           issued_mask |= 1u << stage;
           issued_parity = (issued_parity & ~(1u << stage)) | (phase << stage);
           if (++stage == PC::kStages) {
@@ -536,20 +549,22 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGemmThreads, 1)
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * kGemmBN);
         bool ok = true;
-        for (int kb = 0; kb < kblocks; ++kb) {
+        for (int ks = 0; ks < ksteps; ++ks) {
           if (!mbar_wait(&full_bar[stage], phase)) {
             ok = false;
             break;
           }
           tc_fence_after();
-          const uint32_t a0 = smem_u32(sA + stage * kPairABytes);
-          const uint32_t b0 = smem_u32(sB + stage * kPairBBytes);
+          const uint32_t a0 = smem_u32(sA + stage * PC::kStageABytes);
+          const uint32_t b0 = smem_u32(sB + stage * PC::kStageBBytes);
 #pragma unroll
-          for (int k = 0; k < kGemmBK / 16; ++k) {
-            const uint64_t ad = make_smem_desc(a0 + k * 32, 16, 1024, kSw128);
-            const uint64_t bd = make_smem_desc(b0 + k * 32, 16, 1024, kSw128);
-            umma_f16_ss_pair(d_tmem, ad, bd, idesc, (kb | k) != 0 ? 1u : 0u);
-          }
+          for (int s = 0; s < PC::kSub; ++s)
+#pragma unroll
+            for (int k = 0; k < kGemmBK / 16; ++k) {
+              const uint64_t ad = make_smem_desc(a0 + s * kPairABytes + k * 32, 16, 1024, kSw128);
+              const uint64_t bd = make_smem_desc(b0 + s * kPairBBytes + k * 32, 16, 1024, kSw128);
+              umma_f16_ss_pair(d_tmem, ad, bd, idesc, (ks | s | k) != 0 ? 1u : 0u);
+            }
           umma_commit_pair(&empty_bar[stage], 0x3);
           if (++stage == PC::kStages) {
             stage = 0;

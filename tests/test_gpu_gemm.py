@@ -13,6 +13,8 @@ SHAPES = [
     (257, 96, 136),      # N not a multiple of 256, ragged everything
     (4900, 2304, 768),   # ViT-B windowed qkv shape (one image): 2-SM path
     (16384, 512, 128),   # 2-SM path, exact tiles
+    (8192, 512, 320),    # 2-SM path, odd number of 64-wide K blocks (last stage half past K)
+    (16384, 256, 136),   # 2-SM path, ragged K tail inside the last stage's first sub-tile
     (20000, 1280, 320),  # 2-SM path, M tail inside a CTA pair
     (16500, 768, 1280),  # 2-SM path, M tail in the second CTA of the last pair
 ]
