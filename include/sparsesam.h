@@ -116,19 +116,24 @@ int ssam_a_shape_mask(int N, int m_block, int n_block, int n_init, int with_diag
  *   rel_pos_h / rel_pos_w : bf16 [2*win-1, d] tables (Attention.rel_pos_h/w).
  *   perm  : int32 [n_seq*heads, win*win] permutation of every row.
  *   out   : bf16 [n_seq*win*win, heads*d] in raster token order, leading dim ld_out.
- *   n_init_blocks / with_diag : A-shape mask over 64-token blocks.
+ *   n_init_blocks / n_block / with_diag : A-shape mask over n_block-token blocks
+ *               (n_block 64, SparseSAM's choice at sam.py:52-57, or 128; query
+ *               and key blocks have the same size, as the reference's
+ *               get_compiled_a_shape(D, m_block, n_block, ...) is always called):
+ *               query block m attends to key blocks n < n_init_blocks, and to
+ *               n == m when with_diag != 0 (flash_attn.py:132-145).
  *   out_rows  : optional int32 [n_seq*N]: the output row of (sequence s,
  *               token t) is out_rows[s*N + t] (< 0: not stored); NULL stores it
  *               at row s*N + t. Windowed blocks pass the ssam_window_rows map,
  *               which fuses window_unpartition (sam.py:256) into the store.
  *   workspace : ssam_sparse_attn_workspace_size() bytes (0 for windowed grids,
  *               win <= 16; global grids keep the per-query bias there).
- * d must be 64 or 80.
+ * d must be 64 or 80; n_block other than 64 / 128 returns SSAM_ERR_UNSUPPORTED.
  * ------------------------------------------------------------------------- */
 size_t ssam_sparse_attn_workspace_size(int n_seq, int heads, int win, int d);
 int ssam_sparse_attn_fwd(const void* qkv, int64_t ld_qkv, int n_seq, int heads, int win, int d,
                          const void* rel_pos_h, const void* rel_pos_w, const int32_t* perm,
-                         int n_init_blocks, int with_diag, float scale, void* out, int64_t ld_out,
+                         int n_init_blocks, int n_block, int with_diag, float scale, void* out, int64_t ld_out,
                          const int32_t* out_rows, void* workspace, size_t workspace_bytes, void* stream);
 
 /* ---------------------------------------------------------------------------
@@ -235,7 +240,10 @@ int ssam_layernorm_rows_copy(const float* x, int n_rows, int C, const float* w, 
  *   - Returns SSAM_ERR_UNSUPPORTED when ssam_rc_mlp_workspace_size(n_rows, C,
  *     hidden) exceeds 32 MiB (about 2,600 rows at C = 1280, hidden = 5120).
  *   - The first call on a device resolves the scratch address for that device;
- *     make it before any CUDA stream capture starts.
+ *     make it before any CUDA stream capture starts. After cudaDeviceReset the
+ *     device's next call resolves it again (the address is cached per context).
+ *   - `stream` must belong to the current device (the scratch address is that
+ *     device's); a stream of another device returns SSAM_ERR_INVALID.
  *   - All calls share the one scratch array: calls that may overlap on the GPU
  *     (different streams, or several host threads) race on it; serialise them.
  *   - Allocates nothing (no cudaMalloc / cudaFree, no library allocator).

@@ -3,8 +3,9 @@
 //
 // Semantics (algos/kernels/flash_attn.py:577-909 with algos/sparsesam/sam.py:62-73,
 // 206-233): for one (sequence, head) row with tokens in permuted order
-// p = 0..N-1 (token perm[p]), query block m = p/64 attends to key blocks
-// n < n_init (plus n == m when with_diag):
+// p = 0..N-1 (token perm[p]), query block m = p/n_block attends to key blocks
+// n < n_init (plus n == m when with_diag), n_block = 64 (SparseSAM's own
+// choice, sam.py:52-57) or 128:
 //   logit(p, k) = scale * <q_p, k_k> + relH[p][kh(k)] + relW[p][kw(k)]
 //   relH[p][j]  = <q_p, Th[qh(p) - j + win - 1]>,  relW likewise with columns,
 // keys past N are masked, rows are softmax-normalised (an empty row gives 0),
@@ -44,7 +45,7 @@ namespace ssam {
 
 constexpr int kAttnBM = 128;   // queries per tile
 constexpr int kAttnBN = 128;   // keys per block
-constexpr int kMaskBlk = 64;   // the reference's mask granularity (64-token blocks)
+constexpr int kMaskBlk = 64;   // keep-bar unit inside the kernel (64-token blocks; 128-token masks are converted)
 constexpr int kAttnKW = 4;      // K loader warps (128 / kAttnKW key rows each)
 constexpr int kAttnVW = 2;      // V loader warps
 constexpr int kAttnLW = kAttnKW + kAttnVW + 1;  // loader warps 8 .. 8 + kAttnLW - 1 (last: Q rows)
@@ -201,7 +202,8 @@ struct AttnParams {
   const __nv_bfloat16* th;  // (2win-1, D)
   const __nv_bfloat16* tw;
   const int32_t* perm;
-  int n_init, with_diag;
+  int n_init;     // keep bar in 64-token blocks
+  int with_diag;  // 0: none, 1: 64-token diagonal blocks, 2: 128-token diagonal blocks (the whole tile)
   float scale_log2;  // scale * log2(e)
   float inv_scale;   // 1 / scale
   __nv_bfloat16* out;
@@ -803,9 +805,12 @@ __global__ void __launch_bounds__(kAttnThreads, 1) sparse_attn_kernel(const Attn
         const uint32_t tS = t_lane + sbuf * kAttnBN + 64 * h;
         // this half's 64 keys: 64-key mask block 2 kb + h
         const int mh = 2 * kb + h;
-        const bool full = 2 * kb + 1 < tb.nk && (kb + 1) * kAttnBN <= N;
+        // 64-token masks enable the query's own 64-block on the diagonal, 128-token
+        // masks the tile's whole diagonal block
+        const bool diag_tile = a.with_diag == 2 && kb == tb.qt;
+        const bool full = (2 * kb + 1 < tb.nk || diag_tile) && (kb + 1) * kAttnBN <= N;
         const int kvalid = N - kb * kAttnBN - 64 * h;  // keys of this half inside the sequence
-        const bool on = full || mh < tb.nk || (a.with_diag && mh == my_mb);
+        const bool on = full || mh < tb.nk || diag_tile || (a.with_diag == 1 && mh == my_mb);
         uint32_t s[64];
         {
           uint32_t (&s0)[32] = *reinterpret_cast<uint32_t(*)[32]>(&s[0]);
@@ -1124,18 +1129,18 @@ template <int D, bool SMALL>
 static int launch_attn(const AttnParams& p, cudaStream_t stream) {
   const AttnLayout<D, SMALL> L;
   using RC = RelCfg<D, 64>;
-  static bool configured[64] = {false};
-  int dev = 0;
-  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return SSAM_ERR_CUDA;
-  if (!configured[dev]) {
+  static PerDeviceOnce configured;
+  const int dev = current_device();
+  const int st = configured.run(dev, [&L] {
     if (cudaFuncSetAttribute(sparse_attn_kernel<D, SMALL>, cudaFuncAttributeMaxDynamicSharedMemorySize, L.total) !=
         cudaSuccess)
       return SSAM_ERR_CUDA;
     if (!SMALL && cudaFuncSetAttribute(relbias_kernel<D, 64>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                        RC::kSmem) != cudaSuccess)
       return SSAM_ERR_CUDA;
-    configured[dev] = true;
-  }
+    return SSAM_OK;
+  });
+  if (st != SSAM_OK) return st;
   const int sms = num_sms(dev);
   if (!SMALL) {
     // persistent bias pre-pass, two CTAs per SM (256 TMEM columns each)
@@ -1152,12 +1157,13 @@ static int launch_attn(const AttnParams& p, cudaStream_t stream) {
 }
 
 int sparse_attn_fwd(const void* qkv, int64_t ld_qkv, int n_seq, int heads, int win, int d, const void* rel_pos_h,
-                    const void* rel_pos_w, const int32_t* perm, int n_init_blocks, int with_diag, float scale,
-                    void* out, int64_t ld_out, const int32_t* out_rows, void* workspace, size_t workspace_bytes,
-                    cudaStream_t stream) {
+                    const void* rel_pos_w, const int32_t* perm, int n_init_blocks, int n_block, int with_diag,
+                    float scale, void* out, int64_t ld_out, const int32_t* out_rows, void* workspace,
+                    size_t workspace_bytes, cudaStream_t stream) {
   if (qkv == nullptr || rel_pos_h == nullptr || rel_pos_w == nullptr || perm == nullptr || out == nullptr)
     return SSAM_ERR_INVALID;
   if (n_seq <= 0 || heads <= 0 || win <= 0 || n_init_blocks < 0) return SSAM_ERR_INVALID;
+  if (n_block != 64 && n_block != 128) return SSAM_ERR_UNSUPPORTED;
   if (n_init_blocks == 0 && !with_diag) return SSAM_ERR_INVALID;  // every query would have no key
   if (d != 64 && d != 80) return SSAM_ERR_UNSUPPORTED;
   if (win > 64) return SSAM_ERR_UNSUPPORTED;  // 2*win-1 table rows must fit one 128-wide MMA
@@ -1177,8 +1183,10 @@ int sparse_attn_fwd(const void* qkv, int64_t ld_qkv, int n_seq, int heads, int w
   p.th = static_cast<const __nv_bfloat16*>(rel_pos_h);
   p.tw = static_cast<const __nv_bfloat16*>(rel_pos_w);
   p.perm = perm;
-  p.n_init = n_init_blocks;
-  p.with_diag = with_diag ? 1 : 0;
+  // the kernel's keep bar counts 64-token blocks (n < n_init of 128 tokens = n64 < 2 n_init)
+  const int nblk64 = (p.N + kMaskBlk - 1) / kMaskBlk;
+  p.n_init = n_block == 128 ? (n_init_blocks < nblk64 ? 2 * n_init_blocks : nblk64) : n_init_blocks;
+  p.with_diag = with_diag ? (n_block == 128 ? 2 : 1) : 0;
   p.scale_log2 = scale * 1.4426950408889634f;
   p.out = static_cast<__nv_bfloat16*>(out);
   p.ld_out = ld_out;

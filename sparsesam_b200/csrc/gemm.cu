@@ -628,15 +628,14 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGemmThreads, 1)
 
 template <int EPI>
 static int launch_gemm_pair(const CUtensorMap& ta, const CUtensorMap& tb, const GemmParams& p, cudaStream_t stream) {
-  static bool configured[64] = {false};
-  int dev = 0;
-  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return SSAM_ERR_CUDA;
-  if (!configured[dev]) {
-    if (cudaFuncSetAttribute(gemm_bf16_pair_kernel<EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             PairCfg<EPI>::kSmemBytes) != cudaSuccess)
-      return SSAM_ERR_CUDA;
-    configured[dev] = true;
-  }
+  static PerDeviceOnce configured;
+  const int dev = current_device();
+  const int st = configured.run(dev, [] {
+    return status_from_cuda(cudaFuncSetAttribute(gemm_bf16_pair_kernel<EPI>,
+                                                 cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                 PairCfg<EPI>::kSmemBytes));
+  });
+  if (st != SSAM_OK) return st;
   const int m_tiles = (p.M + kPairBM - 1) / kPairBM;
   const int n_tiles = (p.N + kGemmBN - 1) / kGemmBN;
   const int tiles = m_tiles * n_tiles;
@@ -648,16 +647,13 @@ static int launch_gemm_pair(const CUtensorMap& ta, const CUtensorMap& tb, const 
 
 template <int EPI>
 static int launch_gemm(const CUtensorMap& ta, const CUtensorMap& tb, const GemmParams& p, cudaStream_t stream) {
-  static bool configured[64] = {false};
-  int dev = 0;
-  if (cudaGetDevice(&dev) != cudaSuccess) return SSAM_ERR_CUDA;
-  if (dev < 0 || dev >= 64) return SSAM_ERR_CUDA;
-  if (!configured[dev]) {
-    if (cudaFuncSetAttribute(gemm_bf16_tn_kernel<EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize, kGemmSmemBytes) !=
-        cudaSuccess)
-      return SSAM_ERR_CUDA;
-    configured[dev] = true;
-  }
+  static PerDeviceOnce configured;
+  const int dev = current_device();
+  const int st = configured.run(dev, [] {
+    return status_from_cuda(
+        cudaFuncSetAttribute(gemm_bf16_tn_kernel<EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize, kGemmSmemBytes));
+  });
+  if (st != SSAM_OK) return st;
   const int m_tiles = (p.M + kGemmBM - 1) / kGemmBM;
   const int n_tiles = (p.N + kGemmBN - 1) / kGemmBN;
   const int tiles = m_tiles * n_tiles;

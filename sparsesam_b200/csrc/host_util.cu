@@ -9,14 +9,15 @@ namespace ssam {
 int status_from_cuda(cudaError_t e) { return e == cudaSuccess ? SSAM_OK : SSAM_ERR_CUDA; }
 
 int num_sms(int dev) {
-  static int cache[64] = {0};
-  if (dev < 0 || dev >= 64) return 148;
-  if (cache[dev] == 0) {
-    int n = 0;
+  // racing first calls both store the same value
+  static std::atomic<int> cache[kMaxDevices] = {};
+  if (dev < 0 || dev >= kMaxDevices) return 148;
+  int n = cache[dev].load(std::memory_order_relaxed);
+  if (n == 0) {
     if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0) n = 148;
-    cache[dev] = n;
+    cache[dev].store(n, std::memory_order_relaxed);
   }
-  return cache[dev];
+  return n;
 }
 
 typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,

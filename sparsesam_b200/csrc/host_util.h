@@ -6,11 +6,44 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <atomic>
+#include <mutex>
+
 #include "../../include/sparsesam.h"
 
 namespace ssam {
 
 inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+constexpr int kMaxDevices = 64;
+
+// One-time, per-device launch set-up (cudaFuncSetAttribute and the like) that
+// several host threads may reach at once: later calls read one atomic flag,
+// first calls serialise on a mutex, and a set-up that failed runs again on the
+// next call. `setup` returns an SSAM status.
+class PerDeviceOnce {
+ public:
+  template <class F>
+  int run(int dev, F&& setup) {
+    if (dev < 0 || dev >= kMaxDevices) return SSAM_ERR_CUDA;
+    if (done_[dev].load(std::memory_order_acquire)) return SSAM_OK;
+    std::lock_guard<std::mutex> lock(mu_);
+    if (done_[dev].load(std::memory_order_relaxed)) return SSAM_OK;
+    const int st = setup();
+    if (st == SSAM_OK) done_[dev].store(true, std::memory_order_release);
+    return st;
+  }
+
+ private:
+  std::atomic<bool> done_[kMaxDevices] = {};
+  std::mutex mu_;
+};
+
+// The current device, or -1.
+inline int current_device() {
+  int dev = -1;
+  return cudaGetDevice(&dev) == cudaSuccess && dev >= 0 && dev < kMaxDevices ? dev : -1;
+}
 
 // Multiprocessor count of `dev` (cached; 148 on B200).
 int num_sms(int dev);
@@ -36,7 +69,7 @@ int a_shape_n_init(int N, int n_block, double ratio, int is_global);
 int a_shape_mask(int N, int m_block, int n_block, int n_init, int with_diag, uint8_t* mask);
 size_t sparse_attn_workspace_size(int n_seq, int heads, int win);
 int sparse_attn_fwd(const void* qkv, int64_t ld_qkv, int n_seq, int heads, int win, int d, const void* rel_pos_h,
-                    const void* rel_pos_w, const int32_t* perm, int n_init_blocks, int with_diag, float scale,
+                    const void* rel_pos_w, const int32_t* perm, int n_init_blocks, int n_block, int with_diag, float scale,
                     void* out, int64_t ld_out, const int32_t* out_rows, void* workspace, size_t workspace_bytes,
                     cudaStream_t stream);
 int layernorm_gather(const float* x, int64_t ldx, const int32_t* src_rows, int n_rows, int C, const float* w,

@@ -362,13 +362,12 @@ __global__ void stripe_sort_kernel(const StripeArgs a) {
 
 template <int GS, int CH>
 static int launch_stripe(const StripeArgs& a, int rows, int threads, size_t smem, cudaStream_t stream) {
-  static bool configured = false;
-  if (!configured) {
-    if (cudaFuncSetAttribute(stripe_sort_kernel<GS, CH>, cudaFuncAttributeMaxDynamicSharedMemorySize, 160 * 1024) !=
-        cudaSuccess)
-      return SSAM_ERR_CUDA;
-    configured = true;
-  }
+  static PerDeviceOnce configured;
+  const int st = configured.run(current_device(), [] {
+    return status_from_cuda(
+        cudaFuncSetAttribute(stripe_sort_kernel<GS, CH>, cudaFuncAttributeMaxDynamicSharedMemorySize, 160 * 1024));
+  });
+  if (st != SSAM_OK) return st;
   stripe_sort_kernel<GS, CH><<<rows, threads, smem, stream>>>(a);
   return status_from_cuda(cudaGetLastError());
 }
@@ -438,13 +437,12 @@ int keep_select(const int32_t* inv_perm_group, int B, int heads, int N, int keep
   if (inv_perm_group == nullptr || idx == nullptr) return SSAM_ERR_INVALID;
   if (B <= 0 || heads <= 0 || N <= 0 || keep_n <= 0 || keep_n > N) return SSAM_ERR_INVALID;
   if (N > kMaxTokens) return SSAM_ERR_UNSUPPORTED;
-  static bool configured = false;
-  if (!configured) {
-    if (cudaFuncSetAttribute(keep_select_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             kMaxTokens * sizeof(uint64_t)) != cudaSuccess)
-      return SSAM_ERR_CUDA;
-    configured = true;
-  }
+  static PerDeviceOnce configured;
+  const int st = configured.run(current_device(), [] {
+    return status_from_cuda(cudaFuncSetAttribute(keep_select_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                 kMaxTokens * sizeof(uint64_t)));
+  });
+  if (st != SSAM_OK) return st;
   const int slices = N >= 4096 ? 4 : (N >= 1024 ? 2 : 1);
   keep_select_kernel<<<dim3(B, slices), 1024, N * sizeof(uint64_t), stream>>>(inv_perm_group, heads, N, keep_n, idx,
                                                                               rows);

@@ -59,13 +59,15 @@ def _rowmajor(t: torch.Tensor, name: str) -> int:
 
 def gemm_bf16(a: torch.Tensor, b: torch.Tensor, bias: torch.Tensor | None = None, *,
               epilogue: int = SSAM_EPI_BF16, out: torch.Tensor | None = None,
-              out_rows: torch.Tensor | None = None) -> torch.Tensor:
+              out_rows: torch.Tensor | None = None, k_split: int = 1) -> torch.Tensor:
     """acc = a @ b.T (a: M x K bf16, b: N x K bf16) with a fused epilogue.
 
     SSAM_EPI_BF16 / SSAM_EPI_GELU_BF16 write bf16 `out` (M x N, allocated when
     None), SSAM_EPI_F32 fp32 `out`; SSAM_EPI_ADD_F32 accumulates into the fp32
     `out`. With `out_rows` (int32) accumulator row r goes to out[out_rows[r]]
-    (-1 skips the row) for every epilogue.
+    (-1 skips the row) for every epilogue. `k_split` > 1 marks a GEMM whose K
+    holds that many terms of one product (the fp32-accurate [hi | lo | hi]
+    split): its algorithmic work, as KernelTimer records it, is 2*M*N*K/k_split.
     """
     _check_cuda(a, b, bias, out, out_rows)
     if a.dtype != torch.bfloat16 or b.dtype != torch.bfloat16:
@@ -98,7 +100,7 @@ def gemm_bf16(a: torch.Tensor, b: torch.Tensor, bias: torch.Tensor | None = None
     t0 = KernelTimer.begin()
     _lib.call("ssam_gemm_bf16", a.data_ptr(), lda, b.data_ptr(), ldb, M, N, K, _ptr(bias), epilogue,
               out.data_ptr(), ldo, _ptr(out_rows), _stream(a))
-    KernelTimer.end(t0, "gemm", 2.0 * M * N * K)
+    KernelTimer.end(t0, "gemm", 2.0 * M * N * K / k_split)
     return out
 
 
@@ -199,9 +201,11 @@ def keep_select(inv_perm_group: torch.Tensor, B: int, heads: int, keep_n: int):
 # ---------------------------------------------------------------------------
 def sparse_attn(qkv: torch.Tensor, n_seq: int, heads: int, win: int, d: int, rel_pos_h: torch.Tensor,
                 rel_pos_w: torch.Tensor, perm: torch.Tensor, n_init_blocks: int, with_diag: bool, scale: float,
-                out: torch.Tensor | None = None, out_rows: torch.Tensor | None = None) -> torch.Tensor:
+                out: torch.Tensor | None = None, out_rows: torch.Tensor | None = None,
+                n_block: int = 64) -> torch.Tensor:
     """Block-sparse attention of every (sequence, head) row; output in raster order (n_seq*N, heads*d),
-    or, with `out_rows` (int32 [n_seq*N], -1 skips), (sequence, token) written to row out_rows[s*N + t]."""
+    or, with `out_rows` (int32 [n_seq*N], -1 skips), (sequence, token) written to row out_rows[s*N + t].
+    The A-shape mask is defined on n_block-token blocks (64 or 128)."""
     _check_cuda(qkv, rel_pos_h, rel_pos_w, perm, out, out_rows)
     if qkv.dtype != torch.bfloat16 or rel_pos_h.dtype != torch.bfloat16 or rel_pos_w.dtype != torch.bfloat16:
         raise TypeError("qkv and rel-pos tables must be bf16")
@@ -223,10 +227,10 @@ def sparse_attn(qkv: torch.Tensor, n_seq: int, heads: int, win: int, d: int, rel
     ws = torch.empty(ws_bytes, dtype=torch.uint8, device=qkv.device) if ws_bytes else None
     t0 = KernelTimer.begin()
     _lib.call("ssam_sparse_attn_fwd", qkv.data_ptr(), ld, n_seq, heads, win, d, rel_pos_h.data_ptr(),
-              rel_pos_w.data_ptr(), perm.data_ptr(), n_init_blocks, 1 if with_diag else 0, float(scale),
+              rel_pos_w.data_ptr(), perm.data_ptr(), n_init_blocks, n_block, 1 if with_diag else 0, float(scale),
               out.data_ptr(), ld_out, _ptr(out_rows), _ptr(ws), ws_bytes, _stream(qkv), launches=2 if ws_bytes else 1)
     KernelTimer.end(t0, "attention_global" if ws_bytes else "attention_window",
-                    attention_flops(n_seq * heads, N, d, n_init_blocks, with_diag))
+                    attention_flops(n_seq * heads, N, d, n_init_blocks, with_diag, n_block))
     return out
 
 
@@ -236,8 +240,7 @@ def attention_flops(rows: int, N: int, d: int, n_init: int, with_diag: bool, blo
     pairs = 0
     for m in range(nb):
         q = min(block, N - m * block)
-        keys = min(n_init, nb) * block
-        keys = min(keys, N)
+        keys = min(min(n_init, nb) * block, N)
         if with_diag and m >= n_init:
             keys += min(block, N - m * block)
         pairs += q * keys

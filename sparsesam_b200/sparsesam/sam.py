@@ -170,7 +170,7 @@ def _attention_core(attn, xn: torch.Tensor, n_seq: int, win: int, ratio: float, 
     perm, inv_perm, _ = _get_perm(info, (win, ratio, n_block, perm_mode), qkv, n_seq, heads, win, d)
     n_init = ops.a_shape_n_init(N, n_block, ratio, is_global)          # sam.py:219-223
     o = ops.sparse_attn(qkv, n_seq, heads, win, d, w.rel_h, w.rel_w, perm, n_init, is_global,
-                        attn.scale, out=out, out_rows=out_rows)         # sam.py:206-232
+                        attn.scale, out=out, out_rows=out_rows, n_block=n_block)   # sam.py:206-232
     return o, perm, inv_perm
 
 
@@ -184,8 +184,8 @@ class ToMeSAMAttention(Attention):
                 m_block: int = _FA2_M_BLOCK_LOCAL, n_block: int = _FA2_N_BLOCK_LOCAL,
                 threads: int = _FA2_THREADS_LOCAL, is_global: bool = False, return_perm: bool = False):
         _require_cuda(x)
-        if m_block != 64 or n_block != 64:
-            raise NotImplementedError("the block mask is defined on 64-token blocks (sam.py:52-55)")
+        if m_block != n_block or n_block not in (64, 128):
+            raise NotImplementedError("the block mask is defined on equal query / key blocks of 64 or 128 tokens")
         B, H, W, C = x.shape
         if H != W:
             raise ValueError("SparseSAM attention expects square token grids")
@@ -339,9 +339,9 @@ def encoder_forward(enc, img: torch.Tensor):
     x = torch.empty(B * T, C, dtype=torch.float32, device=img.device)
     if w.pos is not None:
         ops.broadcast_rows(w.pos, B, x)
-        ops.gemm_bf16(cols, w.patch_w, w.patch_b, epilogue=ops.SSAM_EPI_ADD_F32, out=x)
+        ops.gemm_bf16(cols, w.patch_w, w.patch_b, epilogue=ops.SSAM_EPI_ADD_F32, out=x, k_split=3)
     else:
-        ops.gemm_bf16(cols, w.patch_w, w.patch_b, epilogue=ops.SSAM_EPI_F32, out=x)
+        ops.gemm_bf16(cols, w.patch_w, w.patch_b, epilogue=ops.SSAM_EPI_F32, out=x, k_split=3)
     interm = []
     n_blocks = len(enc.blocks)
     pending = None  # the snapshot of x after a global block, written by the next block's norm1
@@ -356,10 +356,10 @@ def encoder_forward(enc, img: torch.Tensor):
                 pending = torch.empty_like(x)
                 interm.append(pending.view(B, gh, gw, C))
     # neck: fp32 activations and weights through the 3-term split (3x K)
-    y = ops.gemm_bf16(ops.split_bf16x3(x), w.neck0_w, None, epilogue=ops.SSAM_EPI_F32)
+    y = ops.gemm_bf16(ops.split_bf16x3(x), w.neck0_w, None, epilogue=ops.SSAM_EPI_F32, k_split=3)
     ya = ops.layernorm_rows(y, w.ln_a_w, w.ln_a_b, w.eps_a, out_bf16=False)
     cols3 = ops.im2col3x3_nhwc(ops.split_bf16x3(ya).view(B, gh, gw, -1))
-    z = ops.gemm_bf16(cols3, w.neck2_w, None, epilogue=ops.SSAM_EPI_F32)
+    z = ops.gemm_bf16(cols3, w.neck2_w, None, epilogue=ops.SSAM_EPI_F32, k_split=3)
     z = ops.layernorm_rows(z, w.ln_b_w, w.ln_b_b, w.eps_b, out_bf16=False)
     feats = ops.nhwc_to_nchw(z, B, gh, gw, z.shape[1])
     return feats, interm

@@ -102,3 +102,78 @@ def test_out_rows_places_rows(cuda_device):
     keep = dst >= 0
     assert torch.equal(out[dst[keep].long()], base[keep])
     assert ops.device_error() == 0
+
+
+def _config1_inputs(cuda_device):
+    """B=8, heads=16, N=4096 (64x64), d=64, Q/K/V ~ N(0, 1) from
+    seed 1, rel-pos tables (127, 64) ~ N(0, 0.02), bf16; the permutation is
+    Stripe-Sort (z_interleave_sort) of the same K, as sam.py:193-209 derives it."""
+    B, heads, win, d = 8, 16, 64, 64
+    N, C = win * win, heads * d
+    g = torch.Generator().manual_seed(1)
+    qkv = torch.randn(B * N, 3 * C, generator=g).to(torch.bfloat16).to(cuda_device)
+    th = (torch.randn(2 * win - 1, d, generator=g) * 0.02).to(torch.bfloat16).to(cuda_device)
+    tw = (torch.randn(2 * win - 1, d, generator=g) * 0.02).to(torch.bfloat16).to(cuda_device)
+    base = ops.zorder(win, win, cuda_device)[0]
+    perm, _, _ = ops.stripe_sort_perm(qkv[:, C:], B, heads, win, win, d, base, ld=qkv.stride(0))
+    return qkv, th, tw, perm, (B, heads, win, d)
+
+
+@pytest.mark.parametrize("n_block", [64, 128])
+def test_config1_shape_stripe_sort_perms(cuda_device, n_block):
+    """Config 1's exact shape on Stripe-Sort permutations of the same K, at
+    densities 0.3 / 0.4 / 0.5 and the dense control, with the reference's 64-token
+    mask and the 128-token mask BASELINE names. Every row runs on the GPU; rows
+    sampled across images and heads are compared with the fp32 oracle on the same
+    bf16 values, and their permutations with the oracle's Stripe-Sort (bit-exact)."""
+    qkv, th, tw, perm, (B, heads, win, d) = _config1_inputs(cuda_device)
+    N, C = win * win, heads * d
+    sample = [0, 77, 127]   # (image, head) rows: b * heads + h
+    qkv_c = qkv.float().cpu().view(B, N, 3, heads, d)
+    perm_c = perm.cpu()
+    for r in sample:
+        b, h = divmod(r, heads)
+        k_row = qkv_c[b, :, 1, h].numpy()[None]
+        p_ref, _, _ = order.stripe_sort(k_row, win, win)
+        assert (perm_c[r].numpy() == p_ref[0]).all(), f"row {r}: Stripe-Sort permutation differs"
+    for ratio in (0.3, 0.4, 0.5, 1.0):
+        n_init = order.a_shape_n_init(N, n_block, ratio, True)
+        out = ops.sparse_attn(qkv, B, heads, win, d, th, tw, perm, n_init, True, d ** -0.5, n_block=n_block)
+        assert ops.device_error() == 0
+        out_c = out.float().cpu().view(B, N, heads, d)
+        for r in sample:
+            b, h = divmod(r, heads)
+            q, k, v = (qkv_c[b, :, i, h][None] for i in range(3))
+            ref = sparse_attention(q, k, v, th.float().cpu(), tw.float().cpu(), perm_c[r][None], win, n_init, True,
+                                   d ** -0.5, m_block=n_block, n_block=n_block, round_tables_fp16=False)[0]
+            err = (out_c[b, :, h] - ref).abs()
+            assert err.max().item() < 3e-2, (ratio, r, err.max().item())
+            assert err.mean().item() < 3e-3, (ratio, r, err.mean().item())
+
+
+@pytest.mark.parametrize("d", [64, 80])
+@pytest.mark.parametrize("win,is_global", [(14, False), (64, True), (16, True)])
+@pytest.mark.parametrize("ratio", [0.3, 0.5])
+def test_128_token_mask_blocks(cuda_device, d, win, is_global, ratio):
+    """The A-shape mask on 128-token blocks (n_block = 128): the keep bar in
+    128-token units and, for global grids, whole 128-token diagonal blocks."""
+    g = torch.Generator().manual_seed(9)
+    n_seq, heads = 2, 2
+    N, C = win * win, heads * d
+    qkv = torch.randn(n_seq * N, 3 * C, generator=g).to(torch.bfloat16)
+    th = (torch.randn(2 * win - 1, d, generator=g) * 0.3).to(torch.bfloat16)
+    tw = (torch.randn(2 * win - 1, d, generator=g) * 0.3).to(torch.bfloat16)
+    perm = torch.stack([torch.randperm(N, generator=g) for _ in range(n_seq * heads)]).to(torch.int32)
+    n_init = order.a_shape_n_init(N, 128, ratio, is_global)
+    if n_init == 0 and not is_global:
+        pytest.skip("no key block enabled")
+    out = ops.sparse_attn(qkv.to(cuda_device), n_seq, heads, win, d, th.to(cuda_device), tw.to(cuda_device),
+                          perm.to(cuda_device), n_init, is_global, d ** -0.5, n_block=128)
+    q, k, v = qkv.float().view(n_seq, N, 3, heads, d).permute(2, 0, 3, 1, 4).reshape(3, n_seq * heads, N, d)
+    ref = sparse_attention(q, k, v, th.float(), tw.float(), perm, win, n_init, is_global, d ** -0.5,
+                           m_block=128, n_block=128, round_tables_fp16=False)
+    ref = ref.view(n_seq, heads, N, d).permute(0, 2, 1, 3).reshape(n_seq * N, C)
+    err = (out.float().cpu() - ref).abs()
+    assert err.max().item() < 3e-2, err.max().item()
+    assert err.mean().item() < 3e-3
+    assert ops.device_error() == 0

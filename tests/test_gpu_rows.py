@@ -42,6 +42,7 @@ def test_rc_mlp(cuda_device, keep):
     w2 = (torch.randn(C, Hd, device=cuda_device) * 0.05).to(torch.bfloat16)
     b2 = torch.randn(C, device=cuda_device) * 0.1
     rows = torch.randperm(n_tok, device=cuda_device)[:2458].to(torch.int32) if keep else None
+    x0 = x.clone()
     ref = x.clone()
     sel = rows.long() if keep else torch.arange(n_tok, device=cuda_device)
     xs = ref[sel]
@@ -50,11 +51,11 @@ def test_rc_mlp(cuda_device, keep):
     ops.rc_mlp(x, rows, sel.numel(), ln_w, ln_b, 1e-6, w1, b1, w2, b2)
     err = (x - ref).abs().max().item()
     assert err < 3e-2, err
-    if keep:   # rows outside the keep set pass through unchanged
-        mask = torch.ones(n_tok, dtype=torch.bool, device=cuda_device)
-        mask[sel] = False
-        untouched = torch.randn(0)
-        del untouched
+    if keep:   # rows outside the keep set pass through unchanged, bit for bit (sam.py:284-288)
+        skipped = torch.ones(n_tok, dtype=torch.bool, device=cuda_device)
+        skipped[sel] = False
+        assert int(skipped.sum()) == n_tok - 2458
+        assert torch.equal(x[skipped], x0[skipped])
 
 
 def test_patch_embed_im2col(cuda_device):

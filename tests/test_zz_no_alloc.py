@@ -71,6 +71,41 @@ def test_no_alloc_matches_workspace_entry_two_calls(cuda_device):
     assert lib.ssam_device_error(1) == 0
 
 
+def test_no_alloc_allocates_nothing(cuda_device):
+    """After a first call (which resolves the scratch address), further calls leave
+    the device's free memory and torch's allocator exactly as they were."""
+    lib = _lib.load()
+    stream = torch.cuda.current_stream(cuda_device).cuda_stream
+    x, *rest = _inputs(13, cuda_device)
+    _no_alloc(lib, x, *rest, stream)
+    torch.cuda.synchronize()
+    free0, _ = torch.cuda.mem_get_info(cuda_device)
+    reserved0 = torch.cuda.memory_reserved(cuda_device)
+    for _ in range(3):
+        _no_alloc(lib, x, *rest, stream)
+    torch.cuda.synchronize()
+    free1, _ = torch.cuda.mem_get_info(cuda_device)
+    assert free1 == free0
+    assert torch.cuda.memory_reserved(cuda_device) == reserved0
+    assert lib.ssam_device_error(1) == 0
+
+
+def test_no_alloc_rejects_a_stream_of_another_device(cuda_device):
+    """The scratch address belongs to the current device; a stream created on
+    another device is refused before anything is enqueued."""
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two devices")
+    lib = _lib.load()
+    other = torch.cuda.Stream(device=1)
+    x, *rest = _inputs(14, cuda_device, n_rows=64)
+    with torch.cuda.device(cuda_device):
+        C, Hd = x.shape[1], rest[3].shape[0]
+        st = lib.ssam_rc_mlp_fwd_noalloc(x.data_ptr(), C, rest[0].data_ptr(), 64, C, Hd, rest[1].data_ptr(),
+                                         rest[2].data_ptr(), 1e-6, rest[3].data_ptr(), rest[4].data_ptr(),
+                                         rest[5].data_ptr(), rest[6].data_ptr(), other.cuda_stream)
+    assert st == _lib.SSAM_ERR_INVALID
+
+
 def test_no_alloc_rejects_oversized_calls(cuda_device):
     lib = _lib.load()
     # 4096 rows x (1280 + 5120) x 2 B = 50 MiB > the 32 MiB scratch
