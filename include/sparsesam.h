@@ -148,6 +148,20 @@ int ssam_keep_select(const int32_t* inv_perm_group, int B, int heads, int N, int
                      int32_t* rows, void* stream);
 
 /* ---------------------------------------------------------------------------
+ * Static keep set of the SAM3 MLP-merge variant. Replaces
+ * algos/sparsesam/sam3.py:49-71 (_get_keep_indices), as used by
+ * ToMeSAM3Block.forward (sam3.py:96-109).
+ * ssam_zstride_keep_n returns keep_n = min(max(1, round(ratio*N)), N) (Python
+ * round: ties to even), or -1 when ratio is outside (0, 1].
+ * ssam_zstride_keep writes idx[i] (i < keep_n) = the raster index of the token
+ * at Morton position rint(f32(i) * f32(N / keep_n)) (clamped to [0, N)) of the
+ * H x W grid, and, when rows != NULL, rows[b*keep_n + i] = b*H*W + idx[i] for
+ * b < B (the row map ssam_rc_mlp_fwd takes).
+ * ------------------------------------------------------------------------- */
+int ssam_zstride_keep_n(int N, double ratio);
+int ssam_zstride_keep(int H, int W, int keep_n, int B, int32_t* idx, int32_t* rows, void* stream);
+
+/* ---------------------------------------------------------------------------
  * a9 / a10 data movement. Row-gathered LayerNorm:
  *   out[r, :] = bf16(LN(x[src_rows[r], :]) * w + b), or 0 when src_rows[r] < 0.
  * src_rows == NULL means identity. Covers norm1 + window_partition (sam.py:248,

@@ -1,5 +1,5 @@
 """SparseSAM-patched SAM ViT image encoder, restated in torch fp32 on CPU —
-test infrastructure only.
+test infrastructure only. Also the SAM3 MLP-merge block (sam3_block).
 
 Restates the reference's patched forward (algos/sparsesam/sam.py:371-380 for the
 per-forward cache, :242-290 for ToMeSAMBlock.forward, :168-236 for
@@ -109,6 +109,24 @@ def _ln2d(x, w, b, eps=1e-6):
     return w[:, None, None] * ((x - mu) / torch.sqrt(var + eps)) + b[:, None, None]
 
 
+def _stem(enc, img):
+    x = F.conv2d(img.float(), enc.patch_embed.proj.weight.float(), enc.patch_embed.proj.bias.float(),
+                 stride=enc.patch_embed.proj.stride)
+    x = x.permute(0, 2, 3, 1)
+    if enc.pos_embed is not None:
+        x = x + enc.pos_embed.float()
+    return x
+
+
+def _neck(enc, x):
+    n = enc.neck
+    y = x.permute(0, 3, 1, 2)
+    y = F.conv2d(y, n[0].weight.float())
+    y = _ln2d(y, n[1].weight.float(), n[1].bias.float())
+    y = F.conv2d(y, n[2].weight.float(), padding=1)
+    return _ln2d(y, n[3].weight.float(), n[3].bias.float())
+
+
 @torch.no_grad()
 def encoder_forward(enc, img, ratio: float, mlp_merge: bool = True, perm_mode: str = "z_interleave_sort",
                     forced_perms=None, return_state: bool = False):
@@ -116,11 +134,7 @@ def encoder_forward(enc, img, ratio: float, mlp_merge: bool = True, perm_mode: s
 
     state = {"perm_cache": {...}, "keep": [idx per sparse-MLP block]}.
     """
-    x = F.conv2d(img.float(), enc.patch_embed.proj.weight.float(), enc.patch_embed.proj.bias.float(),
-                 stride=enc.patch_embed.proj.stride)
-    x = x.permute(0, 2, 3, 1)
-    if enc.pos_embed is not None:
-        x = x + enc.pos_embed.float()
+    x = _stem(enc, img)
     perm_cache: dict = {}
     keep_log: list = []
     interm = []
@@ -128,12 +142,44 @@ def encoder_forward(enc, img, ratio: float, mlp_merge: bool = True, perm_mode: s
         x = block(blk, x, ratio, perm_cache, perm_mode, mlp_merge, forced_perms, keep_log)
         if blk.window_size == 0:
             interm.append(x)
-    n = enc.neck
-    y = x.permute(0, 3, 1, 2)
-    y = F.conv2d(y, n[0].weight.float())
-    y = _ln2d(y, n[1].weight.float(), n[1].bias.float())
-    y = F.conv2d(y, n[2].weight.float(), padding=1)
-    y = _ln2d(y, n[3].weight.float(), n[3].bias.float())
+    y = _neck(enc, x)
     if return_state:
         return y, interm, {"perm_cache": perm_cache, "keep": keep_log}
     return y, interm
+
+
+def sam3_block(blk, x, ratio: float, mlp_merge: bool = True):
+    """ToMeSAM3Block.forward restated (algos/sparsesam/sam3.py:83-109): the stock
+    attention on every token (the block's own attention module, fp32), then the
+    MLP on the static Z-stride keep set only (sam3.py:49-71); the other tokens keep
+    the residual. x: (B, H, W, C) fp32."""
+    B, H, W, C = x.shape
+    shortcut = x
+    xn = _ln(x, blk.norm1.weight.float(), blk.norm1.bias.float(), blk.norm1.eps)
+    if blk.window_size > 0:
+        ws = blk.window_size
+        xw, pad_hw = _window_partition(xn, ws)
+        xa = _window_unpartition(blk.attn(xw), ws, pad_hw, (H, W))
+    else:
+        xa = blk.attn(xn)
+    x = shortcut + xa
+    eps2 = blk.norm2.eps
+    if mlp_merge and ratio < 1.0:
+        idx = torch.from_numpy(order.zstride_keep(H, W, ratio))
+        xs = x.reshape(B, H * W, C).clone()
+        kept = xs[:, idx]
+        xs[:, idx] = kept + _mlp(blk, _ln(kept, blk.norm2.weight.float(), blk.norm2.bias.float(), eps2))
+        return xs.reshape(B, H, W, C)
+    return x + _mlp(blk, _ln(x, blk.norm2.weight.float(), blk.norm2.bias.float(), eps2))
+
+
+@torch.no_grad()
+def sam3_encoder_forward(enc, img, ratio: float, mlp_merge: bool = True):
+    """An encoder with every block patched as ToMeSAM3Block: (features, interm_embeddings)."""
+    x = _stem(enc, img)
+    interm = []
+    for blk in enc.blocks:
+        x = sam3_block(blk, x, ratio, mlp_merge)
+        if blk.window_size == 0:
+            interm.append(x)
+    return _neck(enc, x), interm

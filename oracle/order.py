@@ -160,3 +160,15 @@ def keep_select(inv_perm_group: np.ndarray, B: int, heads: int, keep_n: int) -> 
 def keep_n_for(ratio: float, N: int) -> int:
     """keep_n = max(1, round(ratio * N)) (sam.py:277; Python round-half-even)."""
     return max(1, round(ratio * N))
+
+
+def zstride_keep(H: int, W: int, ratio: float) -> np.ndarray:
+    """Static keep set of the SAM3 MLP-merge variant (algos/sparsesam/sam3.py:49-71):
+    keep_n = min(max(1, round(ratio N)), N) Morton positions at a uniform stride,
+    pos_i = round(float32(i) * float32(N / keep_n)) (ties to even, as torch.round),
+    clamped to [0, N - 1], mapped to raster indices through the Morton order. int64."""
+    N = H * W
+    keep_n = min(max(1, round(ratio * N)), N)
+    zperm = zorder(H, W)[0]
+    pos = np.rint(np.arange(keep_n, dtype=np.float32) * np.float32(N / keep_n)).astype(np.int64)
+    return zperm[np.clip(pos, 0, N - 1)]

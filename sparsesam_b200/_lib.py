@@ -34,6 +34,8 @@ SIGNATURES: dict[str, tuple] = {
     "ssam_sparse_attn_fwd": (c_int, [c_ptr, c_i64, c_int, c_int, c_int, c_int, c_ptr, c_ptr, c_ptr,
                                      c_int, c_int, c_int, c_f32, c_ptr, c_i64, c_ptr, c_ptr, c_size, c_ptr]),
     "ssam_keep_select": (c_int, [c_ptr, c_int, c_int, c_int, c_int, c_ptr, c_ptr, c_ptr]),
+    "ssam_zstride_keep_n": (c_int, [c_int, c_f64]),
+    "ssam_zstride_keep": (c_int, [c_int, c_int, c_int, c_int, c_ptr, c_ptr, c_ptr]),
     "ssam_layernorm_gather": (c_int, [c_ptr, c_i64, c_ptr, c_int, c_int, c_ptr, c_ptr, c_f32, c_ptr, c_i64,
                                       c_ptr]),
     "ssam_window_rows": (c_int, [c_int, c_int, c_int, c_int, c_ptr, c_ptr]),
@@ -80,6 +82,7 @@ KERNELS_PER_CALL = {
     "ssam_patch_im2col": 1, "ssam_broadcast_rows": 1, "ssam_im2col3x3_nhwc": 1, "ssam_nhwc_to_nchw": 1,
     "ssam_layernorm_rows": 1, "ssam_layernorm_rows_copy": 1, "ssam_split_bf16x2": 1, "ssam_rc_mlp_fwd_noalloc": 3,
     "ssam_split_bf16x3": 1, "ssam_patch_im2col_split3": 1, "ssam_window_of_raster": 1, "ssam_fill_pad_rows": 1,
+    "ssam_zstride_keep": 1,
 }
 launch_count = 0  # kernels enqueued through call() since import (read by bench.py)
 

@@ -108,6 +108,12 @@ int ssam_keep_select(const int32_t* inv_perm_group, int B, int heads, int N, int
   return ssam::keep_select(inv_perm_group, B, heads, N, keep_n, idx, rows, static_cast<cudaStream_t>(stream));
 }
 
+int ssam_zstride_keep_n(int N, double ratio) { return ssam::zstride_keep_n(N, ratio); }
+
+int ssam_zstride_keep(int H, int W, int keep_n, int B, int32_t* idx, int32_t* rows, void* stream) {
+  return ssam::zstride_keep(H, W, keep_n, B, idx, rows, static_cast<cudaStream_t>(stream));
+}
+
 int ssam_layernorm_gather(const float* x, int64_t ldx, const int32_t* src_rows, int n_rows, int C, const float* w,
                           const float* b, float eps, void* out, int64_t ld_out, void* stream) {
   return ssam::layernorm_gather(x, ldx, src_rows, n_rows, C, w, b, eps, out, ld_out, static_cast<cudaStream_t>(stream));

@@ -66,6 +66,8 @@ int stripe_sort_perm(const void* k, int64_t ld, int n_seq, int heads, int H, int
 int keep_select(const int32_t* inv_perm_group, int B, int heads, int N, int keep_n, int32_t* idx, int32_t* rows,
                 cudaStream_t stream);
 int a_shape_n_init(int N, int n_block, double ratio, int is_global);
+int zstride_keep_n(int N, double ratio);
+int zstride_keep(int H, int W, int keep_n, int B, int32_t* idx, int32_t* rows, cudaStream_t stream);
 int a_shape_mask(int N, int m_block, int n_block, int n_init, int with_diag, uint8_t* mask);
 size_t sparse_attn_workspace_size(int n_seq, int heads, int win);
 int sparse_attn_fwd(const void* qkv, int64_t ld_qkv, int n_seq, int heads, int win, int d, const void* rel_pos_h,

@@ -459,6 +459,61 @@ int a_shape_n_init(int N, int n_block, double ratio, int is_global) {
   return is_global ? n_keep : n_keep + 1;
 }
 
+// ---------------------------------------------------------------------------
+// Static Z-stride keep set of the SAM3 MLP-merge variant
+// (algos/sparsesam/sam3.py:49-71 _get_keep_indices): keep_n = min(max(1,
+// round(ratio N)), N) Morton positions pos_i = rint(f32(i) * f32(N / keep_n))
+// (fp32 product, ties to even, as torch.arange(float32) * (N / keep_n) and
+// torch.round), clamped to [0, N), and idx[i] = the raster cell at Morton
+// position pos_i. One thread per raster cell finds its Morton rank q (number
+// of smaller keys) and stores itself at the i whose position is q; positions
+// strictly increase with i (N / keep_n >= 1), so at most one i matches.
+// ---------------------------------------------------------------------------
+int zstride_keep_n(int N, double ratio) {
+  if (N <= 0 || !(ratio > 0.0) || ratio > 1.0) return -1;
+  double k = nearbyint(ratio * N);  // Python round(): ties to even (default rounding mode)
+  if (k < 1.0) k = 1.0;
+  return k > N ? N : static_cast<int>(k);
+}
+
+__device__ __forceinline__ int zstride_pos(int i, float step, int N) {
+  const int p = static_cast<int>(rintf(__fmul_rn(static_cast<float>(i), step)));
+  return p < 0 ? 0 : (p > N - 1 ? N - 1 : p);
+}
+
+__global__ void zstride_keep_kernel(int H, int W, int num_bits, int keep_n, float step, int B, int32_t* idx,
+                                    int32_t* rows) {
+  const int N = H * W;
+  const int cell = blockIdx.x * blockDim.x + threadIdx.x;
+  if (cell >= N) return;
+  const uint32_t kc = morton_key(cell / W, cell % W, num_bits);
+  int q = 0;
+  for (int j = 0; j < N; ++j) q += morton_key(j / W, j % W, num_bits) < kc;
+  // candidates around q / step; pos is strictly increasing in i
+  const int i0 = static_cast<int>(static_cast<double>(q) / static_cast<double>(step));
+  for (int i = i0 - 2; i <= i0 + 2; ++i) {
+    if (i < 0 || i >= keep_n || zstride_pos(i, step, N) != q) continue;
+    idx[i] = cell;
+    if (rows != nullptr)
+      for (int b = 0; b < B; ++b) rows[static_cast<int64_t>(b) * keep_n + i] = b * N + cell;
+  }
+}
+
+int zstride_keep(int H, int W, int keep_n, int B, int32_t* idx, int32_t* rows, cudaStream_t stream) {
+  if (H <= 0 || W <= 0 || idx == nullptr || B < 0 || (rows != nullptr && B <= 0)) return SSAM_ERR_INVALID;
+  const int N = H * W;
+  if (N > kMaxTokens) return SSAM_ERR_UNSUPPORTED;
+  if (keep_n < 1 || keep_n > N) return SSAM_ERR_INVALID;
+  if (rows != nullptr && static_cast<int64_t>(B) * N > INT32_MAX) return SSAM_ERR_UNSUPPORTED;
+  int m = H > W ? H : W;
+  int num_bits = 0;
+  while ((1 << num_bits) < m) ++num_bits;  // ceil(log2(m)), z_utils.py:71
+  if (num_bits < 1) num_bits = 1;
+  const float step = static_cast<float>(static_cast<double>(N) / keep_n);  // Python float N / keep_n, then fp32
+  zstride_keep_kernel<<<(N + 255) / 256, 256, 0, stream>>>(H, W, num_bits, keep_n, step, B, idx, rows);
+  return status_from_cuda(cudaGetLastError());
+}
+
 int a_shape_mask(int N, int m_block, int n_block, int n_init, int with_diag, uint8_t* mask) {
   if (N <= 0 || m_block <= 0 || n_block <= 0 || mask == nullptr) return SSAM_ERR_INVALID;
   const int num_m = (N + m_block - 1) / m_block, num_n = (N + n_block - 1) / n_block;

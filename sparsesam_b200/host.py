@@ -224,24 +224,26 @@ VIT_CONFIGS = {
 
 
 def _trunc_normal_(t: torch.Tensor, std: float, gen: torch.Generator) -> None:
-    # N(0, std) truncated at +-2 std, drawn by rejection with an explicit generator.
+    # N(0, std) truncated at +-2 std, drawn by rejection with an explicit (CPU)
+    # generator and copied to t's device, so a seed gives the same values on any device.
     with torch.no_grad():
         flat = t.view(-1)
         n = flat.numel()
         filled = 0
         while filled < n:
-            draw = torch.randn(max(1024, int((n - filled) * 1.06)), generator=gen, device=t.device) * std
+            draw = torch.randn(max(1024, int((n - filled) * 1.06)), generator=gen, device=gen.device) * std
             draw = draw[draw.abs() <= 2 * std][: n - filled]
-            flat[filled:filled + draw.numel()] = draw.to(t.dtype)
+            flat[filled:filled + draw.numel()] = draw.to(device=t.device, dtype=t.dtype)
             filled += draw.numel()
 
 
 def init_weights(model: nn.Module, seed: int = 0) -> nn.Module:
     """Seeded random init used by every configuration of this build:
     trunc-normal(0.02) for Linear/Conv weights and pos_embed, zero biases,
-    LayerNorm weight 1 / bias 0, rel-pos tables N(0, 0.02)."""
+    LayerNorm weight 1 / bias 0, rel-pos tables N(0, 0.02). Values are drawn on
+    the CPU whatever the model's device, so a seed names the same weights everywhere."""
     dev = next(model.parameters()).device
-    gen = torch.Generator(device=dev).manual_seed(seed)
+    gen = torch.Generator(device="cpu").manual_seed(seed)
     with torch.no_grad():
         for name, mod in model.named_modules():
             if isinstance(mod, (nn.Linear, nn.Conv2d)):
@@ -252,8 +254,8 @@ def init_weights(model: nn.Module, seed: int = 0) -> nn.Module:
                 mod.weight.fill_(1.0)
                 mod.bias.zero_()
             if isinstance(mod, Attention) and mod.use_rel_pos:
-                mod.rel_pos_h.copy_(torch.randn(mod.rel_pos_h.shape, generator=gen, device=dev) * 0.02)
-                mod.rel_pos_w.copy_(torch.randn(mod.rel_pos_w.shape, generator=gen, device=dev) * 0.02)
+                mod.rel_pos_h.copy_((torch.randn(mod.rel_pos_h.shape, generator=gen) * 0.02).to(dev))
+                mod.rel_pos_w.copy_((torch.randn(mod.rel_pos_w.shape, generator=gen) * 0.02).to(dev))
         if getattr(model, "pos_embed", None) is not None:
             _trunc_normal_(model.pos_embed, 0.02, gen)
     return model

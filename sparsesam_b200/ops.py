@@ -196,6 +196,26 @@ def keep_select(inv_perm_group: torch.Tensor, B: int, heads: int, keep_n: int):
     return idx, rows
 
 
+def zstride_keep_n(N: int, ratio: float) -> int:
+    """keep_n of the SAM3 MLP-merge keep set: min(max(1, round(ratio*N)), N) (sam3.py:62-63)."""
+    v = _lib.load().ssam_zstride_keep_n(N, float(ratio))
+    if v < 0:
+        raise ValueError(f"ratio must be in (0, 1], got {ratio}")
+    return v
+
+
+def zstride_keep(H: int, W: int, ratio: float, B: int, device):
+    """(idx (keep_n,), rows (B*keep_n,)) of the SAM3 static keep set (sam3.py:49-71):
+    raster indices of tokens sampled at a uniform stride along the Morton order,
+    and their rows b*H*W + idx in a (B*H*W, C) token matrix."""
+    keep_n = zstride_keep_n(H * W, ratio)
+    idx = torch.empty(keep_n, dtype=torch.int32, device=device)
+    rows = torch.empty(B * keep_n, dtype=torch.int32, device=device)
+    _lib.call("ssam_zstride_keep", H, W, keep_n, B, idx.data_ptr(), rows.data_ptr(),
+              torch.cuda.current_stream(idx.device).cuda_stream)
+    return idx, rows
+
+
 # ---------------------------------------------------------------------------
 # Attention (a3-a6, a8)
 # ---------------------------------------------------------------------------

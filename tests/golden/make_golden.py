@@ -23,6 +23,9 @@ Outputs (next to this script):
                     intermediate embeddings, permutations, keep sets, dense control)
   golden_hilbert.npz  the reference's Hilbert orders (hilbert_utils.py) for seven
                     grids and tile_stride_matching in three Hilbert perm modes
+  golden_sam3.npz   the SAM3 MLP-merge keep sets (sam3.py _get_keep_indices) for six
+                    grids x ten ratios, and the small encoder with every block
+                    patched by the reference's ToMeSAM3Block
 """
 from __future__ import annotations
 
@@ -232,17 +235,72 @@ def make_e2e(ref_sam) -> dict:
     return out
 
 
+SAM3_GRIDS = ((64, 64), (72, 72), (14, 14), (7, 9), (1, 5), (3, 3))
+SAM3_RATIOS = (0.001, 0.1, 0.25, 0.3, 0.4, 0.5, 0.7, 0.9, 0.99, 1.0)
+SAM3_E2E_RATIO = 0.3
+
+
+def load_sam3(ref_root: str, ref_z):
+    """`_get_keep_indices` and `ToMeSAM3Block` of algos/sparsesam/sam3.py, unmodified.
+
+    The module imports sam3.model.vitdet (the un-vendored SAM3 package) at load
+    time, so the two definitions are taken from its source with `ast` and run in a
+    namespace that supplies what they use: torch, get_z_order from the reference's
+    z_utils, the host SAM Block as the base class (a vitdet-style block), and the
+    host's window_partition / window_unpartition."""
+    import ast
+    path = os.path.join(ref_root, "algos", "sparsesam", "sam3.py")
+    tree = ast.parse(open(path).read())
+    keep = [n for n in tree.body if isinstance(n, (ast.FunctionDef, ast.ClassDef)) and
+            n.name in ("_get_keep_indices", "ToMeSAM3Block")]
+    assert len(keep) == 2
+    ns = {"torch": torch, "nn": torch.nn, "Optional": None, "get_z_order": ref_z.get_z_order, "Block": host.Block,
+          "window_partition": host.window_partition, "window_unpartition": host.window_unpartition,
+          "_KEEP_PERM_CACHE": {}}
+    exec(compile(ast.Module(body=keep, type_ignores=[]), path, "exec"), ns)
+    return ns["_get_keep_indices"], ns["ToMeSAM3Block"]
+
+
+def make_sam3(ref_root: str, ref_z) -> dict:
+    get_keep, block_cls = load_sam3(ref_root, ref_z)
+    out = {}
+    for H, W in SAM3_GRIDS:
+        for r in SAM3_RATIOS:
+            out[f"keep_{H}x{W}_{r}"] = get_keep(H, W, r, "cpu").numpy().astype(np.int32)
+    # The small golden encoder with every block patched by the reference's
+    # ToMeSAM3Block (full attention, partial MLP on the keep set); SAM blocks carry
+    # no layer scale, dropout or drop path, so those are identities here.
+    img = host.synthetic_images(1, seed=E2E_SEED, img_size=E2E_CFG["img_size"])
+    enc = e2e_encoder()
+    info = {"ratio": SAM3_E2E_RATIO, "mlp_merge": True}
+    for m in enc.modules():
+        if isinstance(m, host.Block):
+            m.__class__ = block_cls
+            m._tome_info = info
+            m.ls1 = m.ls2 = m.dropout = m.drop_path = torch.nn.Identity()
+    with torch.no_grad():
+        feat, interm = enc(img)
+    out["e2e_features"] = feat.numpy()
+    for i, t in enumerate(interm):
+        out[f"e2e_interm_{i}"] = t.numpy()
+    return out
+
+
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", required=True, help="path of a hchautran/SparseSAM checkout")
-    ap.add_argument("--only", choices=("all", "hilbert"), default="all")
+    ap.add_argument("--only", choices=("all", "hilbert", "sam3"), default="all")
     args = ap.parse_args()
     torch.manual_seed(0)
-    ref_sam, ref_z = load_reference(os.path.abspath(args.reference))
+    ref_root = os.path.abspath(args.reference)
+    ref_sam, ref_z = load_reference(ref_root)
     if args.only == "all":
         np.savez_compressed(os.path.join(HERE, "golden_order.npz"), **make_order(ref_sam, ref_z))
         np.savez_compressed(os.path.join(HERE, "golden_e2e.npz"), **make_e2e(ref_sam))
-    np.savez_compressed(os.path.join(HERE, "golden_hilbert.npz"), **make_hilbert(ref_sam))
+    if args.only in ("all", "hilbert"):
+        np.savez_compressed(os.path.join(HERE, "golden_hilbert.npz"), **make_hilbert(ref_sam))
+    if args.only in ("all", "sam3"):
+        np.savez_compressed(os.path.join(HERE, "golden_sam3.npz"), **make_sam3(ref_root, ref_z))
     print("wrote", os.listdir(HERE))
 
 

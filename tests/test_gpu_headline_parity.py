@@ -56,7 +56,7 @@ def _run(arch, ratio, cuda_device):
         return _RUNS[key]
     torch.set_num_threads(max(1, len(os.sched_getaffinity(0))))
     img = host.synthetic_images(1, seed=0)
-    enc = host.build_image_encoder(arch, seed=0, device=cuda_device).eval()
+    enc = host.build_image_encoder(arch, seed=0, device=cuda_device).eval()   # same weights as on the CPU
     registry.apply_sam(enc, "sparsesam", ratio=ratio)
     with torch.no_grad():
         feats, interm = enc(img.to(cuda_device))

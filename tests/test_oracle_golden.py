@@ -7,7 +7,7 @@ from oracle import encoder as oenc
 from oracle import order
 from oracle.attention import sparse_attention
 from tests._golden import (E2E_RATIO, HILBERT_GRIDS, HILBERT_MODES, MODES, bf16_bits_to_f32, e2e_encoder,
-                           group_order, load)
+                           group_order, load, SAM3_E2E_RATIO, SAM3_GRIDS, SAM3_RATIOS)
 
 GO = load("golden_order.npz")
 GE = load("golden_e2e.npz")
@@ -195,3 +195,36 @@ def test_attention_restatement_equals_stock_attention_when_dense():
         o = o.reshape(B, h, N, C // h).permute(0, 2, 1, 3).reshape(B, 8, 8, C)
         out = torch.nn.functional.linear(o, attn.proj.weight, attn.proj.bias)
     torch.testing.assert_close(out, ref, atol=1e-5, rtol=1e-5)
+
+
+@pytest.mark.parametrize("H,W", SAM3_GRIDS)
+def test_zstride_keep_matches_reference(H, W):
+    """The SAM3 keep set (sam3.py:49-71), bit-exact against the reference's own
+    _get_keep_indices for every fixture grid and ratio."""
+    g = load("golden_sam3.npz")
+    for r in SAM3_RATIOS:
+        np.testing.assert_array_equal(order.zstride_keep(H, W, r), g[f"keep_{H}x{W}_{r}"])
+
+
+def test_zstride_keep_n_host_entry_point():
+    """ssam_zstride_keep_n (host-only) equals min(max(1, round(r N)), N), Python's
+    ties-to-even round included (r N = 2.5 -> 2, 3.5 -> 4)."""
+    from sparsesam_b200 import _lib
+    lib = _lib.load()
+    for N in (1, 5, 9, 10, 196, 4096, 5184):
+        for r in SAM3_RATIOS + (0.05, 0.35, 0.45, 0.75):
+            assert lib.ssam_zstride_keep_n(N, r) == min(max(1, round(r * N)), N), (N, r)
+    assert lib.ssam_zstride_keep_n(10, 0.25) == 2 and lib.ssam_zstride_keep_n(10, 0.35) == 4
+    assert lib.ssam_zstride_keep_n(10, 0.0) == -1 and lib.ssam_zstride_keep_n(10, 1.5) == -1
+
+
+def test_sam3_encoder_restatement_matches_reference():
+    """The oracle's ToMeSAM3Block restatement on the small golden encoder equals the
+    reference's own ToMeSAM3Block.forward run by make_golden.py."""
+    from sparsesam_b200 import host
+    g = load("golden_sam3.npz")
+    img = host.synthetic_images(1, seed=0, img_size=256)
+    feats, interm = oenc.sam3_encoder_forward(e2e_encoder(), img, SAM3_E2E_RATIO)
+    np.testing.assert_allclose(feats.numpy(), g["e2e_features"], atol=2e-4, rtol=0)
+    for i, t in enumerate(interm):
+        np.testing.assert_allclose(t.numpy(), g[f"e2e_interm_{i}"], atol=2e-4, rtol=0)
