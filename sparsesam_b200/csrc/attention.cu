@@ -150,6 +150,10 @@ template <int D, bool SMALL>
 struct AttnCfg {
   static constexpr int kS = 2;                    // S / P buffers in TMEM
   static constexpr int kTileGroup = SMALL ? 2 : 1;  // consecutive query tiles per CTA (tile_of)
+  // Q buffers: a tile's Q rows load while the two before it hold theirs (windowed
+  // tiles are one key block long, so the UMMA thread needs the next tile's Q for
+  // its [P_H | P_W] while the current tile's QK^T is being issued)
+  static constexpr int kQBuf = SMALL ? 3 : 2;
   static constexpr int kStages = 2;               // K / V / one-hot stages (3 measured slower for windows)
   static_assert(kStages == kS && kS == 2, "one commit per block frees S, K / V stage and O: indices g % 2");
   static constexpr int kBW = SMALL ? 16 : 64;     // bias columns per table (>= win)
@@ -161,8 +165,12 @@ struct AttnCfg {
   static constexpr int kTmAB = kTmO + kO * D;     // TMEM column of A_bias[0]
   static constexpr int kTmPH = kTmAB + 2 * kABCols;
   static constexpr int kOHBytes = 2 * kAttnBN * kBW * 2;  // one-hot H | W regions per stage
-  static constexpr int kABRow = 36;                       // SMALL bias scratch row per half (bytes, odd word stride)
+  static constexpr int kABRow = 80;  // SMALL: a query's fp16 P row (64 B) + 16 B (conflict-free 16-byte stores)
   static constexpr int kOSplit = D == 80 ? 48 : D / 2;    // O columns of the first softmax half
+  // SMALL epilogue staging: per lane-quarter block, 32 rows of each half's bf16
+  // columns; row strides padded by 16 B so 16-byte stores of 8 lanes hit 32 banks
+  static constexpr int kOStride0 = 2 * kOSplit + 16;
+  static constexpr int kOStride1 = 2 * (D - kOSplit) + 16;
   static_assert(kTmPH + kPHCols <= kAttnTmemCols, "TMEM plan exceeds 512 columns");
 };
 
@@ -181,15 +189,15 @@ struct AttnLayout {
   using TG = TileGeom<D>;
   static constexpr int kStage = 2 * TG::bytes(kAttnBN) + C::kOHBytes;  // K | V | one-hot
   static constexpr int kTables = SMALL ? TG::bytes(2 * C::kNT) : 0;
-  static constexpr int kABStage = SMALL ? 2 * kAttnBM * C::kABRow : kAttnBM * 256;  // scratch / staged bias rows
-  int tab, q, kv, ab, tok, xchg, bars, total;
+  static constexpr int kABStage = SMALL ? kAttnBM * C::kABRow : kAttnBM * 256;  // band scratch / staged bias rows
+  int tab, q, kv, ab, ostage, xchg, bars, total;
   __host__ __device__ AttnLayout() {
     tab = 0;
-    q = align1k(tab + kTables);                   // [2] x bytes(128)
-    kv = align1k(q + 2 * TG::bytes(kAttnBM));     // [stages] x kStage
+    q = align1k(tab + kTables);                   // [kQBuf] x bytes(128)
+    kv = align1k(q + C::kQBuf * TG::bytes(kAttnBM));  // [stages] x kStage
     ab = align1k(kv + C::kStages * kStage);       // kABStage
-    tok = ab + kABStage;                          // int [2][128]
-    xchg = tok + 2 * kAttnBM * 4;                 // float [2 rounds][2 halves][2 values][128]
+    ostage = ab + kABStage;                       // SMALL: epilogue staging, 128 rows x (kOStride0 + kOStride1)
+    xchg = ostage + (SMALL ? kAttnBM * (C::kOStride0 + C::kOStride1) : 0);  // float [2][2 halves][2 values][128]
     bars = (xchg + 2 * 2 * 2 * kAttnBM * 4 + 7) & ~7;  // mbarriers
     total = bars + 64 * 8 + 16 + 1024;            // mbarriers, TMEM address, abort flag + alignment slack
   }
@@ -213,6 +221,24 @@ struct AttnParams {
   int total_tiles;
   __half* bias_ws;  // LARGE: [rows][n_tiles*128][128] fp16 = relH/scale | relW/scale
 };
+
+// Token of permuted query position p of (sequence, head) row `row`, or -1 past N.
+// Without the diagonal every query block attends to the same key blocks
+// (n < n_init), so a query's result does not depend on its place in the
+// permutation: the queries are then taken in raster order (token p) and no
+// permutation entry is read. With the diagonal, position p holds token perm[p].
+__device__ __forceinline__ int query_tok(const AttnParams& a, int row, int p) {
+  if (p >= a.N) return -1;
+  return a.with_diag ? __ldg(a.perm + static_cast<int64_t>(row) * a.N + p) : p;
+}
+
+// Output row of token `tok` of sequence `seq` (-1: not stored); n_seq * N fits
+// int32 (checked on the host).
+__device__ __forceinline__ int query_out_row(const AttnParams& a, int seq, int tok) {
+  if (tok < 0) return -1;
+  const int i = seq * a.N + tok;
+  return a.out_rows != nullptr ? __ldg(a.out_rows + i) : i;
+}
 
 // Key blocks of one tile. The mask enables 64-key block m for query m-block mb
 // when m < nk, or m == mb with the diagonal. Processed 128-key blocks: those
@@ -275,27 +301,109 @@ struct BlockCursor {
 // overlap the softmax of blocks g and g+1.
 enum {
   kBarTab = 0,
-  kBarQFull = 1,     // [2]  loader lanes (cp.async)
-  kBarQEmpty = 3,    // [2]  UMMA commit after the tile's last QK^T
-  kBarKFull = 5,     // [3]  K loader lanes (cp.async)
-  kBarKEmpty = 8,    // [3]  unused: S-full (QK^T done) frees the K stage
-  kBarVFull = 11,    // [3]  V loader lanes (cp.async)
-  kBarVEmpty = 14,   // [3]  unused: O-done (P.V done) frees the V stage
-  kBarPHFull = 17,   //      UMMA commit (SMALL)
-  kBarPHFree = 18,   //      softmax (SMALL)
-  kBarABFull = 19,   // [2]  softmax: A_bias of the tile is in TMEM
-  kBarABSFull = 21,  //      LARGE: bias rows staged (cp.async)
-  kBarABSFree = 22,  //      LARGE: softmax copied the staged rows
-  kBarSFull = 23,    // [2]  UMMA commit after QK^T
-  kBarSFree = 25,    // [2]  unused: O-done frees the S block (P lives in its columns)
-  kBarPFull = 27,    // [2]  softmax
-  kBarODone = 29,    // [2]  UMMA commit after P.V of block g (index g & 1)
-  kBarOFree = 31,    // [2]  softmax epilogue
-  kBarXchg = 33,     // [2 rounds][4 lane quarters]  the two softmax warps of a quarter
-  kBarDrain = 41,
-  kNumBars = 42
+  kBarQFull = 1,     // [kQBuf <= 3]  loader lanes (cp.async)
+  kBarQEmpty = 4,    // [kQBuf <= 3]  UMMA commit after the tile's last QK^T
+  kBarKFull = 7,     // [3]  K loader lanes (cp.async)
+  kBarKEmpty = 10,   // [3]  unused: S-full (QK^T done) frees the K stage
+  kBarVFull = 13,    // [3]  V loader lanes (cp.async)
+  kBarVEmpty = 16,   // [3]  unused: O-done (P.V done) frees the V stage
+  kBarPHFull = 19,   //      UMMA commit (SMALL)
+  kBarPHFree = 20,   //      K loaders (SMALL)
+  kBarABFull = 21,   // [2]  A_bias of the tile is in TMEM (SMALL: K loaders; LARGE: softmax)
+  kBarABSFull = 23,  //      LARGE: bias rows staged (cp.async)
+  kBarABSFree = 24,  //      LARGE: softmax copied the staged rows
+  kBarSFull = 25,    // [2]  UMMA commit after QK^T
+  kBarSFree = 27,    // [2]  unused: O-done frees the S block (P lives in its columns)
+  kBarPFull = 29,    // [2]  softmax
+  kBarODone = 31,    // [2]  UMMA commit after P.V of block g (index g & 1)
+  kBarOFree = 33,    // [2]  softmax epilogue
+  kBarXchg = 35,     // [2 rounds][4 lane quarters]  the two softmax warps of a quarter
+  kBarDrain = 43,
+  kNumBars = 44
 };
 static_assert(kNumBars * 8 + 8 <= 64 * 8, "mbarrier region of AttnLayout too small");
+
+// Band of one table: the BW/2 output words (fp16 pairs) relX[j] = S[qc + win - 1 - j]
+// (j < win, zero above) for the fp16 row S staged at `srow`. With
+// base = qc + win - BW the band is the reversed window S[base .. base + BW - 1]:
+// it is read as BW/2 + 1 consecutive words from word base >> 1 (the words before
+// the row only feed entries that are masked) and re-paired with byte permutes.
+template <int BW>
+__device__ __forceinline__ void relbias_band(const uint8_t* srow, int qc, int win, uint32_t (&out)[BW / 2]) {
+  const int base = qc + win - BW;
+  const int w0 = base >> 1;  // arithmetic shift: floor
+  const uint32_t* sw = reinterpret_cast<const uint32_t*>(srow) + w0;
+  uint32_t u[BW / 2 + 1];
+#pragma unroll
+  for (int i = 0; i <= BW / 2; ++i) u[i] = sw[i];
+  const bool odd = base & 1;
+#pragma unroll
+  for (int k = 0; k < BW / 2; ++k) {
+    // word k = (relX[2k], relX[2k+1]) = (S[base + BW - 1 - 2k], S[base + BW - 2 - 2k])
+    const int m = BW / 2 - 1 - k;
+    uint32_t w = odd ? __byte_perm(u[m + 1], u[m], 0x7610) : __byte_perm(u[m], 0u, 0x1032);
+    if (2 * k >= win) w = 0u;
+    else if (2 * k + 1 >= win) w &= 0xffffu;
+    out[k] = w;
+  }
+}
+
+// Writes the NV fp32 values v (times `mul`) as fp16 to `dst` (16-byte aligned).
+template <int NV>
+__device__ __forceinline__ void stage_f16_row(uint8_t* dst, const uint32_t* v, float mul) {
+  static_assert(NV % 8 == 0, "whole 16-byte units");
+  uint4* sp = reinterpret_cast<uint4*>(dst);
+#pragma unroll
+  for (int i = 0; i < NV / 8; ++i) {
+    uint32_t h[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const __half2 h2 = __floats2half2_rn(__uint_as_float(v[8 * i + 2 * j]) * mul,
+                                           __uint_as_float(v[8 * i + 2 * j + 1]) * mul);
+      h[j] = *reinterpret_cast<const uint32_t*>(&h2);
+    }
+    sp[i] = make_uint4(h[0], h[1], h[2], h[3]);
+  }
+}
+
+// Epilogue of one softmax warp for NC O columns (a multiple of 16) starting at TMEM
+// column tO: each lane's row, times `scale`, as bf16 into its STRIDE-byte row of
+// the warp's staging block; then the warp stores the block row segment by row
+// segment (NC / 8 lanes of 16 bytes per row, four to five rows per instruction)
+// to out row orow of each lane (< 0: not stored), columns starting at obase.
+template <int NC, int STRIDE>
+__device__ __forceinline__ void stage_out_rows(uint32_t tO, uint8_t* stage, int orow, float scale,
+                                               __nv_bfloat16* obase, int64_t ld_out) {
+  static_assert(NC % 16 == 0 && NC <= 64, "16-column TMEM loads, at most two x32 loads");
+  const int lane = static_cast<int>(threadIdx.x & 31);
+  uint32_t v[NC];
+  if constexpr (NC >= 32) {
+    tmem_ld_32x32b_x32(tO, *reinterpret_cast<uint32_t(*)[32]>(&v[0]));
+    if constexpr (NC == 64) tmem_ld_32x32b_x32(tO + 32, *reinterpret_cast<uint32_t(*)[32]>(&v[32]));
+    if constexpr (NC == 48) tmem_ld_32x32b_x16(tO + 32, *reinterpret_cast<uint32_t(*)[16]>(&v[32]));
+  } else {
+    tmem_ld_32x32b_x16(tO, *reinterpret_cast<uint32_t(*)[16]>(&v[0]));
+  }
+  tmem_ld_wait();
+  __syncwarp();  // the previous tile's row segments have been read out of the block
+  uint4* srow = reinterpret_cast<uint4*>(stage + lane * STRIDE);
+#pragma unroll
+  for (int c = 0; c < NC / 8; ++c)
+    srow[c] = make_uint4(pack_bf16x2(__uint_as_float(v[8 * c]) * scale, __uint_as_float(v[8 * c + 1]) * scale),
+                         pack_bf16x2(__uint_as_float(v[8 * c + 2]) * scale, __uint_as_float(v[8 * c + 3]) * scale),
+                         pack_bf16x2(__uint_as_float(v[8 * c + 4]) * scale, __uint_as_float(v[8 * c + 5]) * scale),
+                         pack_bf16x2(__uint_as_float(v[8 * c + 6]) * scale, __uint_as_float(v[8 * c + 7]) * scale));
+  __syncwarp();
+  constexpr int kCh = NC / 8;  // 16-byte chunks per row segment
+#pragma unroll
+  for (int k = 0; k < kCh; ++k) {
+    const int i = lane + 32 * k;
+    const int rr = i / kCh, c = i - rr * kCh;
+    const int dst_row = __shfl_sync(0xffffffffu, orow, rr);
+    const uint4 val = *reinterpret_cast<const uint4*>(stage + rr * STRIDE + c * 16);
+    if (dst_row >= 0) *reinterpret_cast<uint4*>(obase + static_cast<int64_t>(dst_row) * ld_out + c * 8) = val;
+  }
+}
 
 template <int D, bool SMALL>
 __global__ void __launch_bounds__(kAttnThreads, 1) sparse_attn_kernel(const AttnParams a) {
@@ -309,7 +417,6 @@ __global__ void __launch_bounds__(kAttnThreads, 1) sparse_attn_kernel(const Attn
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L.bars);
   uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(bars + kNumBars);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
-  int* s_tok = reinterpret_cast<int*>(smem + L.tok);
 
   const int tid = threadIdx.x;
   const int warp = tid >> 5, lane = tid & 31;
@@ -317,10 +424,12 @@ __global__ void __launch_bounds__(kAttnThreads, 1) sparse_attn_kernel(const Attn
 
   if (tid == 0) {
     mbar_init(&bars[kBarTab], 64);
-    for (int i = 0; i < 2; ++i) {
+    for (int i = 0; i < C::kQBuf; ++i) {
       mbar_init(&bars[kBarQFull + i], 64);
       mbar_init(&bars[kBarQEmpty + i], 1);
-      mbar_init(&bars[kBarABFull + i], 256);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&bars[kBarABFull + i], SMALL ? 128 : 256);
       mbar_init(&bars[kBarSFull + i], 1);
       mbar_init(&bars[kBarSFree + i], 1);
       mbar_init(&bars[kBarPFull + i], 256);
@@ -329,7 +438,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1) sparse_attn_kernel(const Attn
       for (int w = 0; w < 4; ++w) mbar_init(&bars[kBarXchg + 4 * i + w], 64);
     }
     mbar_init(&bars[kBarPHFull], 1);
-    mbar_init(&bars[kBarPHFree], 256);
+    mbar_init(&bars[kBarPHFree], 128);
     mbar_init(&bars[kBarABSFull], kAttnVW * 64);
     mbar_init(&bars[kBarABSFree], 256);
     for (int s = 0; s < C::kStages; ++s) {
@@ -450,20 +559,15 @@ __global__ void __launch_bounds__(kAttnThreads, 1) sparse_attn_kernel(const Attn
       const int tile = tile_of<C::kTileGroup>(lt_);
       const int row = tile / a.n_tiles, qtile = tile - row * a.n_tiles;
       const int seq = row / a.heads, head = row - seq * a.heads;
-      const int32_t* perm = a.perm + static_cast<int64_t>(row) * N;
-      const int qb = lt_ & 1;
+      const int qb = lt_ % C::kQBuf;
       if (q_warp) {
         int qt[4];  // rows 32 i + lane of the tile
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
           const int p = qtile * kAttnBM + 32 * i + lane;
-          qt[i] = p < N ? __ldg(perm + p) : -1;
+          qt[i] = query_tok(a, row, p);
         }
-        if (!wait_or_abort(kBarQEmpty + qb, ((lt_ >> 1) & 1) ^ 1)) return false;
-        if constexpr (SMALL) {
-#pragma unroll
-          for (int i = 0; i < 4; ++i) s_tok[qb * kAttnBM + 32 * i + lane] = qt[i];
-        }
+        if (!wait_or_abort(kBarQEmpty + qb, ((lt_ / C::kQBuf) & 1) ^ 1)) return false;
         copy_rows(sb + L.q + qb * TG::bytes(kAttnBM), kAttnBM, 0, 128, qt,
                   a.qkv + static_cast<int64_t>(seq) * N * a.ld_qkv, head * D);
         mbar_arrive(&bars[kBarQFull + qb]);
@@ -484,6 +588,48 @@ __global__ void __launch_bounds__(kAttnThreads, 1) sparse_attn_kernel(const Attn
         cp_async_arrive_noinc(&bars[kBarABSFull]);
       }
       return true;
+    };
+
+    // SMALL, K warps: the rel-pos bias operand of tile lt_ (thread = query row
+    // 32 (warp % 4) + lane, both tables). [P_H | P_W] of the tile comes from the
+    // UMMA thread; each table row is staged as fp16 (x 1 / scale) and its band
+    // relX[j] = P_X[qc - j + win - 1] read as a reversed window, then the two
+    // bands go to A_bias[lt_ & 1] in TMEM. The buffer's previous reader, QK^T of
+    // tile lt_ - 2, completed before the [P_H | P_W] commit of tile lt_.
+    auto stage_bias_rows = [&](int lt_) -> bool {
+      if constexpr (!SMALL) {
+        return true;
+      } else {
+      const int r = (warp & 3) * 32 + lane;
+      const uint32_t t_lane = tmem + (static_cast<uint32_t>((warp & 3) * 32) << 16);
+      const int tile = tile_of<C::kTileGroup>(lt_);
+      const int row = tile / a.n_tiles, qtile = tile - row * a.n_tiles;
+      const int p = qtile * kAttnBM + r;
+      const int t = query_tok(a, row, p);
+      const int qh = t >= 0 ? t / win : 0;
+      const int qw = t >= 0 ? t - qh * win : 0;
+      if (!wait_or_abort(kBarPHFull, lt_ & 1)) return false;
+      tc_fence_after();
+      uint32_t ph[C::kNT], pw[C::kNT];
+      tmem_ld_32x32b_x32(t_lane + C::kTmPH, ph);
+      tmem_ld_32x32b_x32(t_lane + C::kTmPH + C::kNT, pw);
+      tmem_ld_wait();
+      tc_fence_before();
+      mbar_arrive(&bars[kBarPHFree]);
+      uint8_t* srow = smem + L.ab + r * C::kABRow;
+      uint32_t v[2 * (C::kBW / 2)];
+      uint32_t (&vh)[C::kBW / 2] = *reinterpret_cast<uint32_t(*)[C::kBW / 2]>(&v[0]);
+      uint32_t (&vw)[C::kBW / 2] = *reinterpret_cast<uint32_t(*)[C::kBW / 2]>(&v[C::kBW / 2]);
+      stage_f16_row<C::kNT>(srow, ph, a.inv_scale);
+      relbias_band<C::kBW>(srow, qh, win, vh);
+      stage_f16_row<C::kNT>(srow, pw, a.inv_scale);
+      relbias_band<C::kBW>(srow, qw, win, vw);
+      tmem_st_32x32b_x16(t_lane + C::kTmAB + (lt_ & 1) * C::kABCols, v);
+      tmem_st_wait();
+      tc_fence_before();
+      mbar_arrive(&bars[kBarABFull + (lt_ & 1)]);
+      return true;
+      }
     };
 
     int g = 0;
@@ -551,6 +697,10 @@ __global__ void __launch_bounds__(kAttnThreads, 1) sparse_attn_kernel(const Attn
         mbar_arrive(&bars[full_bar]);
         cp_async_arrive_noinc(&bars[full_bar]);
       }
+      // the tile's bias operand once its key rows are on their way
+      if constexpr (SMALL) {
+        if (ok && kv == 0 && !(ok = stage_bias_rows(lt))) break;
+      }
     }
     cp_async_wait_all();
   } else if (warp == kAttnMmaWarp) {
@@ -563,8 +713,8 @@ __global__ void __launch_bounds__(kAttnThreads, 1) sparse_attn_kernel(const Attn
       bool ok = !SMALL || wait_or_abort(kBarTab, 0);
 
       auto issue_ph = [&](int lt_) -> bool {  // [P_H | P_W] of tile lt_ (SMALL)
-        const int qb = lt_ & 1;
-        if (!wait_or_abort(kBarQFull + qb, (lt_ >> 1) & 1)) return false;
+        const int qb = lt_ % C::kQBuf;
+        if (!wait_or_abort(kBarQFull + qb, (lt_ / C::kQBuf) & 1)) return false;
         if (!wait_or_abort(kBarPHFree, (lt_ & 1) ^ 1)) return false;
         tc_fence_after();
         fence_proxy_async_smem();
@@ -581,7 +731,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1) sparse_attn_kernel(const Attn
           if constexpr (SMALL) {
             if (tile_exists(c.lt + 1) && !issue_ph(c.lt + 1)) return false;
           } else {
-            if (!wait_or_abort(kBarQFull + (c.lt & 1), (c.lt >> 1) & 1)) return false;
+            if (!wait_or_abort(kBarQFull + c.lt % C::kQBuf, (c.lt / C::kQBuf) & 1)) return false;
           }
           if (!wait_or_abort(kBarABFull + (c.lt & 1), (c.lt >> 1) & 1)) return false;
         }
@@ -591,7 +741,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1) sparse_attn_kernel(const Attn
         if (!wait_or_abort(kBarODone + sbuf, ((c.g / C::kS) & 1) ^ 1)) return false;
         tc_fence_after();
         fence_proxy_async_smem();
-        const uint32_t sQ = sb + L.q + (c.lt & 1) * TG::bytes(kAttnBM);
+        const uint32_t sQ = sb + L.q + (c.lt % C::kQBuf) * TG::bytes(kAttnBM);
         const uint32_t sK = sb + L.kv + st * LAY::kStage;
         const uint32_t sOH = sK + 2 * TG::bytes(kAttnBN);
         const uint32_t tAB = tmem + C::kTmAB + (c.lt & 1) * C::kABCols;
@@ -613,7 +763,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1) sparse_attn_kernel(const Attn
           }
         }
         umma_commit(&bars[kBarSFull + sbuf]);  // also frees K stage st (kS == kStages)
-        if (c.j == c.tb.n - 1) umma_commit(&bars[kBarQEmpty + (c.lt & 1)]);
+        if (c.j == c.tb.n - 1) umma_commit(&bars[kBarQEmpty + c.lt % C::kQBuf]);
         return true;
       };
       auto issue_pv = [&](const BlockCursor<C::kTileGroup>& c) -> bool {
@@ -630,9 +780,10 @@ __global__ void __launch_bounds__(kAttnThreads, 1) sparse_attn_kernel(const Attn
         // V as an MN-major operand with N = D: 32B-swizzled atoms of 8 keys x 16
         // channels, the D/16 channel regions LBO = 128 * 32 bytes apart.
 #pragma unroll
+        // P of keys 0..63 sits in columns 0..31 of the S block, keys 64..127 in 64..95
         for (int ks = 0; ks < kAttnBN / 16; ++ks)
-          umma_f16_ts(tO, tP + ks * 8, make_smem_desc(sV + ks * 512, kAttnBN * 32, 256, kSw32), idesc_o,
-                      (c.j > 0 || ks > 0) ? 1u : 0u);
+          umma_f16_ts(tO, tP + ks * 8 + (ks >= kAttnBN / 32 ? 32 : 0),
+                      make_smem_desc(sV + ks * 512, kAttnBN * 32, 256, kSw32), idesc_o, (c.j > 0 || ks > 0) ? 1u : 0u);
         umma_commit(&bars[kBarODone + (c.g & 1)]);  // also frees V stage st and S block sbuf
         return true;
       };
@@ -680,55 +831,25 @@ __global__ void __launch_bounds__(kAttnThreads, 1) sparse_attn_kernel(const Attn
       return true;
     };
 
-    // A_bias of tile lt_ -> TMEM buffer lt_ & 1 (row r): fp16 pairs, relH/scale
-    // at column j (half 0 writes these), then relW/scale (half 1). Called once S
-    // of the current tile's first block is in, so every QK^T that read the
-    // buffer's previous contents has completed.
-    auto stage_bias = [&](int lt_, int& tok_out) -> bool {
+    // LARGE: A_bias of tile lt_ -> TMEM buffer lt_ & 1 (row r): the staged fp16
+    // [relH/scale | relW/scale] row, half h's 32 words. Called once S of the current
+    // tile's first block is in, so every QK^T that read the buffer's previous
+    // contents has completed. (Windowed grids: the K-loader warps stage it.)
+    auto stage_bias = [&](int lt_) -> bool {
       const uint32_t tAB = t_lane + C::kTmAB + (lt_ & 1) * C::kABCols;
-      if constexpr (SMALL) {
-        const int qb = lt_ & 1;
-        if (!wait_or_abort(kBarQFull + qb, (lt_ >> 1) & 1)) return false;
-        const int t = s_tok[qb * kAttnBM + r];
-        tok_out = t;
-        const int qh = t >= 0 ? t / win : 0;
-        const int qw = t >= 0 ? t - qh * win : 0;
-        const int qc = h ? qw : qh;
-        if (!wait_or_abort(kBarPHFull, lt_ & 1)) return false;
-        tc_fence_after();
-        uint8_t* rowp = smem + L.ab + (h * kAttnBM + r) * C::kABRow;  // 16 fp16 of this half
-        uint32_t rp[32];
-        tmem_ld_32x32b_x32(t_lane + C::kTmPH + h * C::kNT, rp);
-        tmem_ld_wait();
-        tc_fence_before();
-        mbar_arrive(&bars[kBarPHFree]);
+      if (!wait_or_abort(kBarABSFull, lt_ & 1)) return false;
+      const uint8_t* hrow = smem + L.ab + h * (kAttnBM * 128) + r * 128;
+      uint32_t v[32];
 #pragma unroll
-        for (int j = 0; j < 16; j += 2) *reinterpret_cast<uint32_t*>(rowp + j * 2) = 0u;  // no NaN/Inf padding
-#pragma unroll
-        for (int c = 0; c < 32; ++c) {
-          const int jj = qc + win - 1 - c;
-          if (jj >= 0 && jj < win)
-            *reinterpret_cast<__half*>(rowp + jj * 2) = __float2half_rn(__uint_as_float(rp[c]) * a.inv_scale);
-        }
-        uint32_t v[8];
-#pragma unroll
-        for (int i = 0; i < 8; ++i) v[i] = *reinterpret_cast<const uint32_t*>(rowp + 4 * i);
-        tmem_st_32x32b_x8(tAB + h * (C::kBW / 2), v);
-      } else {
-        if (!wait_or_abort(kBarABSFull, lt_ & 1)) return false;
-        const uint8_t* hrow = smem + L.ab + h * (kAttnBM * 128) + r * 128;
-        uint32_t v[32];
-#pragma unroll
-        for (int c = 0; c < 8; ++c) {
-          const uint4 x = *reinterpret_cast<const uint4*>(hrow + ((c ^ (r & 7)) << 4));
-          v[4 * c] = x.x;
-          v[4 * c + 1] = x.y;
-          v[4 * c + 2] = x.z;
-          v[4 * c + 3] = x.w;
-        }
-        tmem_st_32x32b_x32(tAB + h * 32, v);
-        mbar_arrive(&bars[kBarABSFree]);
+      for (int c = 0; c < 8; ++c) {
+        const uint4 x = *reinterpret_cast<const uint4*>(hrow + ((c ^ (r & 7)) << 4));
+        v[4 * c] = x.x;
+        v[4 * c + 1] = x.y;
+        v[4 * c + 2] = x.z;
+        v[4 * c + 3] = x.w;
       }
+      tmem_st_32x32b_x32(tAB + h * 32, v);
+      mbar_arrive(&bars[kBarABSFree]);
       tmem_st_wait();
       tc_fence_before();
       mbar_arrive(&bars[kBarABFull + (lt_ & 1)]);
@@ -736,52 +857,64 @@ __global__ void __launch_bounds__(kAttnThreads, 1) sparse_attn_kernel(const Attn
     };
     // This half's O columns / l of tile lt_, stored at the raster token
     // (inverse permutation and head merge)
-    auto epilogue = [&](int lt_, int g_last, int tok, float l) -> bool {
+    // (orow: the output row of this thread's query, looked up a tile ahead)
+    auto epilogue = [&](int lt_, int g_last, int orow, float l) -> bool {
       const int tile = tile_of<C::kTileGroup>(lt_);
       const int row = tile / a.n_tiles;
-      const int seq = row / a.heads, head = row - seq * a.heads;
+      const int head = row % a.heads;
       if (g_last >= 0 && !wait_or_abort(kBarODone + (g_last & 1), (g_last >> 1) & 1)) return false;
       tc_fence_after();
       const float inv_l = l > 0.f ? 1.f / l : 0.f;
-      int64_t orow = tok >= 0 ? static_cast<int64_t>(seq) * N + tok : -1;
-      if (orow >= 0 && a.out_rows != nullptr) orow = __ldg(a.out_rows + orow);
-      uint4* dst = orow >= 0 ? reinterpret_cast<uint4*>(a.out + orow * a.ld_out + head * D) : nullptr;
       const uint32_t tO = t_lane + C::kTmO + (lt_ % C::kO) * D;
+      if constexpr (SMALL) {
+        // The warp's 32 rows x this half's columns: TMEM -> bf16 in the warp's
+        // staging block -> whole row segments stored by consecutive lanes.
+        uint8_t* stage = smem + L.ostage + (warp & 3) * 32 * (C::kOStride0 + C::kOStride1) +
+                         (h ? 32 * C::kOStride0 : 0);
+        __nv_bfloat16* obase = a.out + head * D + oc0;
+        if (h == 0)
+          stage_out_rows<C::kOSplit, C::kOStride0>(tO, stage, orow, g_last >= 0 ? inv_l : 0.f, obase, a.ld_out);
+        else
+          stage_out_rows<D - C::kOSplit, C::kOStride1>(tO + C::kOSplit, stage, orow, g_last >= 0 ? inv_l : 0.f,
+                                                       obase, a.ld_out);
+      } else {
+        uint4* dst = orow >= 0 ? reinterpret_cast<uint4*>(a.out + static_cast<int64_t>(orow) * a.ld_out + head * D)
+                               : nullptr;
 #pragma unroll
-      for (int c0 = 0; c0 < D; c0 += 16) {
-        if (c0 < oc0 || c0 >= oc1) continue;
-        uint32_t r16[16];
-        tmem_ld_32x32b_x16(tO + c0, r16);
-        tmem_ld_wait();
-        if (dst != nullptr) {
-          float o[16];
+        for (int c0 = 0; c0 < D; c0 += 16) {
+          if (c0 < oc0 || c0 >= oc1) continue;
+          uint32_t r16[16];
+          tmem_ld_32x32b_x16(tO + c0, r16);
+          tmem_ld_wait();
+          if (dst != nullptr) {
+            float o[16];
 #pragma unroll
-          for (int e = 0; e < 16; ++e) o[e] = g_last >= 0 ? __uint_as_float(r16[e]) * inv_l : 0.f;
-          dst[c0 / 8] = make_uint4(pack_bf16x2(o[0], o[1]), pack_bf16x2(o[2], o[3]), pack_bf16x2(o[4], o[5]),
-                                   pack_bf16x2(o[6], o[7]));
-          dst[c0 / 8 + 1] = make_uint4(pack_bf16x2(o[8], o[9]), pack_bf16x2(o[10], o[11]),
-                                       pack_bf16x2(o[12], o[13]), pack_bf16x2(o[14], o[15]));
+            for (int e = 0; e < 16; ++e) o[e] = g_last >= 0 ? __uint_as_float(r16[e]) * inv_l : 0.f;
+            dst[c0 / 8] = make_uint4(pack_bf16x2(o[0], o[1]), pack_bf16x2(o[2], o[3]), pack_bf16x2(o[4], o[5]),
+                                     pack_bf16x2(o[6], o[7]));
+            dst[c0 / 8 + 1] = make_uint4(pack_bf16x2(o[8], o[9]), pack_bf16x2(o[10], o[11]),
+                                         pack_bf16x2(o[12], o[13]), pack_bf16x2(o[14], o[15]));
+          }
         }
       }
       tc_fence_before();
       mbar_arrive(&bars[kBarOFree + lt_ % C::kO]);
       return true;
     };
-    // LARGE: this thread's query token of tile lt_, straight from the permutation.
-    auto query_token = [&](int lt_) -> int {
+    // Output row of this thread's query of tile lt_.
+    auto query_row = [&](int lt_) -> int {
       const int tile = tile_of<C::kTileGroup>(lt_);
       const int row = tile / a.n_tiles, qtile = tile - row * a.n_tiles;
-      const int p = qtile * kAttnBM + r;
-      return p < N ? __ldg(a.perm + static_cast<int64_t>(row) * N + p) : -1;
+      return query_out_row(a, row / a.heads, query_tok(a, row, qtile * kAttnBM + r));
     };
 
     bool ok = true;
-    int tok_cur = -1, tok_next = -1;
+    int orow_cur = -1, orow_next = -1;
     if (tile_exists(0)) {
-      ok = stage_bias(0, tok_cur);
-      if (!SMALL) tok_cur = query_token(0);
+      if constexpr (!SMALL) ok = stage_bias(0);
+      orow_cur = query_row(0);
     }
-    int pend_lt = -1, pend_g = -1, pend_tok = -1;  // deferred epilogue
+    int pend_lt = -1, pend_g = -1, pend_orow = -1;  // deferred epilogue
     float pend_l = 0.f;  // this half's share of the pending tile's row sum
     int g = 0;
     for (int lt = 0; ok && tile_exists(lt); ++lt) {
@@ -790,19 +923,13 @@ __global__ void __launch_bounds__(kAttnThreads, 1) sparse_attn_kernel(const Attn
       const TileBlocks tb(a, qtile);
       const int my_mb = 2 * qtile + (r >= 64 ? 1 : 0);
       const uint32_t tO = t_lane + C::kTmO + (lt % C::kO) * D;
-      if (!SMALL && tile_exists(lt + 1)) tok_next = query_token(lt + 1);
+      if (tile_exists(lt + 1)) orow_next = query_row(lt + 1);
       float m_run = -INFINITY, l_run = 0.f;  // l_run: this half's share of the row sum
       for (int j = 0; j < tb.n; ++j, ++g) {
         const int sbuf = g % C::kS;
         const int kb = tb.at(j);
         if (!(ok = wait_or_abort(kBarSFull + sbuf, (g / C::kS) & 1))) break;
         tc_fence_after();
-        // Windowed grids stage the next tile's bias operand before this block's
-        // softmax (their tiles are a single block, so the next tile's QK^T then
-        // overlaps this softmax); its buffer's previous reader, QK^T of tile
-        // lt - 1, completed before this S arrived.
-        if (SMALL && j == 0 && tile_exists(lt + 1) && !(ok = stage_bias(lt + 1, tok_next))) break;
-        const uint32_t tS = t_lane + sbuf * kAttnBN + 64 * h;
         // this half's 64 keys: 64-key mask block 2 kb + h
         const int mh = 2 * kb + h;
         // 64-token masks enable the query's own 64-block on the diagonal, 128-token
@@ -811,30 +938,24 @@ __global__ void __launch_bounds__(kAttnThreads, 1) sparse_attn_kernel(const Attn
         const bool full = (2 * kb + 1 < tb.nk || diag_tile) && (kb + 1) * kAttnBN <= N;
         const int kvalid = N - kb * kAttnBN - 64 * h;  // keys of this half inside the sequence
         const bool on = full || mh < tb.nk || diag_tile || (a.with_diag == 1 && mh == my_mb);
-        uint32_t s[64];
-        {
-          uint32_t (&s0)[32] = *reinterpret_cast<uint32_t(*)[32]>(&s[0]);
-          uint32_t (&s1)[32] = *reinterpret_cast<uint32_t(*)[32]>(&s[32]);
-          tmem_ld_32x32b_x32(tS, s0);
-          tmem_ld_32x32b_x32(tS + 32, s1);
-          tmem_ld_wait();
-        }
-        // LARGE: masked keys (off mask blocks, keys past N) -> -inf, so that one code
-        // path serves every block (exp2(-inf) = 0); measured faster than two paths
-        // for the global grid, slower for windows (whose blocks are all full)
-        if (!SMALL && !full) {
-#pragma unroll
-          for (int jj = 0; jj < 64; ++jj) s[jj] = (on && jj < kvalid) ? s[jj] : 0xff800000u;
-        }
-        // row maximum of the raw logits over both halves (scale > 0 commutes with max)
+        // this half's 64 S columns; P of these keys is written back over their first 32
+        const uint32_t tSh = t_lane + sbuf * kAttnBN + 64 * h;
+        // pass 1: row maximum of the raw logits over both halves (scale > 0 commutes
+        // with max); masked keys (off the mask, past N) do not take part
         float mx4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
-        if (!SMALL || full) {
+        {
+          uint32_t s[64];
+          tmem_ld_32x32b_x32(tSh, *reinterpret_cast<uint32_t(*)[32]>(&s[0]));
+          tmem_ld_32x32b_x32(tSh + 32, *reinterpret_cast<uint32_t(*)[32]>(&s[32]));
+          tmem_ld_wait();
+          if (full) {
 #pragma unroll
-          for (int jj = 0; jj < 64; ++jj) mx4[jj & 3] = fmaxf(mx4[jj & 3], __uint_as_float(s[jj]));
-        } else if (on) {
+            for (int jj = 0; jj < 64; ++jj) mx4[jj & 3] = fmaxf(mx4[jj & 3], __uint_as_float(s[jj]));
+          } else if (on) {
 #pragma unroll
-          for (int jj = 0; jj < 64; ++jj)
-            if (jj < kvalid) mx4[jj & 3] = fmaxf(mx4[jj & 3], __uint_as_float(s[jj]));
+            for (int jj = 0; jj < 64; ++jj)
+              if (jj < kvalid) mx4[jj & 3] = fmaxf(mx4[jj & 3], __uint_as_float(s[jj]));
+          }
         }
         float mx = fmaxf(fmaxf(mx4[0], mx4[1]), fmaxf(mx4[2], mx4[3]));
         float mx_other, l_other;
@@ -870,29 +991,38 @@ __global__ void __launch_bounds__(kAttnThreads, 1) sparse_attn_kernel(const Attn
             tmem_st_32x32b_x16(tO + c0, r16);
           }
         }
-        // P = exp2(s * scale log2e - m) as bf16 pairs over this half's 32 P columns
-        uint32_t pk[32];
+        // pass 2: P = exp2(s * scale log2e - m) as bf16 pairs, 32 keys at a time (S re-read
+        // from TMEM): keys 32c .. 32c + 31 of this half go to its columns 16c .. 16c + 15,
+        // which pass 2 has already read
         float sum4[4] = {0.f, 0.f, 0.f, 0.f};
-        if (!SMALL || full) {
 #pragma unroll
-          for (int e = 0; e < 32; ++e) {
-            const float p0 = fast_exp2(fmaf(__uint_as_float(s[2 * e]), a.scale_log2, -m_off));
-            const float p1 = fast_exp2(fmaf(__uint_as_float(s[2 * e + 1]), a.scale_log2, -m_off));
-            sum4[e & 3] += p0 + p1;
-            pk[e] = pack_bf16x2(p0, p1);
-          }
-        } else {
+        for (int c = 0; c < 2; ++c) {
+          uint32_t sc[32];
+          tmem_ld_32x32b_x32(tSh + 32 * c, sc);
+          tmem_ld_wait();
+          uint32_t pk[16];
+          if (full) {
 #pragma unroll
-          for (int e = 0; e < 32; ++e) {
-            const bool v0 = on && 2 * e < kvalid;
-            const bool v1 = on && 2 * e + 1 < kvalid;
-            const float p0 = v0 ? fast_exp2(fmaf(__uint_as_float(s[2 * e]), a.scale_log2, -m_off)) : 0.f;
-            const float p1 = v1 ? fast_exp2(fmaf(__uint_as_float(s[2 * e + 1]), a.scale_log2, -m_off)) : 0.f;
-            sum4[e & 3] += p0 + p1;
-            pk[e] = pack_bf16x2(p0, p1);
+            for (int e = 0; e < 16; ++e) {
+              const float p0 = fast_exp2(fmaf(__uint_as_float(sc[2 * e]), a.scale_log2, -m_off));
+              const float p1 = fast_exp2(fmaf(__uint_as_float(sc[2 * e + 1]), a.scale_log2, -m_off));
+              sum4[e & 3] += p0 + p1;
+              pk[e] = pack_bf16x2(p0, p1);
+            }
+          } else {
+#pragma unroll
+            for (int e = 0; e < 16; ++e) {
+              const int jj = 32 * c + 2 * e;
+              const bool v0 = on && jj < kvalid;
+              const bool v1 = on && jj + 1 < kvalid;
+              const float p0 = v0 ? fast_exp2(fmaf(__uint_as_float(sc[2 * e]), a.scale_log2, -m_off)) : 0.f;
+              const float p1 = v1 ? fast_exp2(fmaf(__uint_as_float(sc[2 * e + 1]), a.scale_log2, -m_off)) : 0.f;
+              sum4[e & 3] += p0 + p1;
+              pk[e] = pack_bf16x2(p0, p1);
+            }
           }
+          tmem_st_32x32b_x16(tSh + 16 * c, pk);
         }
-        tmem_st_32x32b_x32(t_lane + sbuf * kAttnBN + 32 * h, pk);
         const float sum = (sum4[0] + sum4[1]) + (sum4[2] + sum4[3]);
         l_run = (j == 0 ? 0.f : l_run * alpha) + sum;
         m_run = m_use;
@@ -902,21 +1032,21 @@ __global__ void __launch_bounds__(kAttnThreads, 1) sparse_attn_kernel(const Attn
 
         if (j == 0) {
           // next tile's bias operand and the previous tile's epilogue, off the critical path
-          if (!SMALL && tile_exists(lt + 1) && !(ok = stage_bias(lt + 1, tok_next))) break;
-          if (pend_lt >= 0 && !(ok = epilogue(pend_lt, pend_g, pend_tok, pend_l))) break;
+          if (!SMALL && tile_exists(lt + 1) && !(ok = stage_bias(lt + 1))) break;
+          if (pend_lt >= 0 && !(ok = epilogue(pend_lt, pend_g, pend_orow, pend_l))) break;
           pend_lt = -1;
         }
       }
       if (!ok) break;
       pend_lt = lt;
       pend_g = tb.n > 0 ? g - 1 : -1;
-      pend_tok = tok_cur;
+      pend_orow = orow_cur;
       pend_l = l_run;
-      tok_cur = tok_next;
+      orow_cur = orow_next;
     }
     if (ok && pend_lt >= 0) {  // the last tile's row-sum shares
       float m_unused, l_other;
-      if (exchange(0.f, pend_l, m_unused, l_other)) epilogue(pend_lt, pend_g, pend_tok, pend_l + l_other);
+      if (exchange(0.f, pend_l, m_unused, l_other)) epilogue(pend_lt, pend_g, pend_orow, pend_l + l_other);
     }
   }
 
@@ -943,29 +1073,6 @@ struct RelCfg {
   static constexpr int kSmem = 2 * TileGeom<D>::bytes(kNT) + TileGeom<D>::bytes(kAttnBM) +
                                kAttnBM * kStageStride + 64 + 1024;
 };
-
-// Band of one table: the 32 output words (fp16 pairs) relX[j] = S[qc + win - 1 - j]
-// (j < win, zero above) for the fp16 row S (kNT entries) staged at `srow`.
-// With base = qc + win - 64 the band is the reversed window S[base .. base + 63]:
-// it is read as 33 consecutive words from word base >> 1 (the words before the
-// row only feed entries that are masked) and re-paired with byte permutes.
-__device__ __forceinline__ void relbias_band(const uint8_t* srow, int qc, int win, uint32_t (&out)[32]) {
-  const int base = qc + win - 64;
-  const int w0 = base >> 1;  // arithmetic shift: floor
-  const uint32_t* sw = reinterpret_cast<const uint32_t*>(srow) + w0;
-  uint32_t u[33];
-#pragma unroll
-  for (int i = 0; i < 33; ++i) u[i] = sw[i];
-  const bool odd = base & 1;
-#pragma unroll
-  for (int k = 0; k < 32; ++k) {
-    // word k = (relX[2k], relX[2k+1]) = (S[base + 63 - 2k], S[base + 62 - 2k])
-    uint32_t w = odd ? __byte_perm(u[32 - k], u[31 - k], 0x7610) : __byte_perm(u[31 - k], 0u, 0x1032);
-    if (2 * k >= win) w = 0u;
-    else if (2 * k + 1 >= win) w &= 0xffffu;
-    out[k] = w;
-  }
-}
 
 // relbias_kernel: the rel-pos bias operand of every query, once per query.
 // Persistent, two CTAs per SM, tables loaded once per CTA; per 128-query tile of
@@ -1088,8 +1195,8 @@ __global__ void __launch_bounds__(kRelThreads) relbias_kernel(const AttnParams a
 #pragma unroll
           for (int i = 0; i < 4; ++i) sp[i] = make_uint4(hw[4 * i], hw[4 * i + 1], hw[4 * i + 2], hw[4 * i + 3]);
         }
-        if (tab == 0) relbias_band(my_stage, qh, win, bh);
-        else relbias_band(my_stage, qw, win, bw);
+        if (tab == 0) relbias_band<64>(my_stage, qh, win, bh);
+        else relbias_band<64>(my_stage, qw, win, bw);
       }
       // output row [relH | relW] (zero for queries past N) back into my_stage
       uint4* sp = reinterpret_cast<uint4*>(my_stage);
@@ -1194,7 +1301,7 @@ int sparse_attn_fwd(const void* qkv, int64_t ld_qkv, int n_seq, int heads, int w
   p.inv_scale = 1.0f / scale;
   p.n_tiles = (p.N + kAttnBM - 1) / kAttnBM;
   const int64_t total = static_cast<int64_t>(p.n_tiles) * n_seq * heads;
-  if (total > INT32_MAX) return SSAM_ERR_UNSUPPORTED;
+  if (total > INT32_MAX || static_cast<int64_t>(n_seq) * p.N > INT32_MAX) return SSAM_ERR_UNSUPPORTED;
   p.total_tiles = static_cast<int>(total);
   const bool small = win <= 16;
   p.bias_ws = nullptr;

@@ -14,9 +14,11 @@ Two comparisons:
             differently must be closer in fp64 score than the perturbation that
             bf16 operands cause in those scores (measured by running the oracle
             with bf16-rounded GEMM operands, oracle/bf16_emulation.py, and K
-            stored in bf16 as the GPU's qkv GEMM stores it): the gap between the
-            first pair of groups the two orders rank differently may be at most
-            twice the sum of the two groups' score perturbations.
+            stored in bf16 as the GPU's qkv GEMM stores it): the fp32 score gap
+            between the first pair of groups the two orders rank differently may
+            be at most twice the largest perturbation bf16 causes in any group
+            score of that row (one emulated sample estimates the scale of the
+            GPU's own, independent perturbation, not its value per group).
 
 Tolerances (features = the neck output, interm = the residual stream after each
 global block):
@@ -150,9 +152,9 @@ def test_headline_decisions_unforced(cuda_device, arch, ratio):
             i = diff[0]
             a, b = orf[i], og[i]          # the oracle ranks a here, the GPU b
             gap = abs(s32[row, a] - s32[row, b])
-            allow = noise[row, a] + noise[row, b]
+            allow = 2.0 * noise[row].max()     # the row's largest bf16 perturbation of a score, twice
             worst = max(worst, gap / max(allow, 1e-300))
-            if gap > 2.0 * allow:
+            if gap > allow:
                 unexplained += 1
         entry["perms"].append({"win": win, "rows": int(p_gpu.shape[0]), "rows_identical": rows_same,
                                "positions_identical": elem_same, "unexplained_rows": unexplained,
