@@ -63,6 +63,15 @@ __device__ __forceinline__ void cp_async_arrive_noinc(uint64_t* bar) {
   asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(smem_u32(bar)) : "memory");
 }
 
+// TMA copy of a 2-D tile into this CTA's shared memory (no multicast); completion
+// is counted in bytes on `bar`.
+__device__ __forceinline__ void tma_tile_2d(uint32_t dst, const CUtensorMap* map, uint64_t* bar, int x, int y) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
+          dst),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_u32(bar))
+      : "memory");
+}
 __device__ __forceinline__ float fast_exp2(float x) {
   float y;
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
@@ -405,8 +414,12 @@ __device__ __forceinline__ void stage_out_rows(uint32_t tO, uint8_t* stage, int 
   }
 }
 
+// tm_tile: qkv as a [n_seq*N, 3C] bf16 tensor with a 16-channel x 128-row box, the
+// 32-byte swizzle (one box lands as one TileGeom chunk region): a windowed tile's
+// consecutive Q rows.
 template <int D, bool SMALL>
-__global__ void __launch_bounds__(kAttnThreads, 1) sparse_attn_kernel(const AttnParams a) {
+__global__ void __launch_bounds__(kAttnThreads, 1)
+    sparse_attn_kernel(const AttnParams a, const __grid_constant__ CUtensorMap tm_tile) {
   using TG = TileGeom<D>;
   using C = AttnCfg<D, SMALL>;
   using LAY = AttnLayout<D, SMALL>;
@@ -425,7 +438,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1) sparse_attn_kernel(const Attn
   if (tid == 0) {
     mbar_init(&bars[kBarTab], 64);
     for (int i = 0; i < C::kQBuf; ++i) {
-      mbar_init(&bars[kBarQFull + i], 64);
+      mbar_init(&bars[kBarQFull + i], (SMALL && !a.with_diag) ? 32 : 64);  // TMA tile : cp.async lanes
       mbar_init(&bars[kBarQEmpty + i], 1);
     }
     for (int i = 0; i < 2; ++i) {
@@ -478,15 +491,16 @@ __global__ void __launch_bounds__(kAttnThreads, 1) sparse_attn_kernel(const Attn
   if (warp >= 8 && warp < kAttnMmaWarp) {
     // =========================== loader warps ===========================
     // Warp 8 + w (w < kAttnKW): K rows 32w..32w+31 of each block with their
-    // one-hot rows; warp 8 also the rel-pos tables. Warp 8 + kAttnKW + h: V rows
-    // 64h..64h+63 of each block and (LARGE) the staged bias rows 64h..64h+63 of
-    // each tile. The last loader warp: the 128 Q rows of each tile, as soon as
-    // the tile's Q buffer is free.
-    // K / V warps: per tile t, (LARGE) the bias rows of t+1, then K/V(t, blocks). A copy instruction
-    // moves 16 bytes per lane with eight lanes on one 128-byte row segment (four
-    // rows per instruction), then the 32-byte tails (sixteen rows); lane l holds
-    // the tokens of rows l, l+32, ... and hands them out with shuffles. Rows of
-    // padded positions (token < 0) are zero-filled.
+    // one-hot rows and, for windowed grids, each tile's rel-pos bias operand; warp
+    // 8 also the rel-pos tables. Warp 8 + kAttnKW + h: V rows 64h..64h+63 of each
+    // block and (LARGE) the staged bias rows 64h..64h+63 of each tile. The last
+    // loader warp: the 128 Q rows of each tile, as soon as its Q buffer is free.
+    // Key rows (in permuted order) and gathered Q rows: a copy instruction moves
+    // 16 bytes per lane with eight lanes on one 128-byte row segment (four rows
+    // per instruction), then the 32-byte tails (sixteen rows); lane l holds the
+    // tokens of rows l, l+32, ... and hands them out with shuffles; rows of padded
+    // positions (token < 0) are zero-filled. A windowed tile's consecutive Q rows
+    // (raster query order) arrive by TMA, one tile copy per 16-channel chunk.
     const int lw = warp - 8;
     const int kv = lw < kAttnKW ? 0 : (lw < kAttnKW + kAttnVW ? 1 : 2);  // 0: K, 1: V, 2: Q
     const int part = kv == 0 ? lw : lw - kAttnKW;
@@ -555,23 +569,37 @@ __global__ void __launch_bounds__(kAttnThreads, 1) sparse_attn_kernel(const Attn
       cp_async_arrive_noinc(&bars[kBarTab]);
     }
 
+    int q_last[C::kQBuf];  // last tile whose Q rows came by TMA, per buffer (-1: none)
+#pragma unroll
+    for (int i = 0; i < C::kQBuf; ++i) q_last[i] = -1;
+
     auto load_q = [&](int lt_) -> bool {
       const int tile = tile_of<C::kTileGroup>(lt_);
       const int row = tile / a.n_tiles, qtile = tile - row * a.n_tiles;
       const int seq = row / a.heads, head = row - seq * a.heads;
       const int qb = lt_ % C::kQBuf;
       if (q_warp) {
+        const bool tiled = SMALL && !a.with_diag;  // raster query order: consecutive rows
         int qt[4];  // rows 32 i + lane of the tile
 #pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          const int p = qtile * kAttnBM + 32 * i + lane;
-          qt[i] = query_tok(a, row, p);
-        }
+        for (int i = 0; i < 4; ++i) qt[i] = tiled ? -1 : query_tok(a, row, qtile * kAttnBM + 32 * i + lane);
         if (!wait_or_abort(kBarQEmpty + qb, ((lt_ / C::kQBuf) & 1) ^ 1)) return false;
-        copy_rows(sb + L.q + qb * TG::bytes(kAttnBM), kAttnBM, 0, 128, qt,
-                  a.qkv + static_cast<int64_t>(seq) * N * a.ld_qkv, head * D);
-        mbar_arrive(&bars[kBarQFull + qb]);
-        cp_async_arrive_noinc(&bars[kBarQFull + qb]);
+        const uint32_t dst = sb + L.q + qb * TG::bytes(kAttnBM);
+        uint64_t* fb = &bars[kBarQFull + qb];
+        if (tiled) {
+          // one tile copy per 16-channel chunk (lanes 0 .. D/16 - 1); rows past the
+          // tensor read as zero, rows of the next window are computed but not stored
+          if (lane == 0) mbar_arrive_expect_tx(fb, TG::bytes(kAttnBM));
+          __syncwarp();
+          if (lane < D / 16)
+            tma_tile_2d(dst + lane * kAttnBM * 32, &tm_tile, fb, head * D + 16 * lane, seq * N + qtile * kAttnBM);
+          if (lane != 0) mbar_arrive(fb);
+          q_last[qb] = lt_;
+        } else {
+          copy_rows(dst, kAttnBM, 0, 128, qt, a.qkv + static_cast<int64_t>(seq) * N * a.ld_qkv, head * D);
+          mbar_arrive(fb);
+          cp_async_arrive_noinc(fb);
+        }
       }
       if (!SMALL && kv == 1) {  // bias rows row0 .. row0 + kVRows - 1 of the tile (256 B each), two rows per instruction
         if (!wait_or_abort(kBarABSFree, (lt_ & 1) ^ 1)) return false;
@@ -703,6 +731,14 @@ __global__ void __launch_bounds__(kAttnThreads, 1) sparse_attn_kernel(const Attn
       }
     }
     cp_async_wait_all();
+    // No TMA copy of the Q warp may still be landing when the CTA exits: wait
+    // (bounded) for the last phase of each Q buffer it loaded; already complete
+    // unless the kernel is unwinding.
+    if (q_warp && lane == 0) {
+#pragma unroll
+      for (int i = 0; i < C::kQBuf; ++i)
+        if (q_last[i] >= 0) mbar_wait(&bars[kBarQFull + i], (q_last[i] / C::kQBuf) & 1);
+    }
   } else if (warp == kAttnMmaWarp) {
     // =========================== UMMA issuer ===========================
     if (lane == 0) {
@@ -1233,7 +1269,7 @@ size_t sparse_attn_workspace_size(int n_seq, int heads, int win) {
 }
 
 template <int D, bool SMALL>
-static int launch_attn(const AttnParams& p, cudaStream_t stream) {
+static int launch_attn(const AttnParams& p, const CUtensorMap& tm_tile, cudaStream_t stream) {
   const AttnLayout<D, SMALL> L;
   using RC = RelCfg<D, 64>;
   static PerDeviceOnce configured;
@@ -1259,7 +1295,7 @@ static int launch_attn(const AttnParams& p, cudaStream_t stream) {
   // so its 512 TMEM columns are always available.
   const int smem = L.total > 116 * 1024 ? L.total : 116 * 1024;
   const int grid = p.total_tiles < sms ? p.total_tiles : sms;
-  sparse_attn_kernel<D, SMALL><<<grid, kAttnThreads, smem, stream>>>(p);
+  sparse_attn_kernel<D, SMALL><<<grid, kAttnThreads, smem, stream>>>(p, tm_tile);
   return status_from_cuda(cudaGetLastError());
 }
 
@@ -1311,8 +1347,13 @@ int sparse_attn_fwd(const void* qkv, int64_t ld_qkv, int n_seq, int heads, int w
     if (!aligned16(workspace)) return SSAM_ERR_ALIGN;
     p.bias_ws = static_cast<__half*>(workspace);
   }
-  if (d == 64) return small ? launch_attn<64, true>(p, stream) : launch_attn<64, false>(p, stream);
-  return small ? launch_attn<80, true>(p, stream) : launch_attn<80, false>(p, stream);
+  // qkv as a [n_seq * N, 3C] tensor for the windowed tiles' Q rows (TMA tile copies)
+  CUtensorMap tm_tile;
+  const int st = make_tmap_2d_bf16(&tm_tile, qkv, static_cast<uint64_t>(n_seq) * p.N, 3 * static_cast<uint64_t>(C),
+                                   ld_qkv, 16, kAttnBM, CU_TENSOR_MAP_SWIZZLE_32B);
+  if (st != SSAM_OK) return st;
+  if (d == 64) return small ? launch_attn<64, true>(p, tm_tile, stream) : launch_attn<64, false>(p, tm_tile, stream);
+  return small ? launch_attn<80, true>(p, tm_tile, stream) : launch_attn<80, false>(p, tm_tile, stream);
 }
 
 }  // namespace ssam
