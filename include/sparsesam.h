@@ -126,6 +126,17 @@ int ssam_a_shape_mask(int N, int m_block, int n_block, int n_init, int with_diag
  *               token t) is out_rows[s*N + t] (< 0: not stored); NULL stores it
  *               at row s*N + t. Windowed blocks pass the ssam_window_rows map,
  *               which fuses window_unpartition (sam.py:256) into the store.
+ *   grid_h / grid_w : when both > 0 (windowed grids, win <= 16, without the
+ *               diagonal), the n_seq sequences are the window_partition windows
+ *               (sam.py:252; (image, window row, window column) order, zero
+ *               padding at the bottom and right) of images of a grid_h x grid_w
+ *               token grid, and only each window's real tokens are computed as
+ *               queries: the padding tokens' outputs are discarded by
+ *               window_unpartition (sam.py:256) in any case, and without the
+ *               diagonal every query attends to the same key blocks, so the
+ *               results of the real tokens are unchanged. Padding tokens remain
+ *               keys. 0 / 0: every token is a query. n_seq must then be a
+ *               multiple of the windows per image.
  *   workspace : ssam_sparse_attn_workspace_size() bytes (0 for windowed grids,
  *               win <= 16; global grids keep the per-query bias there).
  * d must be 64 or 80; n_block other than 64 / 128 returns SSAM_ERR_UNSUPPORTED.
@@ -134,7 +145,8 @@ size_t ssam_sparse_attn_workspace_size(int n_seq, int heads, int win, int d);
 int ssam_sparse_attn_fwd(const void* qkv, int64_t ld_qkv, int n_seq, int heads, int win, int d,
                          const void* rel_pos_h, const void* rel_pos_w, const int32_t* perm,
                          int n_init_blocks, int n_block, int with_diag, float scale, void* out, int64_t ld_out,
-                         const int32_t* out_rows, void* workspace, size_t workspace_bytes, void* stream);
+                         const int32_t* out_rows, int grid_h, int grid_w, void* workspace,
+                         size_t workspace_bytes, void* stream);
 
 /* ---------------------------------------------------------------------------
  * a10 (selection). Keep set of the Residual-Consistency MLP.

@@ -36,6 +36,7 @@
 // Every wait is bounded; on timeout the CTA raises SSAM_ERR_TIMEOUT and unwinds.
 #include <cuda_fp16.h>
 
+#include <algorithm>
 #include <type_traits>
 
 #include "common.cuh"
@@ -53,6 +54,7 @@ constexpr int kAttnMmaWarp = 8 + kAttnLW;
 constexpr int kAttnThreads = 32 * (kAttnMmaWarp + 1);
 constexpr int kAttnTmemCols = 512;
 constexpr float kRescaleThreshold = 8.0f;  // log2 units
+
 
 __device__ __forceinline__ void cp_async16(uint32_t dst, const void* src, uint32_t src_bytes) {
   asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "r"(src_bytes) : "memory");
@@ -226,8 +228,21 @@ struct AttnParams {
   __nv_bfloat16* out;
   int64_t ld_out;
   const int32_t* out_rows;  // optional output row of (sequence, token)
-  int n_tiles;  // 128-query tiles per row
+  int n_tiles;  // 128-query tiles per row (without query compaction)
   int total_tiles;
+  // Query compaction of windowed grids (wpi > 0): the sequences are the windows of
+  // images of a grid_h x grid_w token grid (window_partition order, padding at the
+  // bottom / right), and only each window's real tokens are queries.
+  int wpi;        // windows per image (0: every token of every sequence is a query)
+  int nww;        // windows per image row
+  int grid_h, grid_w;
+  int img_tiles;  // query tiles per image
+  int row_tiles;  // query tiles of a window row of an image that is not the last
+  int kt_in, kt_col, kt_row, kt_corner;  // tiles per window-head: inner, last column, last row, corner (1 or 2)
+  int nwh;        // windows per image column
+  // fp32 reciprocals of the compaction divisors (fast_div)
+  float r_img_tiles, r_row_tiles, r_span_in, r_span_row, r_win, r_wlast;
+  int w_last;     // real width of the last window column
   __half* bias_ws;  // LARGE: [rows][n_tiles*128][128] fp16 = relH/scale | relW/scale
 };
 
@@ -236,9 +251,79 @@ struct AttnParams {
 // (n < n_init), so a query's result does not depend on its place in the
 // permutation: the queries are then taken in raster order (token p) and no
 // permutation entry is read. With the diagonal, position p holds token perm[p].
-__device__ __forceinline__ int query_tok(const AttnParams& a, int row, int p) {
-  if (p >= a.N) return -1;
-  return a.with_diag ? __ldg(a.perm + static_cast<int64_t>(row) * a.N + p) : p;
+//
+// With query compaction the window's real tokens (the top-left h_real x w_real
+// block of the win x win window) are taken in raster order: query p is token
+// (p / w_real) win + p % w_real, and tiles past the real tokens do not exist.
+// x / d for 0 <= x < 2^24 and d >= 1 with r = fp32(1 / d): the fp32 product errs
+// by less than one (exact for d = 1), so one correction step gives the quotient.
+__device__ __forceinline__ int fast_div(int x, int d, float r) {
+  int q = __float2int_rz(__int2float_rn(x) * r);
+  const int rem = x - q * d;
+  q += (rem >= d) - (rem < 0);
+  return q;
+}
+
+// A query tile: its (sequence, head) row, sequence, head, query tile, and the real tokens
+// of the row's window (n_real of them, w_real per window row; all N tokens and
+// w_real = win without compaction).
+struct TileDesc {
+  int row, seq, head, qtile, n_real, w_real;
+};
+
+// Token of query position p (= qtile * 128 + tile row) of a tile, or -1.
+template <bool CP>
+__device__ __forceinline__ int query_tok(const AttnParams& a, const TileDesc& d, int p) {
+  if (!CP) {
+    if (p >= a.N) return -1;
+    return a.with_diag ? __ldg(a.perm + static_cast<int64_t>(d.row) * a.N + p) : p;
+  }
+  if (p >= d.n_real) return -1;
+  const int ty = fast_div(p, d.w_real, d.w_real == a.win ? a.r_win : a.r_wlast);
+  return ty * a.win + (p - ty * d.w_real);
+}
+
+// Descriptor of global tile `tile`. Without compaction every row has n_tiles
+// tiles. With it, tiles are numbered image by image, window by window (window
+// rows of the image first), head by head, a window-head holding kt = ceil(real
+// tokens / 128) tiles (1 or 2), where the class of a window is inner, last
+// column, last row or corner. Arithmetic only, with reciprocal divisions: each
+// role decodes every tile once.
+template <bool CP>
+__device__ __forceinline__ TileDesc tile_desc(const AttnParams& a, int tile) {
+  TileDesc d;
+  if (!CP) {
+    d.row = tile / a.n_tiles;
+    d.qtile = tile - d.row * a.n_tiles;
+    d.seq = d.row / a.heads;
+    d.head = d.row - d.seq * a.heads;
+    d.n_real = a.N;
+    d.w_real = a.win;
+    return d;
+  }
+  const int img = fast_div(tile, a.img_tiles, a.r_img_tiles);
+  int rem = tile - img * a.img_tiles;
+  int wy = fast_div(rem, a.row_tiles, a.r_row_tiles);
+  if (wy > a.nwh - 1) wy = a.nwh - 1;
+  rem -= wy * a.row_tiles;
+  const bool last_row = wy == a.nwh - 1;
+  const int k_in = last_row ? a.kt_row : a.kt_in, k_col = last_row ? a.kt_corner : a.kt_col;
+  const int span = a.heads * k_in;  // tiles of one window before the last column
+  int wx = fast_div(rem, span, last_row ? a.r_span_row : a.r_span_in);
+  int k = k_in;
+  const bool last_col = wx >= a.nww - 1;
+  if (last_col) {
+    wx = a.nww - 1;
+    k = k_col;
+  }
+  rem -= wx * span;
+  d.head = k == 2 ? rem >> 1 : rem;
+  d.qtile = k == 2 ? rem & 1 : 0;
+  d.seq = img * a.wpi + wy * a.nww + wx;
+  d.row = d.seq * a.heads + d.head;
+  d.w_real = last_col ? a.w_last : a.win;
+  d.n_real = (last_row ? a.grid_h - (a.nwh - 1) * a.win : a.win) * d.w_real;
+  return d;
 }
 
 // Output row of token `tok` of sequence `seq` (-1: not stored); n_seq * N fits
@@ -278,18 +363,21 @@ __device__ __forceinline__ int tile_of(int lt) {
 }
 
 // Walks the flat (tile, key block) sequence of one persistent CTA.
-template <int GT>
+template <int GT, bool CP>
 struct BlockCursor {
   int tile, lt, j, g;
   bool done;
   TileBlocks tb;
+  __device__ void set_blocks(const AttnParams& a) {
+    tb = TileBlocks(a, tile_desc<CP>(a, tile).qtile);
+  }
   __device__ void start(const AttnParams& a) {
     lt = 0;
     tile = tile_of<GT>(0);
     j = 0;
     g = 0;
     done = tile >= a.total_tiles;
-    if (!done) tb = TileBlocks(a, tile % a.n_tiles);
+    if (!done) set_blocks(a);
   }
   __device__ void advance(const AttnParams& a) {
     ++j;
@@ -299,7 +387,7 @@ struct BlockCursor {
       ++lt;
       tile = tile_of<GT>(lt);
       done = tile >= a.total_tiles;
-      if (!done) tb = TileBlocks(a, tile % a.n_tiles);
+      if (!done) set_blocks(a);
     }
   }
 };
@@ -417,7 +505,7 @@ __device__ __forceinline__ void stage_out_rows(uint32_t tO, uint8_t* stage, int 
 // tm_tile: qkv as a [n_seq*N, 3C] bf16 tensor with a 16-channel x 128-row box, the
 // 32-byte swizzle (one box lands as one TileGeom chunk region): a windowed tile's
 // consecutive Q rows.
-template <int D, bool SMALL>
+template <int D, bool SMALL, bool CP>
 __global__ void __launch_bounds__(kAttnThreads, 1)
     sparse_attn_kernel(const AttnParams a, const __grid_constant__ CUtensorMap tm_tile) {
   using TG = TileGeom<D>;
@@ -438,7 +526,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
   if (tid == 0) {
     mbar_init(&bars[kBarTab], 64);
     for (int i = 0; i < C::kQBuf; ++i) {
-      mbar_init(&bars[kBarQFull + i], (SMALL && !a.with_diag) ? 32 : 64);  // TMA tile : cp.async lanes
+      mbar_init(&bars[kBarQFull + i], 32);  // one arrival per lane of the Q warp
       mbar_init(&bars[kBarQEmpty + i], 1);
     }
     for (int i = 0; i < 2; ++i) {
@@ -569,20 +657,20 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       cp_async_arrive_noinc(&bars[kBarTab]);
     }
 
-    int q_last[C::kQBuf];  // last tile whose Q rows came by TMA, per buffer (-1: none)
+    int q_last[C::kQBuf];  // last tile loaded into each Q buffer (-1: none)
 #pragma unroll
     for (int i = 0; i < C::kQBuf; ++i) q_last[i] = -1;
 
     auto load_q = [&](int lt_) -> bool {
-      const int tile = tile_of<C::kTileGroup>(lt_);
-      const int row = tile / a.n_tiles, qtile = tile - row * a.n_tiles;
-      const int seq = row / a.heads, head = row - seq * a.heads;
+      const TileDesc td = tile_desc<CP>(a, tile_of<C::kTileGroup>(lt_));
+      const int row = td.row, qtile = td.qtile, seq = td.seq, head = td.head;
       const int qb = lt_ % C::kQBuf;
       if (q_warp) {
-        const bool tiled = SMALL && !a.with_diag;  // raster query order: consecutive rows
+        // raster query order over whole window rows: the tile's Q rows are consecutive
+        const bool tiled = SMALL && !a.with_diag && td.w_real == win;
         int qt[4];  // rows 32 i + lane of the tile
 #pragma unroll
-        for (int i = 0; i < 4; ++i) qt[i] = tiled ? -1 : query_tok(a, row, qtile * kAttnBM + 32 * i + lane);
+        for (int i = 0; i < 4; ++i) qt[i] = tiled ? -1 : query_tok<CP>(a, td, qtile * kAttnBM + 32 * i + lane);
         if (!wait_or_abort(kBarQEmpty + qb, ((lt_ / C::kQBuf) & 1) ^ 1)) return false;
         const uint32_t dst = sb + L.q + qb * TG::bytes(kAttnBM);
         uint64_t* fb = &bars[kBarQFull + qb];
@@ -594,12 +682,13 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
           if (lane < D / 16)
             tma_tile_2d(dst + lane * kAttnBM * 32, &tm_tile, fb, head * D + 16 * lane, seq * N + qtile * kAttnBM);
           if (lane != 0) mbar_arrive(fb);
-          q_last[qb] = lt_;
         } else {
           copy_rows(dst, kAttnBM, 0, 128, qt, a.qkv + static_cast<int64_t>(seq) * N * a.ld_qkv, head * D);
-          mbar_arrive(fb);
           cp_async_arrive_noinc(fb);
         }
+#pragma unroll
+        for (int i = 0; i < C::kQBuf; ++i)
+          if (i == qb) q_last[i] = lt_;
       }
       if (!SMALL && kv == 1) {  // bias rows row0 .. row0 + kVRows - 1 of the tile (256 B each), two rows per instruction
         if (!wait_or_abort(kBarABSFree, (lt_ & 1) ^ 1)) return false;
@@ -624,16 +713,13 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     // relX[j] = P_X[qc - j + win - 1] read as a reversed window, then the two
     // bands go to A_bias[lt_ & 1] in TMEM. The buffer's previous reader, QK^T of
     // tile lt_ - 2, completed before the [P_H | P_W] commit of tile lt_.
-    auto stage_bias_rows = [&](int lt_) -> bool {
+    auto stage_bias_rows = [&](int lt_, const TileDesc& td) -> bool {
       if constexpr (!SMALL) {
         return true;
       } else {
       const int r = (warp & 3) * 32 + lane;
       const uint32_t t_lane = tmem + (static_cast<uint32_t>((warp & 3) * 32) << 16);
-      const int tile = tile_of<C::kTileGroup>(lt_);
-      const int row = tile / a.n_tiles, qtile = tile - row * a.n_tiles;
-      const int p = qtile * kAttnBM + r;
-      const int t = query_tok(a, row, p);
+      const int t = query_tok<CP>(a, td, td.qtile * kAttnBM + r);
       const int qh = t >= 0 ? t / win : 0;
       const int qw = t >= 0 ? t - qh * win : 0;
       if (!wait_or_abort(kBarPHFull, lt_ & 1)) return false;
@@ -668,9 +754,8 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     if (kv < 2 && tile_exists(0)) ok = load_q(0);
     for (int lt = 0; kv < 2 && ok && tile_exists(lt) && !*abort_flag; ++lt) {
       if (tile_exists(lt + 1) && !(ok = load_q(lt + 1))) break;
-      const int tile = tile_of<C::kTileGroup>(lt);
-      const int row = tile / a.n_tiles, qtile = tile - row * a.n_tiles;
-      const int seq = row / a.heads, head = row - seq * a.heads;
+      const TileDesc td = tile_desc<CP>(a, tile_of<C::kTileGroup>(lt));
+      const int row = td.row, qtile = td.qtile, seq = td.seq, head = td.head;
       const int32_t* perm = a.perm + static_cast<int64_t>(row) * N;
       const __nv_bfloat16* base = a.qkv + static_cast<int64_t>(seq) * N * a.ld_qkv;
       const int xcol = (kv == 0 ? a.C : 2 * a.C) + head * D;
@@ -727,13 +812,13 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       }
       // the tile's bias operand once its key rows are on their way
       if constexpr (SMALL) {
-        if (ok && kv == 0 && !(ok = stage_bias_rows(lt))) break;
+        if (ok && kv == 0 && !(ok = stage_bias_rows(lt, td))) break;
       }
     }
     cp_async_wait_all();
     // No TMA copy of the Q warp may still be landing when the CTA exits: wait
-    // (bounded) for the last phase of each Q buffer it loaded; already complete
-    // unless the kernel is unwinding.
+    // (bounded) for the last phase of each Q buffer (whichever path filled it);
+    // already complete unless the kernel is unwinding.
     if (q_warp && lane == 0) {
 #pragma unroll
       for (int i = 0; i < C::kQBuf; ++i)
@@ -762,7 +847,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         umma_commit(&bars[kBarPHFull]);
         return true;
       };
-      auto issue_qk = [&](const BlockCursor<C::kTileGroup>& c) -> bool {
+      auto issue_qk = [&](const BlockCursor<C::kTileGroup, CP>& c) -> bool {
         if (c.j == 0) {
           if constexpr (SMALL) {
             if (tile_exists(c.lt + 1) && !issue_ph(c.lt + 1)) return false;
@@ -802,7 +887,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         if (c.j == c.tb.n - 1) umma_commit(&bars[kBarQEmpty + c.lt % C::kQBuf]);
         return true;
       };
-      auto issue_pv = [&](const BlockCursor<C::kTileGroup>& c) -> bool {
+      auto issue_pv = [&](const BlockCursor<C::kTileGroup, CP>& c) -> bool {
         if (!wait_or_abort(kBarPFull + (c.g & 1), (c.g >> 1) & 1)) return false;
         const int ob = c.lt % C::kO;
         if (c.j == 0 && !wait_or_abort(kBarOFree + ob, ((c.lt / C::kO) & 1) ^ 1)) return false;
@@ -825,7 +910,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       };
 
       if (ok && SMALL && tile_exists(0)) ok = issue_ph(0);
-      BlockCursor<C::kTileGroup> cq, cp;
+      BlockCursor<C::kTileGroup, CP> cq, cp;
       cq.start(a);
       cp.start(a);
       while (ok && !cp.done) {
@@ -894,10 +979,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     // This half's O columns / l of tile lt_, stored at the raster token
     // (inverse permutation and head merge)
     // (orow: the output row of this thread's query, looked up a tile ahead)
-    auto epilogue = [&](int lt_, int g_last, int orow, float l) -> bool {
-      const int tile = tile_of<C::kTileGroup>(lt_);
-      const int row = tile / a.n_tiles;
-      const int head = row % a.heads;
+    auto epilogue = [&](int lt_, int g_last, int orow, int head, float l) -> bool {
       if (g_last >= 0 && !wait_or_abort(kBarODone + (g_last & 1), (g_last >> 1) & 1)) return false;
       tc_fence_after();
       const float inv_l = l > 0.f ? 1.f / l : 0.f;
@@ -937,29 +1019,30 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       mbar_arrive(&bars[kBarOFree + lt_ % C::kO]);
       return true;
     };
-    // Output row of this thread's query of tile lt_.
-    auto query_row = [&](int lt_) -> int {
-      const int tile = tile_of<C::kTileGroup>(lt_);
-      const int row = tile / a.n_tiles, qtile = tile - row * a.n_tiles;
-      return query_out_row(a, row / a.heads, query_tok(a, row, qtile * kAttnBM + r));
+    // Tile lt_ once per tile (decoded a tile ahead): its query tile, its head and
+    // the output row of this thread's query.
+    auto tile_info = [&](int lt_, int& qtile, int& head) -> int {
+      const TileDesc td = tile_desc<CP>(a, tile_of<C::kTileGroup>(lt_));
+      qtile = td.qtile;
+      head = td.head;
+      return query_out_row(a, td.seq, query_tok<CP>(a, td, td.qtile * kAttnBM + r));
     };
 
     bool ok = true;
-    int orow_cur = -1, orow_next = -1;
+    int orow_cur = -1, orow_next = -1, qt_cur = 0, qt_next = 0, hd_cur = 0, hd_next = 0;
     if (tile_exists(0)) {
       if constexpr (!SMALL) ok = stage_bias(0);
-      orow_cur = query_row(0);
+      orow_cur = tile_info(0, qt_cur, hd_cur);
     }
-    int pend_lt = -1, pend_g = -1, pend_orow = -1;  // deferred epilogue
+    int pend_lt = -1, pend_g = -1, pend_orow = -1, pend_head = 0;  // deferred epilogue
     float pend_l = 0.f;  // this half's share of the pending tile's row sum
     int g = 0;
     for (int lt = 0; ok && tile_exists(lt); ++lt) {
-      const int tile = tile_of<C::kTileGroup>(lt);
-      const int qtile = tile % a.n_tiles;
+      const int qtile = qt_cur;
       const TileBlocks tb(a, qtile);
       const int my_mb = 2 * qtile + (r >= 64 ? 1 : 0);
       const uint32_t tO = t_lane + C::kTmO + (lt % C::kO) * D;
-      if (tile_exists(lt + 1)) orow_next = query_row(lt + 1);
+      if (tile_exists(lt + 1)) orow_next = tile_info(lt + 1, qt_next, hd_next);
       float m_run = -INFINITY, l_run = 0.f;  // l_run: this half's share of the row sum
       for (int j = 0; j < tb.n; ++j, ++g) {
         const int sbuf = g % C::kS;
@@ -1069,7 +1152,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         if (j == 0) {
           // next tile's bias operand and the previous tile's epilogue, off the critical path
           if (!SMALL && tile_exists(lt + 1) && !(ok = stage_bias(lt + 1))) break;
-          if (pend_lt >= 0 && !(ok = epilogue(pend_lt, pend_g, pend_orow, pend_l))) break;
+          if (pend_lt >= 0 && !(ok = epilogue(pend_lt, pend_g, pend_orow, pend_head, pend_l))) break;
           pend_lt = -1;
         }
       }
@@ -1077,12 +1160,15 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       pend_lt = lt;
       pend_g = tb.n > 0 ? g - 1 : -1;
       pend_orow = orow_cur;
+      pend_head = hd_cur;
       pend_l = l_run;
       orow_cur = orow_next;
+      qt_cur = qt_next;
+      hd_cur = hd_next;
     }
     if (ok && pend_lt >= 0) {  // the last tile's row-sum shares
       float m_unused, l_other;
-      if (exchange(0.f, pend_l, m_unused, l_other)) epilogue(pend_lt, pend_g, pend_orow, pend_l + l_other);
+      if (exchange(0.f, pend_l, m_unused, l_other)) epilogue(pend_lt, pend_g, pend_orow, pend_head, pend_l + l_other);
     }
   }
 
@@ -1268,14 +1354,14 @@ size_t sparse_attn_workspace_size(int n_seq, int heads, int win) {
   return static_cast<size_t>(n_seq) * heads * n_tiles * kAttnBM * 128 * 2;
 }
 
-template <int D, bool SMALL>
+template <int D, bool SMALL, bool CP>
 static int launch_attn(const AttnParams& p, const CUtensorMap& tm_tile, cudaStream_t stream) {
   const AttnLayout<D, SMALL> L;
   using RC = RelCfg<D, 64>;
   static PerDeviceOnce configured;
   const int dev = current_device();
   const int st = configured.run(dev, [&L] {
-    if (cudaFuncSetAttribute(sparse_attn_kernel<D, SMALL>, cudaFuncAttributeMaxDynamicSharedMemorySize, L.total) !=
+    if (cudaFuncSetAttribute(sparse_attn_kernel<D, SMALL, CP>, cudaFuncAttributeMaxDynamicSharedMemorySize, L.total) !=
         cudaSuccess)
       return SSAM_ERR_CUDA;
     if (!SMALL && cudaFuncSetAttribute(relbias_kernel<D, 64>, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -1295,14 +1381,14 @@ static int launch_attn(const AttnParams& p, const CUtensorMap& tm_tile, cudaStre
   // so its 512 TMEM columns are always available.
   const int smem = L.total > 116 * 1024 ? L.total : 116 * 1024;
   const int grid = p.total_tiles < sms ? p.total_tiles : sms;
-  sparse_attn_kernel<D, SMALL><<<grid, kAttnThreads, smem, stream>>>(p, tm_tile);
+  sparse_attn_kernel<D, SMALL, CP><<<grid, kAttnThreads, smem, stream>>>(p, tm_tile);
   return status_from_cuda(cudaGetLastError());
 }
 
 int sparse_attn_fwd(const void* qkv, int64_t ld_qkv, int n_seq, int heads, int win, int d, const void* rel_pos_h,
                     const void* rel_pos_w, const int32_t* perm, int n_init_blocks, int n_block, int with_diag,
-                    float scale, void* out, int64_t ld_out, const int32_t* out_rows, void* workspace,
-                    size_t workspace_bytes, cudaStream_t stream) {
+                    float scale, void* out, int64_t ld_out, const int32_t* out_rows, int grid_h, int grid_w,
+                    void* workspace, size_t workspace_bytes, cudaStream_t stream) {
   if (qkv == nullptr || rel_pos_h == nullptr || rel_pos_w == nullptr || perm == nullptr || out == nullptr)
     return SSAM_ERR_INVALID;
   if (n_seq <= 0 || heads <= 0 || win <= 0 || n_init_blocks < 0) return SSAM_ERR_INVALID;
@@ -1336,10 +1422,47 @@ int sparse_attn_fwd(const void* qkv, int64_t ld_qkv, int n_seq, int heads, int w
   p.out_rows = out_rows;
   p.inv_scale = 1.0f / scale;
   p.n_tiles = (p.N + kAttnBM - 1) / kAttnBM;
-  const int64_t total = static_cast<int64_t>(p.n_tiles) * n_seq * heads;
+  const bool small = win <= 16;
+  int64_t total = static_cast<int64_t>(p.n_tiles) * n_seq * heads;
+  // query compaction: windowed grids without the diagonal whose image grid is known
+  p.wpi = p.nww = p.grid_h = p.grid_w = p.img_tiles = p.row_tiles = 0;
+  p.kt_in = p.kt_col = p.kt_row = p.kt_corner = 0;
+  if (grid_h < 0 || grid_w < 0) return SSAM_ERR_INVALID;
+  if (small && !with_diag && grid_h > 0 && grid_w > 0) {
+    const int64_t nwh = (grid_h + win - 1) / win, nww = (grid_w + win - 1) / win;
+    if (nwh * nww > INT32_MAX / 4) return SSAM_ERR_UNSUPPORTED;
+    const int wpi = static_cast<int>(nwh * nww);
+    if (n_seq % wpi != 0) return SSAM_ERR_INVALID;  // whole images of windows
+    const int h_last = grid_h - static_cast<int>(nwh - 1) * win, w_last = grid_w - static_cast<int>(nww - 1) * win;
+    auto tiles = [](int hr, int wr) { return (hr * wr + kAttnBM - 1) / kAttnBM; };
+    p.kt_in = tiles(win, win);
+    p.nwh = static_cast<int>(nwh);
+    p.w_last = w_last;
+    p.kt_col = tiles(win, w_last);
+    p.kt_row = tiles(h_last, win);
+    p.kt_corner = tiles(h_last, w_last);
+    const int64_t row_tiles = heads * ((nww - 1) * p.kt_in + p.kt_col);
+    const int64_t img_tiles = (nwh - 1) * row_tiles + heads * ((nww - 1) * p.kt_row + p.kt_corner);
+    if (img_tiles > INT32_MAX) return SSAM_ERR_UNSUPPORTED;
+    p.wpi = wpi;
+    p.nww = static_cast<int>(nww);
+    p.grid_h = grid_h;
+    p.grid_w = grid_w;
+    p.row_tiles = static_cast<int>(row_tiles);
+    p.img_tiles = static_cast<int>(img_tiles);
+    auto rcp = [](int64_t v) { return static_cast<float>(1.0 / static_cast<double>(v)); };
+    p.r_img_tiles = rcp(img_tiles);
+    p.r_row_tiles = rcp(row_tiles);
+    p.r_span_in = rcp(static_cast<int64_t>(heads) * p.kt_in);
+    p.r_span_row = rcp(static_cast<int64_t>(heads) * p.kt_row);
+    p.r_win = rcp(win);
+    p.r_wlast = rcp(w_last);
+    // the decode's fp32 divisions are exact below 2^24
+    if (static_cast<int64_t>(n_seq) * heads * 2 >= (1 << 24)) return SSAM_ERR_UNSUPPORTED;
+    total = img_tiles * (n_seq / wpi);
+  }
   if (total > INT32_MAX || static_cast<int64_t>(n_seq) * p.N > INT32_MAX) return SSAM_ERR_UNSUPPORTED;
   p.total_tiles = static_cast<int>(total);
-  const bool small = win <= 16;
   p.bias_ws = nullptr;
   if (!small) {
     const size_t need = sparse_attn_workspace_size(n_seq, heads, win);
@@ -1352,8 +1475,12 @@ int sparse_attn_fwd(const void* qkv, int64_t ld_qkv, int n_seq, int heads, int w
   const int st = make_tmap_2d_bf16(&tm_tile, qkv, static_cast<uint64_t>(n_seq) * p.N, 3 * static_cast<uint64_t>(C),
                                    ld_qkv, 16, kAttnBM, CU_TENSOR_MAP_SWIZZLE_32B);
   if (st != SSAM_OK) return st;
-  if (d == 64) return small ? launch_attn<64, true>(p, tm_tile, stream) : launch_attn<64, false>(p, tm_tile, stream);
-  return small ? launch_attn<80, true>(p, tm_tile, stream) : launch_attn<80, false>(p, tm_tile, stream);
+  const bool cp = p.wpi > 0;  // query compaction (windowed grids with an image grid)
+  if (d == 64)
+    return small ? (cp ? launch_attn<64, true, true>(p, tm_tile, stream) : launch_attn<64, true, false>(p, tm_tile, stream))
+                 : launch_attn<64, false, false>(p, tm_tile, stream);
+  return small ? (cp ? launch_attn<80, true, true>(p, tm_tile, stream) : launch_attn<80, true, false>(p, tm_tile, stream))
+               : launch_attn<80, false, false>(p, tm_tile, stream);
 }
 
 }  // namespace ssam

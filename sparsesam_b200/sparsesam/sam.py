@@ -153,11 +153,12 @@ def _get_perm(info: dict, key: tuple, qkv: torch.Tensor, n_seq: int, heads: int,
 
 def _attention_core(attn, xn: torch.Tensor, n_seq: int, win: int, ratio: float, is_global: bool,
                     n_block: int, qkv: torch.Tensor | None = None, out: torch.Tensor | None = None,
-                    out_rows: torch.Tensor | None = None):
+                    out_rows: torch.Tensor | None = None, grid: tuple[int, int] | None = None):
     """xn: bf16 (n_seq*win*win, C) -> (o bf16 (rows, C) raster order, perm, inv_perm).
 
     With `qkv` given (already projected, e.g. from the real tokens only), xn is
-    not used; `out` / `out_rows` place the attention rows (see ops.sparse_attn)."""
+    not used; `out` / `out_rows` place the attention rows and `grid` (the image token grid of
+    windowed sequences) limits the queries to real tokens (see ops.sparse_attn)."""
     w = _attn_weights(attn)
     heads = attn.num_heads
     C = w.proj_w.shape[1]
@@ -170,7 +171,7 @@ def _attention_core(attn, xn: torch.Tensor, n_seq: int, win: int, ratio: float, 
     perm, inv_perm, _ = _get_perm(info, (win, ratio, n_block, perm_mode), qkv, n_seq, heads, win, d)
     n_init = ops.a_shape_n_init(N, n_block, ratio, is_global)          # sam.py:219-223
     o = ops.sparse_attn(qkv, n_seq, heads, win, d, w.rel_h, w.rel_w, perm, n_init, is_global,
-                        attn.scale, out=out, out_rows=out_rows, n_block=n_block)   # sam.py:206-232
+                        attn.scale, out=out, out_rows=out_rows, n_block=n_block, grid=grid)   # sam.py:206-232
     return o, perm, inv_perm
 
 
@@ -253,7 +254,7 @@ class ToMeSAMBlock(Block):
             ops.fill_pad_rows(qkv, rows, aw.qkv_b)
             o = torch.empty(B * H * W, C, dtype=torch.bfloat16, device=xr.device)
             _attention_core(self.attn, None, n_win, ws, ratio, False, _FA2_N_BLOCK_LOCAL, qkv=qkv, out=o,
-                            out_rows=rows)
+                            out_rows=rows, grid=(H, W))
             ops.gemm_bf16(o, aw.proj_w, aw.proj_b, epilogue=ops.SSAM_EPI_ADD_F32, out=xr)     # + residual
         else:
             if H != W:

@@ -177,3 +177,37 @@ def test_128_token_mask_blocks(cuda_device, d, win, is_global, ratio):
     assert err.max().item() < 3e-2, err.max().item()
     assert err.mean().item() < 3e-3
     assert ops.device_error() == 0
+
+
+@pytest.mark.parametrize("d", [64, 80])
+@pytest.mark.parametrize("B,H,W,ws", [(2, 20, 20, 14), (1, 64, 64, 14), (3, 9, 13, 7), (2, 16, 30, 14)])
+def test_query_compaction_matches_every_token(cuda_device, d, B, H, W, ws):
+    """Windowed grids with the image grid given compute only the real tokens of each
+    window as queries (padding tokens stay keys); every stored row equals the run that
+    computes all tokens, bit for bit, and matches the fp32 oracle."""
+    heads = 2
+    g = torch.Generator().manual_seed(11)
+    rows = ops.window_rows(B, H, W, ws, cuda_device)
+    n_win, N, C = rows.numel() // (ws * ws), ws * ws, heads * d
+    qkv = torch.randn(n_win * N, 3 * C, generator=g).to(torch.bfloat16).to(cuda_device)
+    th = (torch.randn(2 * ws - 1, d, generator=g) * 0.3).to(torch.bfloat16).to(cuda_device)
+    tw = (torch.randn(2 * ws - 1, d, generator=g) * 0.3).to(torch.bfloat16).to(cuda_device)
+    perm = torch.stack([torch.randperm(N, generator=g) for _ in range(n_win * heads)]).to(torch.int32)
+    n_init = order.a_shape_n_init(N, 64, 0.4, False)
+    out_all = torch.full((B * H * W, C), 3.0, device=cuda_device, dtype=torch.bfloat16)
+    out_cmp = out_all.clone()
+    ops.sparse_attn(qkv, n_win, heads, ws, d, th, tw, perm.to(cuda_device), n_init, False, d ** -0.5,
+                    out=out_all, out_rows=rows)
+    ops.sparse_attn(qkv, n_win, heads, ws, d, th, tw, perm.to(cuda_device), n_init, False, d ** -0.5,
+                    out=out_cmp, out_rows=rows, grid=(H, W))
+    assert ops.device_error() == 0
+    assert torch.equal(out_all, out_cmp)
+    q, k, v = qkv.float().cpu().view(n_win, N, 3, heads, d).permute(2, 0, 3, 1, 4).reshape(3, n_win * heads, N, d)
+    ref = sparse_attention(q, k, v, th.float().cpu(), tw.float().cpu(), perm, ws, n_init, False, d ** -0.5,
+                           round_tables_fp16=False)
+    ref = ref.view(n_win, heads, N, d).permute(0, 2, 1, 3).reshape(n_win * N, C)
+    real = rows.cpu() >= 0
+    got = torch.empty(n_win * N, C)
+    got[real] = out_cmp.float().cpu()[rows.cpu()[real].long()]
+    err = (got[real] - ref[real]).abs()
+    assert err.max().item() < 3e-2 and err.mean().item() < 3e-3
