@@ -44,6 +44,18 @@ RATIO = 0.3
 IMG = 1024
 
 
+def encoder_stream_gb(arch: str, batch: int, img: int = 1024) -> tuple:
+    """(bf16 weights of the blocks, one block's activations) in GB for `batch` images:
+    12 C^2 weights per block; the fp32 residual rows plus the bf16 qkv rows of the
+    padded 14x14 window grid."""
+    from sparsesam_b200.host import VIT_CONFIGS
+    cfg = VIT_CONFIGS[arch]
+    C, depth = cfg["embed_dim"], cfg["depth"]
+    T = (img // 16) ** 2
+    Tp = (-(-(img // 16) // 14) * 14) ** 2
+    return depth * 12 * C * C * 2 / 1e9, batch * (T * C * 4 + Tp * 3 * C * 2) / 1e9
+
+
 def encoder_flops(arch: str, ratio: float, img: int = 1024, mlp_merge: bool = True) -> float:
     """Algorithmic FLOPs per image, valid-token convention: qkv/proj on the real
     tokens, windowed attention over valid queries x enabled keys, global attention
@@ -338,9 +350,12 @@ def run_ours(args) -> None:
         return
     traffic = None
     tpath = os.path.join(REPO, "profiles", "gemm_traffic.json")
-    if os.path.exists(tpath):
+    if arch == "vit_h" and os.path.exists(tpath):
+        # captured on ViT-H at batch 8; GEMM rows (tokens) and with them the bytes grow with the batch
         with open(tpath) as f:
-            traffic = json.load(f).get("bytes_per_launch")
+            t = json.load(f)
+        traffic = t["bytes_per_launch_at_batch8"] * batch / t["measured_at_batch"]
+    img_mb = x_host.numel() * 4 / 1e6
     line = {
         "metric": METRIC if (arch, ratio) == (ARCH, RATIO) else
         f"SAM {arch} encoder images/sec @1024², d={ratio}, bf16, B200; % TC peak",
@@ -352,7 +367,8 @@ def run_ours(args) -> None:
                                f"{batch} images per GPU, seed-0 random weights",
                    "global_batch": batch * world, "per_gpu_batch": batch, "ratio": ratio,
                    "parallelism": f"dp{world} (independent image shards, no collective)",
-                   "l2": "inputs larger than L2 (805 MB of images and GBs of activations per step)"},
+                   "l2": "inputs larger than L2 (126 MB): each step streams {:.0f} MB of images, {:.2f} GB of "
+                         "bf16 weights and {:.2f} GB of block activations".format(img_mb, *encoder_stream_gb(arch, batch))},
         "e2e": {"value": e2e, "unit": "images/s", "h2d_bytes_per_step": x_host.numel() * 4,
                 "d2h_bytes_per_step": feat_host.numel() * 4},
         "gpu_launches": launches,
