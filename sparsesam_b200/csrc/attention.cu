@@ -463,42 +463,49 @@ __device__ __forceinline__ void stage_f16_row(uint8_t* dst, const uint32_t* v, f
   }
 }
 
-// Epilogue of one softmax warp for NC O columns (a multiple of 16) starting at TMEM
-// column tO: each lane's row, times `scale`, as bf16 into its STRIDE-byte row of
+// Epilogue of one softmax warp for nc16 16-column chunks of O starting at TMEM
+// column tO: each lane's row, times `scale`, as bf16 into its `stride`-byte row of
 // the warp's staging block; then the warp stores the block row segment by row
-// segment (NC / 8 lanes of 16 bytes per row, four to five rows per instruction)
-// to out row orow of each lane (< 0: not stored), columns starting at obase.
-template <int NC, int STRIDE>
-__device__ __forceinline__ void stage_out_rows(uint32_t tO, uint8_t* stage, int orow, float scale,
-                                               __nv_bfloat16* obase, int64_t ld_out) {
-  static_assert(NC % 16 == 0 && NC <= 64, "16-column TMEM loads, at most two x32 loads");
+// segment (2 nc16 lanes of 16 bytes per row) to out row orow of each lane (< 0: not
+// stored), columns starting at obase. Both loops stay rolled: the epilogue runs once
+// per tile, and its code is fetched anew each time.
+__device__ __forceinline__ void stage_out_rows(uint32_t tO, int nc16, uint8_t* stage, int stride, int orow,
+                                               float scale, __nv_bfloat16* obase, int64_t ld_out) {
   const int lane = static_cast<int>(threadIdx.x & 31);
-  uint32_t v[NC];
-  if constexpr (NC >= 32) {
-    tmem_ld_32x32b_x32(tO, *reinterpret_cast<uint32_t(*)[32]>(&v[0]));
-    if constexpr (NC == 64) tmem_ld_32x32b_x32(tO + 32, *reinterpret_cast<uint32_t(*)[32]>(&v[32]));
-    if constexpr (NC == 48) tmem_ld_32x32b_x16(tO + 32, *reinterpret_cast<uint32_t(*)[16]>(&v[32]));
-  } else {
-    tmem_ld_32x32b_x16(tO, *reinterpret_cast<uint32_t(*)[16]>(&v[0]));
-  }
-  tmem_ld_wait();
   __syncwarp();  // the previous tile's row segments have been read out of the block
-  uint4* srow = reinterpret_cast<uint4*>(stage + lane * STRIDE);
+  uint8_t* srow = stage + lane * stride;
+  const float2 sc2 = make_float2(scale, scale);
+#pragma unroll 1
+  for (int c = 0; c < nc16; ++c) {
+    uint32_t v[16];
+    tmem_ld_32x32b_x16(tO + 16 * c, v);
+    tmem_ld_wait();
+    uint32_t w[8];
 #pragma unroll
-  for (int c = 0; c < NC / 8; ++c)
-    srow[c] = make_uint4(pack_bf16x2(__uint_as_float(v[8 * c]) * scale, __uint_as_float(v[8 * c + 1]) * scale),
-                         pack_bf16x2(__uint_as_float(v[8 * c + 2]) * scale, __uint_as_float(v[8 * c + 3]) * scale),
-                         pack_bf16x2(__uint_as_float(v[8 * c + 4]) * scale, __uint_as_float(v[8 * c + 5]) * scale),
-                         pack_bf16x2(__uint_as_float(v[8 * c + 6]) * scale, __uint_as_float(v[8 * c + 7]) * scale));
+    for (int e = 0; e < 8; ++e) {
+      const float2 o = mul2(make_float2(__uint_as_float(v[2 * e]), __uint_as_float(v[2 * e + 1])), sc2);
+      w[e] = pack_bf16x2(o.x, o.y);
+    }
+    uint4* d = reinterpret_cast<uint4*>(srow + 32 * c);
+    d[0] = make_uint4(w[0], w[1], w[2], w[3]);
+    d[1] = make_uint4(w[4], w[5], w[6], w[7]);
+  }
   __syncwarp();
-  constexpr int kCh = NC / 8;  // 16-byte chunks per row segment
-#pragma unroll
-  for (int k = 0; k < kCh; ++k) {
-    const int i = lane + 32 * k;
-    const int rr = i / kCh, c = i - rr * kCh;
+  // round k: lane l moves chunk (l + 32 k) % kch of block row (l + 32 k) / kch
+  const int kch = 2 * nc16;
+  int rr = lane / kch, c = lane - rr * kch;
+  const int drr = 32 / kch, dc = 32 - drr * kch;
+#pragma unroll 1
+  for (int k = 0; k < kch; ++k) {
     const int dst_row = __shfl_sync(0xffffffffu, orow, rr);
-    const uint4 val = *reinterpret_cast<const uint4*>(stage + rr * STRIDE + c * 16);
+    const uint4 val = *reinterpret_cast<const uint4*>(stage + rr * stride + c * 16);
     if (dst_row >= 0) *reinterpret_cast<uint4*>(obase + static_cast<int64_t>(dst_row) * ld_out + c * 8) = val;
+    rr += drr;
+    c += dc;
+    if (c >= kch) {
+      c -= kch;
+      ++rr;
+    }
   }
 }
 
@@ -751,9 +758,11 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     if (kv == 2) {  // Q warp: every tile as soon as its Q buffer is free
       for (int lt = 0; ok && tile_exists(lt) && !*abort_flag; ++lt) ok = load_q(lt);
     }
-    if (kv < 2 && tile_exists(0)) ok = load_q(0);
+    // (K / V warps of windowed grids load no Q and no staged bias rows: they skip
+    // load_q, whose code would otherwise be inlined into their loop)
+    if (!SMALL && kv < 2 && tile_exists(0)) ok = load_q(0);
     for (int lt = 0; kv < 2 && ok && tile_exists(lt) && !*abort_flag; ++lt) {
-      if (tile_exists(lt + 1) && !(ok = load_q(lt + 1))) break;
+      if (!SMALL && tile_exists(lt + 1) && !(ok = load_q(lt + 1))) break;
       const TileDesc td = tile_desc<CP>(a, tile_of<C::kTileGroup>(lt));
       const int row = td.row, qtile = td.qtile, seq = td.seq, head = td.head;
       const int32_t* perm = a.perm + static_cast<int64_t>(row) * N;
@@ -989,12 +998,8 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         // staging block -> whole row segments stored by consecutive lanes.
         uint8_t* stage = smem + L.ostage + (warp & 3) * 32 * (C::kOStride0 + C::kOStride1) +
                          (h ? 32 * C::kOStride0 : 0);
-        __nv_bfloat16* obase = a.out + head * D + oc0;
-        if (h == 0)
-          stage_out_rows<C::kOSplit, C::kOStride0>(tO, stage, orow, g_last >= 0 ? inv_l : 0.f, obase, a.ld_out);
-        else
-          stage_out_rows<D - C::kOSplit, C::kOStride1>(tO + C::kOSplit, stage, orow, g_last >= 0 ? inv_l : 0.f,
-                                                       obase, a.ld_out);
+        stage_out_rows(tO + oc0, (oc1 - oc0) / 16, stage, h ? C::kOStride1 : C::kOStride0, orow,
+                       g_last >= 0 ? inv_l : 0.f, a.out + head * D + oc0, a.ld_out);
       } else {
         uint4* dst = orow >= 0 ? reinterpret_cast<uint4*>(a.out + static_cast<int64_t>(orow) * a.ld_out + head * D)
                                : nullptr;
@@ -1113,8 +1118,10 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         // pass 2: P = exp2(s * scale log2e - m) as bf16 pairs, 32 keys at a time (S re-read
         // from TMEM): keys 32c .. 32c + 31 of this half go to its columns 16c .. 16c + 15,
         // which pass 2 has already read
+        float2 sum2[2] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
         float sum4[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll
+        const float2 sl2 = make_float2(a.scale_log2, a.scale_log2), nm2 = make_float2(-m_off, -m_off);
+#pragma unroll 1
         for (int c = 0; c < 2; ++c) {
           uint32_t sc[32];
           tmem_ld_32x32b_x32(tSh + 32 * c, sc);
@@ -1123,10 +1130,10 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
           if (full) {
 #pragma unroll
             for (int e = 0; e < 16; ++e) {
-              const float p0 = fast_exp2(fmaf(__uint_as_float(sc[2 * e]), a.scale_log2, -m_off));
-              const float p1 = fast_exp2(fmaf(__uint_as_float(sc[2 * e + 1]), a.scale_log2, -m_off));
-              sum4[e & 3] += p0 + p1;
-              pk[e] = pack_bf16x2(p0, p1);
+              const float2 x = fma2(make_float2(__uint_as_float(sc[2 * e]), __uint_as_float(sc[2 * e + 1])), sl2, nm2);
+              const float2 p = make_float2(fast_exp2(x.x), fast_exp2(x.y));
+              sum2[e & 1] = add2(sum2[e & 1], p);
+              pk[e] = pack_bf16x2(p.x, p.y);
             }
           } else {
 #pragma unroll
@@ -1142,7 +1149,8 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
           }
           tmem_st_32x32b_x16(tSh + 16 * c, pk);
         }
-        const float sum = (sum4[0] + sum4[1]) + (sum4[2] + sum4[3]);
+        const float2 s2 = add2(sum2[0], sum2[1]);
+        const float sum = ((sum4[0] + sum4[1]) + (sum4[2] + sum4[3])) + (s2.x + s2.y);
         l_run = (j == 0 ? 0.f : l_run * alpha) + sum;
         m_run = m_use;
         tmem_st_wait();
