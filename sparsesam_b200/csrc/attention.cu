@@ -51,7 +51,9 @@ constexpr int kAttnKW = 4;      // K loader warps (128 / kAttnKW key rows each)
 constexpr int kAttnVW = 2;      // V loader warps
 constexpr int kAttnLW = kAttnKW + kAttnVW + 1;  // loader warps 8 .. 8 + kAttnLW - 1 (last: Q rows)
 constexpr int kAttnMmaWarp = 8 + kAttnLW;
-constexpr int kAttnThreads = 32 * (kAttnMmaWarp + 1);
+constexpr int kAttnEpiWarp = kAttnMmaWarp + 1;  // windowed grids: epilogue warps 16 .. 19
+// threads per CTA: windowed grids add the four epilogue warps
+__host__ __device__ constexpr int attn_threads(bool small) { return 32 * (kAttnMmaWarp + 1 + (small ? 4 : 0)); }
 constexpr int kAttnTmemCols = 512;
 constexpr float kRescaleThreshold = 8.0f;  // log2 units
 
@@ -178,10 +180,11 @@ struct AttnCfg {
   static constexpr int kOHBytes = 2 * kAttnBN * kBW * 2;  // one-hot H | W regions per stage
   static constexpr int kABRow = 80;  // SMALL: a query's fp16 P row (64 B) + 16 B (conflict-free 16-byte stores)
   static constexpr int kOSplit = D == 80 ? 48 : D / 2;    // O columns of the first softmax half
-  // SMALL epilogue staging: per lane-quarter block, 32 rows of each half's bf16
-  // columns; row strides padded by 16 B so 16-byte stores of 8 lanes hit 32 banks
-  static constexpr int kOStride0 = 2 * kOSplit + 16;
-  static constexpr int kOStride1 = 2 * (D - kOSplit) + 16;
+  // SMALL epilogue staging: per lane-quarter block, 32 bf16 rows of D columns; the
+  // row stride padded by 16 B (an odd number of 16-byte units: 16-byte stores of
+  // 8 lanes hit 32 banks)
+  static constexpr int kOStride = 2 * D + 16;
+  static_assert(!SMALL || kO == 2, "the epilogue warps pair O buffer, l slot and tile parity");
   static_assert(kTmPH + kPHCols <= kAttnTmemCols, "TMEM plan exceeds 512 columns");
 };
 
@@ -201,15 +204,17 @@ struct AttnLayout {
   static constexpr int kStage = 2 * TG::bytes(kAttnBN) + C::kOHBytes;  // K | V | one-hot
   static constexpr int kTables = SMALL ? TG::bytes(2 * C::kNT) : 0;
   static constexpr int kABStage = SMALL ? kAttnBM * C::kABRow : kAttnBM * 256;  // band scratch / staged bias rows
-  int tab, q, kv, ab, ostage, xchg, bars, total;
+  int tab, q, kv, ab, ostage, xchg, lsum, tinfo, bars, total;
   __host__ __device__ AttnLayout() {
     tab = 0;
     q = align1k(tab + kTables);                   // [kQBuf] x bytes(128)
     kv = align1k(q + C::kQBuf * TG::bytes(kAttnBM));  // [stages] x kStage
     ab = align1k(kv + C::kStages * kStage);       // kABStage
-    ostage = ab + kABStage;                       // SMALL: epilogue staging, 128 rows x (kOStride0 + kOStride1)
-    xchg = ostage + (SMALL ? kAttnBM * (C::kOStride0 + C::kOStride1) : 0);  // float [2][2 halves][2 values][128]
-    bars = (xchg + 2 * 2 * 2 * kAttnBM * 4 + 7) & ~7;  // mbarriers
+    ostage = ab + kABStage;                       // SMALL: epilogue staging, 128 rows x kOStride
+    xchg = ostage + (SMALL ? kAttnBM * C::kOStride : 0);  // float [2][2 halves][2 values][128]
+    lsum = xchg + 2 * 2 * 2 * kAttnBM * 4;        // SMALL: float [2 slots][2 halves][128] row-sum shares
+    tinfo = lsum + (SMALL ? 2 * 2 * kAttnBM * 4 : 0);  // SMALL: int [2]: the next tile shares the K / V fill
+    bars = (tinfo + (SMALL ? 8 : 0) + 7) & ~7;    // mbarriers
     total = bars + 64 * 8 + 16 + 1024;            // mbarriers, TMEM address, abort flag + alignment slack
   }
 };
@@ -351,6 +356,13 @@ struct TileBlocks {
   __device__ int at(int i) const { return i < nkb ? i : qt; }
 };
 
+// Whether local tile lt + 1 reads local tile lt's K / V fill: lt is the first query
+// tile of a window-head with a second one (query compaction, one key block).
+template <bool SMALL, bool CP>
+__device__ __forceinline__ bool next_shares(int lt, const TileDesc& d, const TileBlocks& tb) {
+  return SMALL && CP && !(lt & 1) && d.qtile == 0 && d.n_real > kAttnBM && tb.n == 1;
+}
+
 // A persistent CTA's local tile lt covers global tile tile_of<GT>(lt): groups of
 // GT consecutive tiles, group index blockIdx.x + k gridDim.x. Windowed grids use
 // GT = 2: a window-head's two query tiles read the same key block, so the
@@ -368,8 +380,10 @@ struct BlockCursor {
   int tile, lt, j, g;
   bool done;
   TileBlocks tb;
+  // the block list depends on the query tile only with the diagonal (never with
+  // query compaction): the UMMA thread decodes no tile otherwise
   __device__ void set_blocks(const AttnParams& a) {
-    tb = TileBlocks(a, tile_desc<CP>(a, tile).qtile);
+    tb = TileBlocks(a, (!CP && a.with_diag) ? tile_desc<CP>(a, tile).qtile : 0);
   }
   __device__ void start(const AttnParams& a) {
     lt = 0;
@@ -401,9 +415,9 @@ enum {
   kBarQFull = 1,     // [kQBuf <= 3]  loader lanes (cp.async)
   kBarQEmpty = 4,    // [kQBuf <= 3]  UMMA commit after the tile's last QK^T
   kBarKFull = 7,     // [3]  K loader lanes (cp.async)
-  kBarKEmpty = 10,   // [3]  unused: S-full (QK^T done) frees the K stage
+  kBarKEmpty = 10,   // [3]  UMMA commit after each QK^T reading the stage
   kBarVFull = 13,    // [3]  V loader lanes (cp.async)
-  kBarVEmpty = 16,   // [3]  unused: O-done (P.V done) frees the V stage
+  kBarVEmpty = 16,   // [3]  UMMA commit after each P.V reading the stage
   kBarPHFull = 19,   //      UMMA commit (SMALL)
   kBarPHFree = 20,   //      K loaders (SMALL)
   kBarABFull = 21,   // [2]  A_bias of the tile is in TMEM (SMALL: K loaders; LARGE: softmax)
@@ -413,10 +427,12 @@ enum {
   kBarSFree = 27,    // [2]  unused: O-done frees the S block (P lives in its columns)
   kBarPFull = 29,    // [2]  softmax
   kBarODone = 31,    // [2]  UMMA commit after P.V of block g (index g & 1)
-  kBarOFree = 33,    // [2]  softmax epilogue
+  kBarOFree = 33,    // [2]  epilogue (LARGE: softmax warps; SMALL: epilogue warps)
   kBarXchg = 35,     // [2 rounds][4 lane quarters]  the two softmax warps of a quarter
   kBarDrain = 43,
-  kNumBars = 44
+  kBarOFull = 44,    // [2]  SMALL: UMMA commit after the tile's last P.V (index tile & 1)
+  kBarLFull = 46,    // [2]  SMALL: softmax row-sum shares of the tile (index tile & 1)
+  kNumBars = 48
 };
 static_assert(kNumBars * 8 + 8 <= 64 * 8, "mbarrier region of AttnLayout too small");
 
@@ -513,7 +529,7 @@ __device__ __forceinline__ void stage_out_rows(uint32_t tO, int nc16, uint8_t* s
 // 32-byte swizzle (one box lands as one TileGeom chunk region): a windowed tile's
 // consecutive Q rows.
 template <int D, bool SMALL, bool CP>
-__global__ void __launch_bounds__(kAttnThreads, 1)
+__global__ void __launch_bounds__(attn_threads(SMALL), 1)
     sparse_attn_kernel(const AttnParams a, const __grid_constant__ CUtensorMap tm_tile) {
   using TG = TileGeom<D>;
   using C = AttnCfg<D, SMALL>;
@@ -542,7 +558,9 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       mbar_init(&bars[kBarSFree + i], 1);
       mbar_init(&bars[kBarPFull + i], 256);
       mbar_init(&bars[kBarODone + i], 1);
-      mbar_init(&bars[kBarOFree + i], 256);
+      mbar_init(&bars[kBarOFree + i], SMALL ? 128 : 256);
+      mbar_init(&bars[kBarOFull + i], 1);
+      mbar_init(&bars[kBarLFull + i], 256);
       for (int w = 0; w < 4; ++w) mbar_init(&bars[kBarXchg + 4 * i + w], 64);
     }
     mbar_init(&bars[kBarPHFull], 1);
@@ -720,7 +738,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     // relX[j] = P_X[qc - j + win - 1] read as a reversed window, then the two
     // bands go to A_bias[lt_ & 1] in TMEM. The buffer's previous reader, QK^T of
     // tile lt_ - 2, completed before the [P_H | P_W] commit of tile lt_.
-    auto stage_bias_rows = [&](int lt_, const TileDesc& td) -> bool {
+    auto stage_bias_rows = [&](int lt_, const TileDesc& td, bool next_share) -> bool {
       if constexpr (!SMALL) {
         return true;
       } else {
@@ -748,12 +766,17 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       tmem_st_32x32b_x16(t_lane + C::kTmAB + (lt_ & 1) * C::kABCols, v);
       tmem_st_wait();
       tc_fence_before();
+      // the UMMA thread reads whether the next tile shares this one's K / V fill once
+      // A_bias is in (the slot's next write, for tile lt_ + 2, waits for [P_H | P_W]
+      // of that tile, which the UMMA thread issues after reading this one)
+      if (warp == 8 && lane == 0) reinterpret_cast<volatile int*>(smem + L.tinfo)[lt_ & 1] = next_share ? 1 : 0;
       mbar_arrive(&bars[kBarABFull + (lt_ & 1)]);
       return true;
       }
     };
 
-    int g = 0;
+    int g = 0;  // stage fills of this loader (stage g % kStages)
+    bool share = false;  // the tile reads the previous tile's fill
     bool ok = true;
     if (kv == 2) {  // Q warp: every tile as soon as its Q buffer is free
       for (int lt = 0; ok && tile_exists(lt) && !*abort_flag; ++lt) ok = load_q(lt);
@@ -769,23 +792,30 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       const __nv_bfloat16* base = a.qkv + static_cast<int64_t>(seq) * N * a.ld_qkv;
       const int xcol = (kv == 0 ? a.C : 2 * a.C) + head * D;
       const TileBlocks tb(a, qtile);
+      // With query compaction a window-head with more than 128 real tokens has two
+      // query tiles, global tiles 2m and 2m + 1 (a window's tiles start at an even
+      // index), hence local tiles lt and lt + 1 of one CTA: with one key block, the
+      // second reads the first one's K / V fill instead of gathering it again. Each
+      // fill gets one empty commit, after its last reader.
+      const bool next_share = next_shares<SMALL, CP>(lt, td, tb);
       int nt[4] = {-1, -1, -1, -1};  // tokens of keys row0 + lane + 32 i of the next block
       auto fetch = [&](int jb) {
         const int kp = tb.at(jb) * kAttnBN + row0 + lane;
 #pragma unroll
         for (int i = 0; i < kMaxKV; ++i) nt[i] = (32 * i < my_rows && kp + 32 * i < N) ? __ldg(perm + kp + 32 * i) : -1;
       };
-      if (tb.n > 0) fetch(0);
-      for (int j = 0; j < tb.n; ++j, ++g) {
+      if (tb.n > 0 && !share) fetch(0);
+      for (int j = 0; j < (share ? 0 : tb.n); ++j, ++g) {
         int t[4] = {-1, -1, -1, -1};
 #pragma unroll
         for (int i = 0; i < kMaxKV; ++i) t[i] = nt[i];
         if (j + 1 < tb.n) fetch(j + 1);  // the next block's tokens, one block ahead
         const int stage = g % C::kStages;
         const int full_bar = (kv == 0 ? kBarKFull : kBarVFull) + stage;
-        // K stage free once QK^T of block g - kStages completed (its S-full commit), V
-        // stage once P.V of that block did (its O-done commit)
-        if (!(ok = wait_or_abort((kv == 0 ? kBarSFull : kBarODone) + stage, ((g / C::kStages) & 1) ^ 1))) break;
+        // the stage is free once every QK^T (K) or P.V (V) that read its previous
+        // fill has completed: one empty commit each
+        const int empty_bar = (kv == 0 ? kBarKEmpty : kBarVEmpty) + stage;
+        if (!(ok = wait_or_abort(empty_bar, ((g / C::kStages) & 1) ^ 1))) break;
         const uint32_t sK = sb + L.kv + stage * LAY::kStage;
         if (kv == 0) {  // one-hot rows of this lane's two keys
           uint8_t* oh_h = smem + L.kv + stage * LAY::kStage + 2 * TG::bytes(kAttnBN);
@@ -821,8 +851,9 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       }
       // the tile's bias operand once its key rows are on their way
       if constexpr (SMALL) {
-        if (ok && kv == 0 && !(ok = stage_bias_rows(lt, td))) break;
+        if (ok && kv == 0 && !(ok = stage_bias_rows(lt, td, next_share))) break;
       }
+      share = next_share;
     }
     cp_async_wait_all();
     // No TMA copy of the Q warp may still be landing when the CTA exits: wait
@@ -841,6 +872,13 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       const uint32_t idesc_b = make_idesc_f16(kAttnBM, kAttnBN);
       const uint32_t idesc_o = make_idesc_bf16(kAttnBM, D, 0, 1);
       bool ok = !SMALL || wait_or_abort(kBarTab, 0);
+      // K / V fill read by the current QK^T (fq) and P.V (fp): a new fill per block,
+      // except a window-head's second tile, which shares its first tile's; bit
+      // lt & 3 of nexts = tile lt + 1 shares tile lt's fill (read with A_bias of
+      // tile lt; tile lt shares when bit (lt - 1) & 3 is set)
+      int fq = -1, fp = -1;
+      uint32_t nexts = 0;
+      const volatile int* tinfo = reinterpret_cast<const volatile int*>(smem + L.tinfo);
 
       auto issue_ph = [&](int lt_) -> bool {  // [P_H | P_W] of tile lt_ (SMALL)
         const int qb = lt_ % C::kQBuf;
@@ -865,8 +903,13 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
           }
           if (!wait_or_abort(kBarABFull + (c.lt & 1), (c.lt >> 1) & 1)) return false;
         }
-        const int st = c.g % C::kStages, sbuf = c.g % C::kS;
-        if (!wait_or_abort(kBarKFull + st, (c.g / C::kStages) & 1)) return false;
+        if (SMALL && CP && c.j == 0)
+          nexts = (nexts & ~(1u << (c.lt & 3))) | (static_cast<uint32_t>(tinfo[c.lt & 1] != 0) << (c.lt & 3));
+        const bool share = SMALL && CP && c.j == 0 && ((nexts >> ((c.lt - 1) & 3)) & 1u);
+        const bool shared_next = SMALL && CP && ((nexts >> (c.lt & 3)) & 1u);
+        if (!share) ++fq;
+        const int st = fq % C::kStages, sbuf = c.g % C::kS;
+        if (!wait_or_abort(kBarKFull + st, (fq / C::kStages) & 1)) return false;
         // S block free once P.V of block g - kS (which reads P from it) completed
         if (!wait_or_abort(kBarODone + sbuf, ((c.g / C::kS) & 1) ^ 1)) return false;
         tc_fence_after();
@@ -892,7 +935,8 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
               umma_f16_ts(tS, ab + ks * 8, make_smem_desc(oh + ks * 32, 16, 1024, kSw128), idesc_b, 1u);
           }
         }
-        umma_commit(&bars[kBarSFull + sbuf]);  // also frees K stage st (kS == kStages)
+        umma_commit(&bars[kBarSFull + sbuf]);
+        if (!shared_next) umma_commit(&bars[kBarKEmpty + st]);  // the fill's last QK^T
         if (c.j == c.tb.n - 1) umma_commit(&bars[kBarQEmpty + c.lt % C::kQBuf]);
         return true;
       };
@@ -900,8 +944,9 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         if (!wait_or_abort(kBarPFull + (c.g & 1), (c.g >> 1) & 1)) return false;
         const int ob = c.lt % C::kO;
         if (c.j == 0 && !wait_or_abort(kBarOFree + ob, ((c.lt / C::kO) & 1) ^ 1)) return false;
-        const int st = c.g % C::kStages, sbuf = c.g % C::kS;
-        if (!wait_or_abort(kBarVFull + st, (c.g / C::kStages) & 1)) return false;
+        if (!(SMALL && CP && c.j == 0 && ((nexts >> ((c.lt - 1) & 3)) & 1u))) ++fp;
+        const int st = fp % C::kStages, sbuf = c.g % C::kS;
+        if (!wait_or_abort(kBarVFull + st, (fp / C::kStages) & 1)) return false;
         tc_fence_after();
         fence_proxy_async_smem();
         const uint32_t tP = tmem + sbuf * kAttnBN;
@@ -914,7 +959,9 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         for (int ks = 0; ks < kAttnBN / 16; ++ks)
           umma_f16_ts(tO, tP + ks * 8 + (ks >= kAttnBN / 32 ? 32 : 0),
                       make_smem_desc(sV + ks * 512, kAttnBN * 32, 256, kSw32), idesc_o, (c.j > 0 || ks > 0) ? 1u : 0u);
-        umma_commit(&bars[kBarODone + (c.g & 1)]);  // also frees V stage st and S block sbuf
+        umma_commit(&bars[kBarODone + (c.g & 1)]);  // also frees S block sbuf
+        if (!(SMALL && CP && ((nexts >> (c.lt & 3)) & 1u))) umma_commit(&bars[kBarVEmpty + st]);  // last P.V
+        if (SMALL && c.j == c.tb.n - 1) umma_commit(&bars[kBarOFull + ob]);
         return true;
       };
 
@@ -936,10 +983,43 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       umma_commit(&bars[kBarDrain]);
       mbar_wait_slow(&bars[kBarDrain], 0);
     }
+  } else if (warp >= kAttnEpiWarp) {
+    if constexpr (SMALL) {
+      // ===================== epilogue warps (windowed grids) =====================
+      // Warp kAttnEpiWarp + q: query rows 32q .. 32q + 31 of every tile (TMEM lane
+      // quarter q), all D columns: O / l as bf16, stored at the raster token of
+      // the row (inverse permutation and head merge). The tile's O buffer and
+      // row-sum slot are tile & 1; both are released through O-free.
+      const int q4 = warp & 3;
+      const int r = q4 * 32 + lane;
+      const uint32_t t_lane = tmem + (static_cast<uint32_t>(q4 * 32) << 16);
+      uint8_t* stage = smem + L.ostage + q4 * 32 * C::kOStride;
+      const float* lsum = reinterpret_cast<const float*>(smem + L.lsum);
+      uint32_t ofull_par = 0;  // bit b: parity of the next O-full phase of buffer b
+      bool ok = true;
+      for (int lt = 0; ok && tile_exists(lt) && !*abort_flag; ++lt) {
+        const TileDesc td = tile_desc<CP>(a, tile_of<C::kTileGroup>(lt));
+        const int orow = query_out_row(a, td.seq, query_tok<CP>(a, td, td.qtile * kAttnBM + r));
+        const bool any = TileBlocks(a, td.qtile).n > 0;
+        const int ob = lt & 1;
+        if (any) {  // O-full commits only for tiles with key blocks
+          if (!(ok = wait_or_abort(kBarOFull + ob, (ofull_par >> ob) & 1))) break;
+          ofull_par ^= 1u << ob;
+        }
+        if (!(ok = wait_or_abort(kBarLFull + ob, (lt >> 1) & 1))) break;
+        tc_fence_after();
+        const float l = lsum[(2 * ob) * kAttnBM + r] + lsum[(2 * ob + 1) * kAttnBM + r];
+        stage_out_rows(t_lane + C::kTmO + ob * D, D / 16, stage, C::kOStride, orow, (any && l > 0.f) ? 1.f / l : 0.f,
+                       a.out + td.head * D, a.ld_out);
+        tc_fence_before();
+        mbar_arrive(&bars[kBarOFree + ob]);
+      }
+    }
   } else {
     // ========================= softmax warps =========================
     // Thread (row r, half h): query row r = tid % 128 of the tile, keys 64h..64h+63
-    // of every block, O columns [h ? kOSplit : 0, h ? D : kOSplit).
+    // of every block, O columns [h ? kOSplit : 0, h ? D : kOSplit) (their
+    // rescale; the epilogue of windowed grids runs on the epilogue warps).
     const int r = tid & (kAttnBM - 1);
     const int h = tid >> 7;
     const uint32_t t_lane = tmem + (static_cast<uint32_t>((warp & 3) * 32) << 16);
@@ -993,14 +1073,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       tc_fence_after();
       const float inv_l = l > 0.f ? 1.f / l : 0.f;
       const uint32_t tO = t_lane + C::kTmO + (lt_ % C::kO) * D;
-      if constexpr (SMALL) {
-        // The warp's 32 rows x this half's columns: TMEM -> bf16 in the warp's
-        // staging block -> whole row segments stored by consecutive lanes.
-        uint8_t* stage = smem + L.ostage + (warp & 3) * 32 * (C::kOStride0 + C::kOStride1) +
-                         (h ? 32 * C::kOStride0 : 0);
-        stage_out_rows(tO + oc0, (oc1 - oc0) / 16, stage, h ? C::kOStride1 : C::kOStride0, orow,
-                       g_last >= 0 ? inv_l : 0.f, a.out + head * D + oc0, a.ld_out);
-      } else {
+      {
         uint4* dst = orow >= 0 ? reinterpret_cast<uint4*>(a.out + static_cast<int64_t>(orow) * a.ld_out + head * D)
                                : nullptr;
 #pragma unroll
@@ -1033,11 +1106,18 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       return query_out_row(a, td.seq, query_tok<CP>(a, td, td.qtile * kAttnBM + r));
     };
 
+    // SMALL: this half's row-sum shares go to the epilogue warps; the query tile
+    // matters to the block list and the mask only with the diagonal
+    float* lsum = reinterpret_cast<float*>(smem + L.lsum);
     bool ok = true;
     int orow_cur = -1, orow_next = -1, qt_cur = 0, qt_next = 0, hd_cur = 0, hd_next = 0;
     if (tile_exists(0)) {
-      if constexpr (!SMALL) ok = stage_bias(0);
-      orow_cur = tile_info(0, qt_cur, hd_cur);
+      if constexpr (!SMALL) {
+        ok = stage_bias(0);
+        orow_cur = tile_info(0, qt_cur, hd_cur);
+      } else {
+        qt_cur = (CP || !a.with_diag) ? 0 : tile_desc<CP>(a, tile_of<C::kTileGroup>(0)).qtile;
+      }
     }
     int pend_lt = -1, pend_g = -1, pend_orow = -1, pend_head = 0;  // deferred epilogue
     float pend_l = 0.f;  // this half's share of the pending tile's row sum
@@ -1047,7 +1127,12 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       const TileBlocks tb(a, qtile);
       const int my_mb = 2 * qtile + (r >= 64 ? 1 : 0);
       const uint32_t tO = t_lane + C::kTmO + (lt % C::kO) * D;
-      if (tile_exists(lt + 1)) orow_next = tile_info(lt + 1, qt_next, hd_next);
+      if (tile_exists(lt + 1)) {
+        if constexpr (SMALL)
+          qt_next = (CP || !a.with_diag) ? 0 : tile_desc<CP>(a, tile_of<C::kTileGroup>(lt + 1)).qtile;
+        else
+          orow_next = tile_info(lt + 1, qt_next, hd_next);
+      }
       float m_run = -INFINITY, l_run = 0.f;  // l_run: this half's share of the row sum
       for (int j = 0; j < tb.n; ++j, ++g) {
         const int sbuf = g % C::kS;
@@ -1084,8 +1169,8 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         float mx = fmaxf(fmaxf(mx4[0], mx4[1]), fmaxf(mx4[2], mx4[3]));
         float mx_other, l_other;
         // block 0's exchange also hands over the pending tile's row-sum shares
-        if (!(ok = exchange(mx, j == 0 ? pend_l : 0.f, mx_other, l_other))) break;
-        if (j == 0) pend_l += l_other;
+        if (!(ok = exchange(mx, (!SMALL && j == 0) ? pend_l : 0.f, mx_other, l_other))) break;
+        if (!SMALL && j == 0) pend_l += l_other;
         mx = fmaxf(mx, mx_other);
         mx = mx == -INFINITY ? -INFINITY : mx * a.scale_log2;
         const float m_new = fmaxf(m_run, mx);
@@ -1157,14 +1242,23 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         tc_fence_before();
         mbar_arrive(&bars[kBarPFull + (g & 1)]);
 
-        if (j == 0) {
+        if (!SMALL && j == 0) {
           // next tile's bias operand and the previous tile's epilogue, off the critical path
-          if (!SMALL && tile_exists(lt + 1) && !(ok = stage_bias(lt + 1))) break;
+          if (tile_exists(lt + 1) && !(ok = stage_bias(lt + 1))) break;
           if (pend_lt >= 0 && !(ok = epilogue(pend_lt, pend_g, pend_orow, pend_head, pend_l))) break;
           pend_lt = -1;
         }
       }
       if (!ok) break;
+      if constexpr (SMALL) {
+        // this half's row-sum share of tile lt for the epilogue warps; the slot's
+        // previous tile (lt - 2) was read before its O buffer was released
+        if (!(ok = wait_or_abort(kBarOFree + (lt & 1), ((lt >> 1) & 1) ^ 1))) break;
+        lsum[(2 * (lt & 1) + h) * kAttnBM + r] = l_run;
+        mbar_arrive(&bars[kBarLFull + (lt & 1)]);
+        qt_cur = qt_next;
+        continue;
+      }
       pend_lt = lt;
       pend_g = tb.n > 0 ? g - 1 : -1;
       pend_orow = orow_cur;
@@ -1389,7 +1483,7 @@ static int launch_attn(const AttnParams& p, const CUtensorMap& tm_tile, cudaStre
   // so its 512 TMEM columns are always available.
   const int smem = L.total > 116 * 1024 ? L.total : 116 * 1024;
   const int grid = p.total_tiles < sms ? p.total_tiles : sms;
-  sparse_attn_kernel<D, SMALL, CP><<<grid, kAttnThreads, smem, stream>>>(p, tm_tile);
+  sparse_attn_kernel<D, SMALL, CP><<<grid, attn_threads(SMALL), smem, stream>>>(p, tm_tile);
   return status_from_cuda(cudaGetLastError());
 }
 

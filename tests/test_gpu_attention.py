@@ -211,3 +211,39 @@ def test_query_compaction_matches_every_token(cuda_device, d, B, H, W, ws):
     got[real] = out_cmp.float().cpu()[rows.cpu()[real].long()]
     err = (got[real] - ref[real]).abs()
     assert err.max().item() < 3e-2 and err.mean().item() < 3e-3
+
+
+def test_query_compaction_many_tiles_per_cta(cuda_device):
+    """ViT-H's windowed shape (16 heads, d = 80, 64 x 64 grid, 3 images): 1,968 query
+    tiles, about 13 per persistent CTA, so a CTA runs many window-heads whose two
+    query tiles read one K / V fill, next to window-heads with a single tile. Every
+    stored row equals the run without compaction bit for bit, and sampled windows
+    match the fp32 oracle."""
+    B, H, W, ws, heads, d = 3, 64, 64, 14, 16, 80
+    g = torch.Generator().manual_seed(5)
+    rows = ops.window_rows(B, H, W, ws, cuda_device)
+    n_win, N, C = rows.numel() // (ws * ws), ws * ws, heads * d
+    qkv = torch.randn(n_win * N, 3 * C, generator=g).to(torch.bfloat16).to(cuda_device)
+    th = (torch.randn(2 * ws - 1, d, generator=g) * 0.3).to(torch.bfloat16).to(cuda_device)
+    tw = (torch.randn(2 * ws - 1, d, generator=g) * 0.3).to(torch.bfloat16).to(cuda_device)
+    perm = torch.stack([torch.randperm(N, generator=g) for _ in range(n_win * heads)]).to(torch.int32)
+    n_init = order.a_shape_n_init(N, 64, 0.3, False)
+    out_all = torch.full((B * H * W, C), 3.0, device=cuda_device, dtype=torch.bfloat16)
+    out_cmp = out_all.clone()
+    ops.sparse_attn(qkv, n_win, heads, ws, d, th, tw, perm.to(cuda_device), n_init, False, d ** -0.5,
+                    out=out_all, out_rows=rows)
+    ops.sparse_attn(qkv, n_win, heads, ws, d, th, tw, perm.to(cuda_device), n_init, False, d ** -0.5,
+                    out=out_cmp, out_rows=rows, grid=(H, W))
+    assert ops.device_error() == 0
+    assert torch.equal(out_all, out_cmp)
+    sample = [0, 4, 20, 24, 37, 74]   # inner, last-column, last-row and corner windows of images 0-2
+    q, k, v = qkv.float().cpu().view(n_win, N, 3, heads, d)[sample].permute(2, 0, 3, 1, 4).reshape(3, -1, N, d)
+    ps = perm.view(n_win, heads, N)[sample].reshape(-1, N)
+    ref = sparse_attention(q, k, v, th.float().cpu(), tw.float().cpu(), ps, ws, n_init, False, d ** -0.5,
+                           round_tables_fp16=False)
+    ref = ref.view(len(sample), heads, N, d).permute(0, 2, 1, 3).reshape(len(sample) * N, C)
+    r = rows.view(n_win, N)[sample].reshape(-1).cpu()
+    real = r >= 0
+    got = out_cmp.float().cpu()[r[real].long()]
+    err = (got - ref[real]).abs()
+    assert err.max().item() < 3e-2 and err.mean().item() < 3e-3
