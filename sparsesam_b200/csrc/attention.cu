@@ -886,11 +886,11 @@ __global__ void __launch_bounds__(attn_threads(SMALL), 1)
         if (!wait_or_abort(kBarPHFree, (lt_ & 1) ^ 1)) return false;
         tc_fence_after();
         fence_proxy_async_smem();
-        const uint32_t sQ = sb + L.q + qb * TG::bytes(kAttnBM);
-#pragma unroll
+        const uint64_t dq = kmajor_desc<D>(sb + L.q + qb * TG::bytes(kAttnBM), kAttnBM, 0);
+        const uint64_t dt = kmajor_desc<D>(sb + L.tab, 2 * C::kNT, 0);
+#pragma unroll 1
         for (int ks = 0; ks < D / 16; ++ks)
-          umma_f16_ss(tmem + C::kTmPH, kmajor_desc<D>(sQ, kAttnBM, ks), kmajor_desc<D>(sb + L.tab, 2 * C::kNT, ks),
-                      idesc_t, ks > 0);
+          umma_f16_ss(tmem + C::kTmPH, dq + ks * (kAttnBM * 2), dt + ks * (2 * C::kNT * 2), idesc_t, ks > 0);
         umma_commit(&bars[kBarPHFull]);
         return true;
       };
@@ -919,11 +919,15 @@ __global__ void __launch_bounds__(attn_threads(SMALL), 1)
         const uint32_t sOH = sK + 2 * TG::bytes(kAttnBN);
         const uint32_t tAB = tmem + C::kTmAB + (c.lt & 1) * C::kABCols;
         const uint32_t tS = tmem + sbuf * kAttnBN;
-#pragma unroll
+        // (windowed grids issue each MMA once per tile: rolled loops keep the UMMA
+        // thread's code, fetched anew every tile, short; descriptors step by the
+        // 16-byte-unit offset of a 16-channel chunk)
+        const uint64_t dq = kmajor_desc<D>(sQ, kAttnBM, 0), dk = kmajor_desc<D>(sK, kAttnBN, 0);
+#pragma unroll(SMALL ? 1 : D / 16)
         for (int ks = 0; ks < D / 16; ++ks)
-          umma_f16_ss(tS, kmajor_desc<D>(sQ, kAttnBM, ks), kmajor_desc<D>(sK, kAttnBN, ks), idesc_s, ks > 0);
+          umma_f16_ss(tS, dq + ks * (kAttnBM * 2), dk + ks * (kAttnBN * 2), idesc_s, ks > 0);
         // + A_bias . onehot^T  (relH / scale at kh, relW / scale at kw); A_bias from TMEM
-#pragma unroll
+#pragma unroll(SMALL ? 1 : 2)
         for (int part = 0; part < 2; ++part) {
           const uint32_t ab = tAB + part * (C::kBW / 2);
           const uint32_t oh = sOH + part * kAttnBN * C::kBW * 2;
@@ -953,12 +957,13 @@ __global__ void __launch_bounds__(attn_threads(SMALL), 1)
         const uint32_t sV = sb + L.kv + st * LAY::kStage + TG::bytes(kAttnBN);
         const uint32_t tO = tmem + C::kTmO + ob * D;
         // V as an MN-major operand with N = D: 32B-swizzled atoms of 8 keys x 16
-        // channels, the D/16 channel regions LBO = 128 * 32 bytes apart.
-#pragma unroll
+        // channels, the D/16 channel regions LBO = 128 * 32 bytes apart; 16 keys = 512 B.
         // P of keys 0..63 sits in columns 0..31 of the S block, keys 64..127 in 64..95
+        const uint64_t dv = make_smem_desc(sV, kAttnBN * 32, 256, kSw32);
+#pragma unroll(SMALL ? 1 : kAttnBN / 16)
         for (int ks = 0; ks < kAttnBN / 16; ++ks)
-          umma_f16_ts(tO, tP + ks * 8 + (ks >= kAttnBN / 32 ? 32 : 0),
-                      make_smem_desc(sV + ks * 512, kAttnBN * 32, 256, kSw32), idesc_o, (c.j > 0 || ks > 0) ? 1u : 0u);
+          umma_f16_ts(tO, tP + ks * 8 + (ks >= kAttnBN / 32 ? 32 : 0), dv + ks * 32, idesc_o,
+                      (c.j > 0 || ks > 0) ? 1u : 0u);
         umma_commit(&bars[kBarODone + (c.g & 1)]);  // also frees S block sbuf
         if (!(SMALL && CP && ((nexts >> (c.lt & 3)) & 1u))) umma_commit(&bars[kBarVEmpty + st]);  // last P.V
         if (SMALL && c.j == c.tb.n - 1) umma_commit(&bars[kBarOFull + ob]);
