@@ -12,12 +12,14 @@
 // and the result of permuted row p is written to raster token perm[p]
 // (the inverse permutation and the head merge are fused into the store).
 //
-// Persistent, warp-specialised CTA (one per SM), 512 threads (16 warps):
+// Persistent, warp-specialised CTA (one per SM), 512 threads (16 warps; 640 in
+// 20 warps for windowed grids):
 //   warps 0-7   softmax: warps w and w+4 share TMEM lane quarter w % 4 (query
 //               rows 32(w%4)..+31 of the tile) and split each 128-key block
 //               into two 64-key halves; the row maxima are exchanged through
-//               shared memory. They also place the next tile's rel-pos bias
-//               operand in TMEM and run the deferred epilogue, split the same way;
+//               shared memory. For the global grid they also place the next
+//               tile's rel-pos bias operand in TMEM and run the deferred
+//               epilogue, split the same way;
 //   warps 8-14  loaders: coalesced cp.async gathers (eight lanes per 128-byte row
 //               segment) of the permuted K rows with the one-hot key-position
 //               operand (warps 8-11, 32 rows each), the V rows (warps 12-13,
@@ -25,7 +27,12 @@
 //               rows (warp 14);
 //   warp 15     UMMA issuer: S = Q K^T + A_bias onehot^T (A_bias from TMEM),
 //               O += P V (P from TMEM, V as one N = D operand); for windowed
-//               grids also [P_H | P_W] = Q [Th ; Tw]^T of the next tile.
+//               grids also [P_H | P_W] = Q [Th ; Tw]^T of the next tile;
+//   warps 16-19 (windowed grids) epilogue: O / l of lane quarter w % 4, all D
+//               columns, stored at the raster rows.
+// Windowed grids run each role's per-tile code once per tile, so it is fetched
+// anew every tile: loops that run once per tile stay rolled and each role keeps
+// one copy of its code (instruction fetch, not FLOPs or bandwidth, bounds them).
 // Blocks are 128 keys wide (one N = 128 MMA per 16 channels of QK^T) and P.V
 // is one MMA per 16 keys. The loaders are latency-bound gathers, so the key rows
 // are spread over four warps, and the copy loop is kept rolled (one body shared
