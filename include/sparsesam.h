@@ -137,6 +137,11 @@ int ssam_a_shape_mask(int N, int m_block, int n_block, int n_init, int with_diag
  *               results of the real tokens are unchanged. Padding tokens remain
  *               keys. 0 / 0: every token is a query. n_seq must then be a
  *               multiple of the windows per image.
+ *   pad_row   : optional bf16 [3*heads*d], with grid_h / grid_w given: the qkv
+ *               projection of SAM's zero padding (the qkv bias in bf16). The
+ *               kernel then reads it for the padding tokens' K and V and never
+ *               reads their qkv rows (which need not be written). NULL: the
+ *               padding rows of qkv hold those values (ssam_fill_pad_rows).
  *   workspace : ssam_sparse_attn_workspace_size() bytes (0 for windowed grids,
  *               win <= 16; global grids keep the per-query bias there).
  * d must be 64 or 80; n_block other than 64 / 128 returns SSAM_ERR_UNSUPPORTED.
@@ -145,7 +150,7 @@ size_t ssam_sparse_attn_workspace_size(int n_seq, int heads, int win, int d);
 int ssam_sparse_attn_fwd(const void* qkv, int64_t ld_qkv, int n_seq, int heads, int win, int d,
                          const void* rel_pos_h, const void* rel_pos_w, const int32_t* perm,
                          int n_init_blocks, int n_block, int with_diag, float scale, void* out, int64_t ld_out,
-                         const int32_t* out_rows, int grid_h, int grid_w, void* workspace,
+                         const int32_t* out_rows, int grid_h, int grid_w, const void* pad_row, void* workspace,
                          size_t workspace_bytes, void* stream);
 
 /* ---------------------------------------------------------------------------

@@ -32,8 +32,8 @@ SIGNATURES: dict[str, tuple] = {
     "ssam_hilbert_order": (c_int, [c_int, c_int, c_ptr, c_ptr, c_ptr]),
     "ssam_sparse_attn_workspace_size": (c_size, [c_int, c_int, c_int, c_int]),
     "ssam_sparse_attn_fwd": (c_int, [c_ptr, c_i64, c_int, c_int, c_int, c_int, c_ptr, c_ptr, c_ptr,
-                                     c_int, c_int, c_int, c_f32, c_ptr, c_i64, c_ptr, c_int, c_int, c_ptr, c_size,
-                                     c_ptr]),
+                                     c_int, c_int, c_int, c_f32, c_ptr, c_i64, c_ptr, c_int, c_int, c_ptr, c_ptr,
+                                     c_size, c_ptr]),
     "ssam_keep_select": (c_int, [c_ptr, c_int, c_int, c_int, c_int, c_ptr, c_ptr, c_ptr]),
     "ssam_zstride_keep_n": (c_int, [c_int, c_f64]),
     "ssam_zstride_keep": (c_int, [c_int, c_int, c_int, c_int, c_ptr, c_ptr, c_ptr]),

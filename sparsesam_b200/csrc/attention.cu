@@ -255,6 +255,9 @@ struct AttnParams {
   // fp32 reciprocals of the compaction divisors (fast_div)
   float r_img_tiles, r_row_tiles, r_span_in, r_span_row, r_win, r_wlast;
   int w_last;     // real width of the last window column
+  // with compaction: bf16 qkv row of SAM's zero padding, read for padding keys (null:
+  // the padding rows of qkv hold it)
+  const __nv_bfloat16* pad_row;
   __half* bias_ws;  // LARGE: [rows][n_tiles*128][128] fp16 = relH/scale | relW/scale
 };
 
@@ -280,7 +283,7 @@ __device__ __forceinline__ int fast_div(int x, int d, float r) {
 // of the row's window (n_real of them, w_real per window row; all N tokens and
 // w_real = win without compaction).
 struct TileDesc {
-  int row, seq, head, qtile, n_real, w_real;
+  int row, seq, head, qtile, n_real, w_real, h_real;
 };
 
 // Token of query position p (= qtile * 128 + tile row) of a tile, or -1.
@@ -311,6 +314,7 @@ __device__ __forceinline__ TileDesc tile_desc(const AttnParams& a, int tile) {
     d.head = d.row - d.seq * a.heads;
     d.n_real = a.N;
     d.w_real = a.win;
+    d.h_real = a.win;
     return d;
   }
   const int img = fast_div(tile, a.img_tiles, a.r_img_tiles);
@@ -334,7 +338,8 @@ __device__ __forceinline__ TileDesc tile_desc(const AttnParams& a, int tile) {
   d.seq = img * a.wpi + wy * a.nww + wx;
   d.row = d.seq * a.heads + d.head;
   d.w_real = last_col ? a.w_last : a.win;
-  d.n_real = (last_row ? a.grid_h - (a.nwh - 1) * a.win : a.win) * d.w_real;
+  d.h_real = last_row ? a.grid_h - (a.nwh - 1) * a.win : a.win;
+  d.n_real = d.h_real * d.w_real;
   return d;
 }
 
@@ -629,7 +634,8 @@ __global__ void __launch_bounds__(attn_threads(SMALL), 1)
     const int row0 = part * my_rows;   // this warp's first key row of a block
     const bool q_warp = kv == 2;       // all Q rows of each tile
     // nrows (a multiple of 32, at most 128) rows starting at tile row r0, channel
-    // offset xcol of each token row; tok[s] holds the token of row r0 + 32 s + lane.
+    // offset xcol of each token row; tok[s] holds the token of row r0 + 32 s + lane
+    // (-1: zero-filled, -2 - t: padding key t, read from pad_row).
     // One 32-row group per iteration (kept rolled: the loop body is shared by all
     // loader roles, which keeps the kernel's hot code small).
     auto copy_rows = [&](uint32_t region, int R, int r0, int nrows, const int (&tok)[4], const __nv_bfloat16* base,
@@ -644,16 +650,18 @@ __global__ void __launch_bounds__(attn_threads(SMALL), 1)
         for (int i = 0; i < 8; ++i) {  // 4 rows per instruction
           const int rr = 4 * i + (lane >> 3);
           const int t = __shfl_sync(0xffffffffu, tk, rr);
-          const __nv_bfloat16* src = t >= 0 ? base + static_cast<int64_t>(t) * a.ld_qkv + xcol + c * 8 : a.qkv;
-          cp_async16(tile_chunk_addr<D>(region, R, rb + rr, c), src, t >= 0 ? 16u : 0u);
+          const __nv_bfloat16* src = t >= 0 ? base + static_cast<int64_t>(t) * a.ld_qkv + xcol + c * 8
+                                            : (t < -1 ? a.pad_row + xcol + c * 8 : a.qkv);
+          cp_async16(tile_chunk_addr<D>(region, R, rb + rr, c), src, t != -1 ? 16u : 0u);
         }
         if constexpr (D > 64) {
 #pragma unroll
           for (int i = 0; i < 2; ++i) {  // 16 rows per instruction
             const int rr = 16 * i + (lane >> 1);
             const int t = __shfl_sync(0xffffffffu, tk, rr);
-            const __nv_bfloat16* src = t >= 0 ? base + static_cast<int64_t>(t) * a.ld_qkv + xcol + ct * 8 : a.qkv;
-            cp_async16(tile_chunk_addr<D>(region, R, rb + rr, ct), src, t >= 0 ? 16u : 0u);
+            const __nv_bfloat16* src = t >= 0 ? base + static_cast<int64_t>(t) * a.ld_qkv + xcol + ct * 8
+                                              : (t < -1 ? a.pad_row + xcol + ct * 8 : a.qkv);
+            cp_async16(tile_chunk_addr<D>(region, R, rb + rr, ct), src, t != -1 ? 16u : 0u);
           }
         }
       }
@@ -806,10 +814,20 @@ __global__ void __launch_bounds__(attn_threads(SMALL), 1)
       // fill gets one empty commit, after its last reader.
       const bool next_share = next_shares<SMALL, CP>(lt, td, tb);
       int nt[4] = {-1, -1, -1, -1};  // tokens of keys row0 + lane + 32 i of the next block
+      // keys of the window's padding (outside its h_real x w_real top-left block)
+      // are read from pad_row when given
+      const bool sub_pad = CP && a.pad_row != nullptr && td.n_real < N;
       auto fetch = [&](int jb) {
         const int kp = tb.at(jb) * kAttnBN + row0 + lane;
 #pragma unroll
-        for (int i = 0; i < kMaxKV; ++i) nt[i] = (32 * i < my_rows && kp + 32 * i < N) ? __ldg(perm + kp + 32 * i) : -1;
+        for (int i = 0; i < kMaxKV; ++i) {
+          int t = (32 * i < my_rows && kp + 32 * i < N) ? __ldg(perm + kp + 32 * i) : -1;
+          if (sub_pad && t >= 0) {
+            const int ty = fast_div(t, win, a.r_win);
+            if (ty >= td.h_real || t - ty * win >= td.w_real) t = -2 - t;
+          }
+          nt[i] = t;
+        }
       };
       if (tb.n > 0 && !share) fetch(0);
       for (int j = 0; j < (share ? 0 : tb.n); ++j, ++g) {
@@ -819,9 +837,11 @@ __global__ void __launch_bounds__(attn_threads(SMALL), 1)
         if (j + 1 < tb.n) fetch(j + 1);  // the next block's tokens, one block ahead
         const int stage = g % C::kStages;
         const int full_bar = (kv == 0 ? kBarKFull : kBarVFull) + stage;
-        // the stage is free once every QK^T (K) or P.V (V) that read its previous
-        // fill has completed: one empty commit each
-        const int empty_bar = (kv == 0 ? kBarKEmpty : kBarVEmpty) + stage;
+        // the stage is free once the QK^T (K) or P.V (V) that read its previous
+        // fill last has completed: its K- / V-empty commit where fills can be
+        // shared, else the S-full / O-done commit of that block (one fill per block)
+        const int empty_bar = (SMALL && CP) ? (kv == 0 ? kBarKEmpty : kBarVEmpty) + stage
+                                            : (kv == 0 ? kBarSFull : kBarODone) + stage;
         if (!(ok = wait_or_abort(empty_bar, ((g / C::kStages) & 1) ^ 1))) break;
         const uint32_t sK = sb + L.kv + stage * LAY::kStage;
         if (kv == 0) {  // one-hot rows of this lane's two keys
@@ -834,9 +854,10 @@ __global__ void __launch_bounds__(attn_threads(SMALL), 1)
             for (int i = 0; i < kKRows / 32; ++i) {
               const int r = row0 + lane + 32 * i;
               int info = -1;
-              if (t[i] >= 0) {
-                const int kh = t[i] / win;
-                info = kh | ((t[i] - kh * win) << 16);
+              const int tk = t[i] >= 0 ? t[i] : (t[i] < -1 ? -2 - t[i] : -1);  // padding keys keep their place
+              if (tk >= 0) {
+                const int kh = tk / win;
+                info = kh | ((tk - kh * win) << 16);
               }
               const int old = oh_prev[s2][i];
               if (old >= 0) {  // clear the previous one-hot entries of this row
@@ -947,7 +968,7 @@ __global__ void __launch_bounds__(attn_threads(SMALL), 1)
           }
         }
         umma_commit(&bars[kBarSFull + sbuf]);
-        if (!shared_next) umma_commit(&bars[kBarKEmpty + st]);  // the fill's last QK^T
+        if (SMALL && CP && !shared_next) umma_commit(&bars[kBarKEmpty + st]);  // the fill's last QK^T
         if (c.j == c.tb.n - 1) umma_commit(&bars[kBarQEmpty + c.lt % C::kQBuf]);
         return true;
       };
@@ -972,7 +993,7 @@ __global__ void __launch_bounds__(attn_threads(SMALL), 1)
           umma_f16_ts(tO, tP + ks * 8 + (ks >= kAttnBN / 32 ? 32 : 0), dv + ks * 32, idesc_o,
                       (c.j > 0 || ks > 0) ? 1u : 0u);
         umma_commit(&bars[kBarODone + (c.g & 1)]);  // also frees S block sbuf
-        if (!(SMALL && CP && ((nexts >> (c.lt & 3)) & 1u))) umma_commit(&bars[kBarVEmpty + st]);  // last P.V
+        if (SMALL && CP && !((nexts >> (c.lt & 3)) & 1u)) umma_commit(&bars[kBarVEmpty + st]);  // last P.V
         if (SMALL && c.j == c.tb.n - 1) umma_commit(&bars[kBarOFull + ob]);
         return true;
       };
@@ -1502,7 +1523,7 @@ static int launch_attn(const AttnParams& p, const CUtensorMap& tm_tile, cudaStre
 int sparse_attn_fwd(const void* qkv, int64_t ld_qkv, int n_seq, int heads, int win, int d, const void* rel_pos_h,
                     const void* rel_pos_w, const int32_t* perm, int n_init_blocks, int n_block, int with_diag,
                     float scale, void* out, int64_t ld_out, const int32_t* out_rows, int grid_h, int grid_w,
-                    void* workspace, size_t workspace_bytes, cudaStream_t stream) {
+                    const void* pad_row, void* workspace, size_t workspace_bytes, cudaStream_t stream) {
   if (qkv == nullptr || rel_pos_h == nullptr || rel_pos_w == nullptr || perm == nullptr || out == nullptr)
     return SSAM_ERR_INVALID;
   if (n_seq <= 0 || heads <= 0 || win <= 0 || n_init_blocks < 0) return SSAM_ERR_INVALID;
@@ -1534,6 +1555,8 @@ int sparse_attn_fwd(const void* qkv, int64_t ld_qkv, int n_seq, int heads, int w
   p.out = static_cast<__nv_bfloat16*>(out);
   p.ld_out = ld_out;
   p.out_rows = out_rows;
+  p.pad_row = static_cast<const __nv_bfloat16*>(pad_row);
+  if (pad_row != nullptr && !aligned16(pad_row)) return SSAM_ERR_ALIGN;
   p.inv_scale = 1.0f / scale;
   p.n_tiles = (p.N + kAttnBM - 1) / kAttnBM;
   const bool small = win <= 16;

@@ -97,10 +97,10 @@ size_t ssam_sparse_attn_workspace_size(int n_seq, int heads, int win, int d) {
 int ssam_sparse_attn_fwd(const void* qkv, int64_t ld_qkv, int n_seq, int heads, int win, int d, const void* rel_pos_h,
                          const void* rel_pos_w, const int32_t* perm, int n_init_blocks, int n_block, int with_diag,
                          float scale, void* out, int64_t ld_out, const int32_t* out_rows, int grid_h, int grid_w,
-                         void* workspace, size_t workspace_bytes, void* stream) {
+                         const void* pad_row, void* workspace, size_t workspace_bytes, void* stream) {
   return ssam::sparse_attn_fwd(qkv, ld_qkv, n_seq, heads, win, d, rel_pos_h, rel_pos_w, perm, n_init_blocks, n_block,
-                               with_diag, scale, out, ld_out, out_rows, grid_h, grid_w, workspace, workspace_bytes,
-                               static_cast<cudaStream_t>(stream));
+                               with_diag, scale, out, ld_out, out_rows, grid_h, grid_w, pad_row, workspace,
+                               workspace_bytes, static_cast<cudaStream_t>(stream));
 }
 
 int ssam_keep_select(const int32_t* inv_perm_group, int B, int heads, int N, int keep_n, int32_t* idx, int32_t* rows,

@@ -72,8 +72,8 @@ int a_shape_mask(int N, int m_block, int n_block, int n_init, int with_diag, uin
 size_t sparse_attn_workspace_size(int n_seq, int heads, int win);
 int sparse_attn_fwd(const void* qkv, int64_t ld_qkv, int n_seq, int heads, int win, int d, const void* rel_pos_h,
                     const void* rel_pos_w, const int32_t* perm, int n_init_blocks, int n_block, int with_diag, float scale,
-                    void* out, int64_t ld_out, const int32_t* out_rows, int grid_h, int grid_w, void* workspace,
-                    size_t workspace_bytes, cudaStream_t stream);
+                    void* out, int64_t ld_out, const int32_t* out_rows, int grid_h, int grid_w, const void* pad_row,
+                    void* workspace, size_t workspace_bytes, cudaStream_t stream);
 int layernorm_gather(const float* x, int64_t ldx, const int32_t* src_rows, int n_rows, int C, const float* w,
                      const float* b, float eps, void* out, int64_t ld_out, cudaStream_t stream);
 int hilbert_order(int H, int W, int32_t* perm, int32_t* inv_perm, cudaStream_t stream);

@@ -222,13 +222,19 @@ def zstride_keep(H: int, W: int, ratio: float, B: int, device):
 def sparse_attn(qkv: torch.Tensor, n_seq: int, heads: int, win: int, d: int, rel_pos_h: torch.Tensor,
                 rel_pos_w: torch.Tensor, perm: torch.Tensor, n_init_blocks: int, with_diag: bool, scale: float,
                 out: torch.Tensor | None = None, out_rows: torch.Tensor | None = None,
-                n_block: int = 64, grid: tuple[int, int] | None = None) -> torch.Tensor:
+                n_block: int = 64, grid: tuple[int, int] | None = None,
+                pad_row: torch.Tensor | None = None) -> torch.Tensor:
     """Block-sparse attention of every (sequence, head) row; output in raster order (n_seq*N, heads*d),
     or, with `out_rows` (int32 [n_seq*N], -1 skips), (sequence, token) written to row out_rows[s*N + t].
     The A-shape mask is defined on n_block-token blocks (64 or 128). `grid` = (H, W): the
     sequences are the window_partition windows of H x W token grids, and only their real
-    tokens are computed as queries (windowed grids without the diagonal)."""
-    _check_cuda(qkv, rel_pos_h, rel_pos_w, perm, out, out_rows)
+    tokens are computed as queries (windowed grids without the diagonal). `pad_row` (bf16
+    [3*heads*d], with `grid`): the qkv row of the windows' zero padding, read for padding keys
+    instead of their qkv rows."""
+    _check_cuda(qkv, rel_pos_h, rel_pos_w, perm, out, out_rows, pad_row)
+    if pad_row is not None and (grid is None or pad_row.dtype != torch.bfloat16 or not pad_row.is_contiguous()
+                                or pad_row.numel() != 3 * heads * d):
+        raise ValueError("pad_row: contiguous bf16 [3*heads*d], with `grid`")
     if qkv.dtype != torch.bfloat16 or rel_pos_h.dtype != torch.bfloat16 or rel_pos_w.dtype != torch.bfloat16:
         raise TypeError("qkv and rel-pos tables must be bf16")
     if perm.dtype != torch.int32 or not perm.is_contiguous():
@@ -250,8 +256,8 @@ def sparse_attn(qkv: torch.Tensor, n_seq: int, heads: int, win: int, d: int, rel
     t0 = KernelTimer.begin()
     _lib.call("ssam_sparse_attn_fwd", qkv.data_ptr(), ld, n_seq, heads, win, d, rel_pos_h.data_ptr(),
               rel_pos_w.data_ptr(), perm.data_ptr(), n_init_blocks, n_block, 1 if with_diag else 0, float(scale),
-              out.data_ptr(), ld_out, _ptr(out_rows), grid[0] if grid else 0, grid[1] if grid else 0, _ptr(ws),
-              ws_bytes, _stream(qkv), launches=2 if ws_bytes else 1)
+              out.data_ptr(), ld_out, _ptr(out_rows), grid[0] if grid else 0, grid[1] if grid else 0, _ptr(pad_row),
+              _ptr(ws), ws_bytes, _stream(qkv), launches=2 if ws_bytes else 1)
     KernelTimer.end(t0, "attention_global" if ws_bytes else "attention_window",
                     attention_flops(n_seq * heads, N, d, n_init_blocks, with_diag, n_block))
     return out

@@ -79,6 +79,7 @@ class _AttnWeights:
     proj_b: torch.Tensor
     rel_h: torch.Tensor
     rel_w: torch.Tensor
+    pad_row: torch.Tensor   # bf16 qkv bias: the qkv row of SAM's zero window padding
 
 
 @dataclass
@@ -110,8 +111,9 @@ def _attn_weights(attn) -> _AttnWeights:
         C = attn.qkv.weight.shape[1]
         if not attn.use_rel_pos:
             raise NotImplementedError("the SparseSAM B200 attention needs SAM's decomposed rel-pos tables")
-        w = _AttnWeights(_bf16(attn.qkv.weight), _f32(attn.qkv.bias, 3 * C, dev), _bf16(attn.proj.weight),
-                         _f32(attn.proj.bias, C, dev), _bf16(attn.rel_pos_h), _bf16(attn.rel_pos_w))
+        qkv_b = _f32(attn.qkv.bias, 3 * C, dev)
+        w = _AttnWeights(_bf16(attn.qkv.weight), qkv_b, _bf16(attn.proj.weight), _f32(attn.proj.bias, C, dev),
+                         _bf16(attn.rel_pos_h), _bf16(attn.rel_pos_w), _bf16(qkv_b))
         attn._ssam_w = w
     return w
 
@@ -153,12 +155,14 @@ def _get_perm(info: dict, key: tuple, qkv: torch.Tensor, n_seq: int, heads: int,
 
 def _attention_core(attn, xn: torch.Tensor, n_seq: int, win: int, ratio: float, is_global: bool,
                     n_block: int, qkv: torch.Tensor | None = None, out: torch.Tensor | None = None,
-                    out_rows: torch.Tensor | None = None, grid: tuple[int, int] | None = None):
+                    out_rows: torch.Tensor | None = None, grid: tuple[int, int] | None = None,
+                    pad_row: torch.Tensor | None = None):
     """xn: bf16 (n_seq*win*win, C) -> (o bf16 (rows, C) raster order, perm, inv_perm).
 
     With `qkv` given (already projected, e.g. from the real tokens only), xn is
     not used; `out` / `out_rows` place the attention rows and `grid` (the image token grid of
-    windowed sequences) limits the queries to real tokens (see ops.sparse_attn)."""
+    windowed sequences) limits the queries to real tokens; `pad_row` stands for the qkv rows
+    of the windows' padding keys (see ops.sparse_attn)."""
     w = _attn_weights(attn)
     heads = attn.num_heads
     C = w.proj_w.shape[1]
@@ -171,7 +175,8 @@ def _attention_core(attn, xn: torch.Tensor, n_seq: int, win: int, ratio: float, 
     perm, inv_perm, _ = _get_perm(info, (win, ratio, n_block, perm_mode), qkv, n_seq, heads, win, d)
     n_init = ops.a_shape_n_init(N, n_block, ratio, is_global)          # sam.py:219-223
     o = ops.sparse_attn(qkv, n_seq, heads, win, d, w.rel_h, w.rel_w, perm, n_init, is_global,
-                        attn.scale, out=out, out_rows=out_rows, n_block=n_block, grid=grid)   # sam.py:206-232
+                        attn.scale, out=out, out_rows=out_rows, n_block=n_block, grid=grid,
+                        pad_row=pad_row)                                                 # sam.py:206-232
     return o, perm, inv_perm
 
 
@@ -251,10 +256,15 @@ class ToMeSAMBlock(Block):
                                     copy_out=snapshot)                                      # norm1
             qkv = torch.empty(rows.numel(), 3 * C, dtype=torch.bfloat16, device=xr.device)
             ops.gemm_bf16(xn, aw.qkv_w, aw.qkv_b, out=qkv, out_rows=_window_of_raster(B, H, W, ws, xr.device))
-            ops.fill_pad_rows(qkv, rows, aw.qkv_b)
+            # the attention reads the padding keys' qkv from aw.pad_row; only the block
+            # that computes the window permutation (from K of every window token) needs
+            # the padding rows written
+            perm_key = (ws, ratio, _FA2_N_BLOCK_LOCAL, info.get("perm_mode", "z_interleave_sort"))
+            if perm_key not in info.get("perm_cache", {}):
+                ops.fill_pad_rows(qkv, rows, aw.qkv_b)
             o = torch.empty(B * H * W, C, dtype=torch.bfloat16, device=xr.device)
             _attention_core(self.attn, None, n_win, ws, ratio, False, _FA2_N_BLOCK_LOCAL, qkv=qkv, out=o,
-                            out_rows=rows, grid=(H, W))
+                            out_rows=rows, grid=(H, W), pad_row=aw.pad_row)
             ops.gemm_bf16(o, aw.proj_w, aw.proj_b, epilogue=ops.SSAM_EPI_ADD_F32, out=xr)     # + residual
         else:
             if H != W:

@@ -59,15 +59,15 @@ def test_invalid_arguments_rejected_on_host():
     nul = None
     # null pointers / bad shapes never reach the GPU
     assert lib.ssam_gemm_bf16(nul, 64, nul, 64, 128, 256, 64, nul, 0, nul, 256, nul, nul) == _lib.SSAM_ERR_INVALID
-    assert lib.ssam_sparse_attn_fwd(1, 240, 1, 1, 14, 48, 16, 16, 16, 2, 64, 0, 1.0, 16, 48, nul, 0, 0, nul, 0, nul) == \
+    assert lib.ssam_sparse_attn_fwd(1, 240, 1, 1, 14, 48, 16, 16, 16, 2, 64, 0, 1.0, 16, 48, nul, 0, 0, nul, nul, 0, nul) == \
         _lib.SSAM_ERR_UNSUPPORTED
     # global grids need the bias workspace; a query row without any key block is rejected
-    assert lib.ssam_sparse_attn_fwd(16, 240, 1, 1, 64, 80, 16, 16, 16, 2, 64, 1, 1.0, 16, 80, nul, 0, 0, nul, 0, nul) == \
+    assert lib.ssam_sparse_attn_fwd(16, 240, 1, 1, 64, 80, 16, 16, 16, 2, 64, 1, 1.0, 16, 80, nul, 0, 0, nul, nul, 0, nul) == \
         _lib.SSAM_ERR_INVALID
-    assert lib.ssam_sparse_attn_fwd(16, 240, 1, 1, 14, 80, 16, 16, 16, 0, 64, 0, 1.0, 16, 80, nul, 0, 0, nul, 0, nul) == \
+    assert lib.ssam_sparse_attn_fwd(16, 240, 1, 1, 14, 80, 16, 16, 16, 0, 64, 0, 1.0, 16, 80, nul, 0, 0, nul, nul, 0, nul) == \
         _lib.SSAM_ERR_INVALID
     # mask blocks other than 64 / 128 tokens are not implemented
-    assert lib.ssam_sparse_attn_fwd(16, 240, 1, 1, 14, 80, 16, 16, 16, 2, 32, 0, 1.0, 16, 80, nul, 0, 0, nul, 0, nul) == \
+    assert lib.ssam_sparse_attn_fwd(16, 240, 1, 1, 14, 80, 16, 16, 16, 2, 32, 0, 1.0, 16, 80, nul, 0, 0, nul, nul, 0, nul) == \
         _lib.SSAM_ERR_UNSUPPORTED
     assert lib.ssam_stripe_sort_perm(16, 64, 1, 1, 3, 3, 64, 4, 0, 0, 16, 16, 16, 16, nul) == _lib.SSAM_ERR_INVALID
     assert lib.ssam_keep_select(16, 1, 1, 16, 17, 16, nul, nul) == _lib.SSAM_ERR_INVALID

@@ -247,3 +247,34 @@ def test_query_compaction_many_tiles_per_cta(cuda_device):
     got = out_cmp.float().cpu()[r[real].long()]
     err = (got - ref[real]).abs()
     assert err.max().item() < 3e-2 and err.mean().item() < 3e-3
+
+
+@pytest.mark.parametrize("B,H,W,heads,d", [(2, 64, 64, 4, 80), (3, 9, 13, 2, 64)])
+def test_pad_row_stands_for_padding_keys(cuda_device, B, H, W, heads, d):
+    """With `pad_row` the kernel reads the padding keys' K / V from that row and
+    never their qkv rows: qkv whose padding rows are NaN gives, bit for bit, the
+    output of the run whose padding rows hold the bias (ssam_fill_pad_rows)."""
+    ws = 14 if H > 14 else 7
+    g = torch.Generator().manual_seed(21)
+    rows = ops.window_rows(B, H, W, ws, cuda_device)
+    n_win, N, C = rows.numel() // (ws * ws), ws * ws, heads * d
+    qkv = torch.randn(n_win * N, 3 * C, generator=g).to(torch.bfloat16).to(cuda_device)
+    bias = torch.randn(3 * C, generator=g).to(cuda_device)
+    th = (torch.randn(2 * ws - 1, d, generator=g) * 0.3).to(torch.bfloat16).to(cuda_device)
+    tw = (torch.randn(2 * ws - 1, d, generator=g) * 0.3).to(torch.bfloat16).to(cuda_device)
+    perm = torch.stack([torch.randperm(N, generator=g) for _ in range(n_win * heads)]).to(torch.int32)
+    perm = perm.to(cuda_device)
+    n_init = order.a_shape_n_init(N, 64, 0.3, False)
+    filled = qkv.clone()
+    ops.fill_pad_rows(filled, rows, bias)
+    holes = qkv.clone()
+    holes[rows < 0] = float("nan")
+    out_a = torch.zeros(B * H * W, C, device=cuda_device, dtype=torch.bfloat16)
+    out_b = out_a.clone()
+    ops.sparse_attn(filled, n_win, heads, ws, d, th, tw, perm, n_init, False, d ** -0.5, out=out_a,
+                    out_rows=rows, grid=(H, W))
+    ops.sparse_attn(holes, n_win, heads, ws, d, th, tw, perm, n_init, False, d ** -0.5, out=out_b,
+                    out_rows=rows, grid=(H, W), pad_row=bias.to(torch.bfloat16))
+    assert ops.device_error() == 0
+    assert torch.isfinite(out_b.float()).all()
+    assert torch.equal(out_a, out_b)
