@@ -248,9 +248,18 @@ int ssam_im2col3x3_nhwc(const void* in, int B, int H, int W, int C, void* out, v
 /* Channels-last fp32 (B, H*W, C) -> channels-first fp32 (B, C, H*W). */
 int ssam_nhwc_to_nchw(const float* in, int B, int HW, int C, float* out, void* stream);
 
-/* Row LayerNorm fp32 -> fp32 or bf16, used by the neck LayerNorm2d. out_bf16 != 0 selects bf16. */
+/* Row LayerNorm of fp32 rows (nn.LayerNorm / the neck's LayerNorm2d over channels-last
+ * rows). out_mode 0: fp32 [n_rows, C]; 1: bf16 [n_rows, C]; 2: the bf16 3-term split
+ * [hi | lo | hi] of the result, [n_rows, 3*C] (the operand of the neck's 3x3
+ * convolution, see ssam_split_bf16x3); other values return SSAM_ERR_INVALID. */
 int ssam_layernorm_rows(const float* x, int n_rows, int C, const float* w, const float* b, float eps,
-                        void* out, int out_bf16, void* stream);
+                        void* out, int out_mode, void* stream);
+
+/* LayerNorm over C of channels-last fp32 rows (B, HW, C), stored channels-first
+ * fp32 (B, C, HW): the neck's last LayerNorm2d and the NCHW features in one pass
+ * (same arithmetic as ssam_layernorm_rows). C <= 256 (SSAM_ERR_UNSUPPORTED above). */
+int ssam_layernorm_nchw(const float* x, int B, int HW, int C, const float* w, const float* b, float eps,
+                        float* out, void* stream);
 
 /* Row LayerNorm fp32 -> bf16 that also stores its input rows unchanged to
  * copy (fp32 [n_rows, C], 16-byte aligned). The encoder keeps its intermediate

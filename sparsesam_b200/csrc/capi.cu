@@ -151,8 +151,13 @@ int ssam_nhwc_to_nchw(const float* in, int B, int HW, int C, float* out, void* s
 }
 
 int ssam_layernorm_rows(const float* x, int n_rows, int C, const float* w, const float* b, float eps, void* out,
-                        int out_bf16, void* stream) {
-  return ssam::layernorm_rows(x, n_rows, C, w, b, eps, out, out_bf16, static_cast<cudaStream_t>(stream));
+                        int out_mode, void* stream) {
+  return ssam::layernorm_rows(x, n_rows, C, w, b, eps, out, out_mode, static_cast<cudaStream_t>(stream));
+}
+
+int ssam_layernorm_nchw(const float* x, int B, int HW, int C, const float* w, const float* b, float eps, float* out,
+                        void* stream) {
+  return ssam::layernorm_nchw(x, B, HW, C, w, b, eps, out, static_cast<cudaStream_t>(stream));
 }
 
 int ssam_layernorm_rows_copy(const float* x, int n_rows, int C, const float* w, const float* b, float eps,

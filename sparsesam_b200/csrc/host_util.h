@@ -78,7 +78,9 @@ int layernorm_gather(const float* x, int64_t ldx, const int32_t* src_rows, int n
                      const float* b, float eps, void* out, int64_t ld_out, cudaStream_t stream);
 int hilbert_order(int H, int W, int32_t* perm, int32_t* inv_perm, cudaStream_t stream);
 int layernorm_rows(const float* x, int n_rows, int C, const float* w, const float* b, float eps, void* out,
-                   int out_bf16, cudaStream_t stream);
+                   int out_mode, cudaStream_t stream);
+int layernorm_nchw(const float* x, int B, int HW, int C, const float* w, const float* b, float eps, float* out,
+                   cudaStream_t stream);
 int layernorm_rows_copy(const float* x, int n_rows, int C, const float* w, const float* b, float eps, void* out,
                         float* copy, cudaStream_t stream);
 int window_rows(int B, int H, int W, int ws, int32_t* rows, cudaStream_t stream);

@@ -13,48 +13,23 @@ namespace ssam {
 // One warp per output row; the row lives in registers as float4 chunks.
 // Matches torch.nn.LayerNorm: biased variance, (x - mean) * rsqrt(var + eps).
 // COPY: the input row is also stored unchanged to copy[r] (fp32, C wide).
+// OUT: 0 fp32, 1 bf16, 2 the bf16 3-term split [hi | lo | hi] (3C columns; the
+// neck's 3x3 convolution operand, hi = bf16(y), lo = bf16(y - hi)).
 // ---------------------------------------------------------------------------
-template <int CHUNKS, bool OUT_BF16, bool COPY = false>
-__global__ void layernorm_rows_kernel(const float* __restrict__ x, int64_t ldx, const int32_t* __restrict__ src_rows,
-                                      int n_rows, int C, const float* __restrict__ w, const float* __restrict__ b,
-                                      float eps, void* __restrict__ out, int64_t ld_out, float* __restrict__ copy) {
-  const int warps_per_block = blockDim.x >> 5;
-  const int r = blockIdx.x * warps_per_block + (threadIdx.x >> 5);
+enum { kLnF32 = 0, kLnBf16 = 1, kLnSplit3 = 2 };
+
+// Mean and 1/std of one row held as float4 chunks (lane + 32 i) by a warp; the
+// one reduction order every LayerNorm kernel here uses.
+template <int CHUNKS>
+__device__ __forceinline__ void ln_row_stats(const float4 (&v)[CHUNKS], int nc4, int C, float eps, float& mean,
+                                             float& rstd) {
   const int lane = threadIdx.x & 31;
-  if (r >= n_rows) return;
-  const int src = src_rows != nullptr ? __ldg(src_rows + r) : r;
-  const int nc4 = C >> 2;
-  if (src < 0) {
-    for (int i = lane; i < nc4; i += 32) {
-      if constexpr (OUT_BF16) {
-        reinterpret_cast<uint2*>(static_cast<__nv_bfloat16*>(out) + static_cast<int64_t>(r) * ld_out)[i] =
-            make_uint2(0u, 0u);
-      } else {
-        reinterpret_cast<float4*>(static_cast<float*>(out) + static_cast<int64_t>(r) * ld_out)[i] =
-            make_float4(0.f, 0.f, 0.f, 0.f);
-      }
-    }
-    return;
-  }
-  const float4* xr = reinterpret_cast<const float4*>(x + static_cast<int64_t>(src) * ldx);
-  float4 v[CHUNKS];
   float s = 0.f;
 #pragma unroll
-  for (int i = 0; i < CHUNKS; ++i) {
-    const int c = lane + 32 * i;
-    v[i] = c < nc4 ? __ldg(xr + c) : make_float4(0.f, 0.f, 0.f, 0.f);
-    s += (v[i].x + v[i].y) + (v[i].z + v[i].w);
-  }
-  if constexpr (COPY) {
-#pragma unroll
-    for (int i = 0; i < CHUNKS; ++i) {
-      const int c = lane + 32 * i;
-      if (c < nc4) reinterpret_cast<float4*>(copy + static_cast<int64_t>(r) * C)[c] = v[i];
-    }
-  }
+  for (int i = 0; i < CHUNKS; ++i) s += (v[i].x + v[i].y) + (v[i].z + v[i].w);
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
-  const float mean = s / C;
+  mean = s / C;
   float q = 0.f;
 #pragma unroll
   for (int i = 0; i < CHUNKS; ++i) {
@@ -66,7 +41,47 @@ __global__ void layernorm_rows_kernel(const float* __restrict__ x, int64_t ldx, 
   }
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) q += __shfl_xor_sync(0xffffffffu, q, o);
-  const float rstd = rsqrtf(q / C + eps);
+  rstd = rsqrtf(q / C + eps);
+}
+
+template <int CHUNKS, int OUT, bool COPY = false>
+__global__ void layernorm_rows_kernel(const float* __restrict__ x, int64_t ldx, const int32_t* __restrict__ src_rows,
+                                      int n_rows, int C, const float* __restrict__ w, const float* __restrict__ b,
+                                      float eps, void* __restrict__ out, int64_t ld_out, float* __restrict__ copy) {
+  const int warps_per_block = blockDim.x >> 5;
+  const int r = blockIdx.x * warps_per_block + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (r >= n_rows) return;
+  const int src = src_rows != nullptr ? __ldg(src_rows + r) : r;
+  const int nc4 = C >> 2;
+  if (src < 0) {
+    for (int i = lane; i < (OUT == kLnSplit3 ? 3 * nc4 : nc4); i += 32) {
+      if constexpr (OUT != kLnF32) {
+        reinterpret_cast<uint2*>(static_cast<__nv_bfloat16*>(out) + static_cast<int64_t>(r) * ld_out)[i] =
+            make_uint2(0u, 0u);
+      } else {
+        reinterpret_cast<float4*>(static_cast<float*>(out) + static_cast<int64_t>(r) * ld_out)[i] =
+            make_float4(0.f, 0.f, 0.f, 0.f);
+      }
+    }
+    return;
+  }
+  const float4* xr = reinterpret_cast<const float4*>(x + static_cast<int64_t>(src) * ldx);
+  float4 v[CHUNKS];
+#pragma unroll
+  for (int i = 0; i < CHUNKS; ++i) {
+    const int c = lane + 32 * i;
+    v[i] = c < nc4 ? __ldg(xr + c) : make_float4(0.f, 0.f, 0.f, 0.f);
+  }
+  if constexpr (COPY) {
+#pragma unroll
+    for (int i = 0; i < CHUNKS; ++i) {
+      const int c = lane + 32 * i;
+      if (c < nc4) reinterpret_cast<float4*>(copy + static_cast<int64_t>(r) * C)[c] = v[i];
+    }
+  }
+  float mean, rstd;
+  ln_row_stats<CHUNKS>(v, nc4, C, eps, mean, rstd);
   const float4* w4 = reinterpret_cast<const float4*>(w);
   const float4* b4 = reinterpret_cast<const float4*>(b);
 #pragma unroll
@@ -78,9 +93,17 @@ __global__ void layernorm_rows_kernel(const float* __restrict__ x, int64_t ldx, 
       const float y1 = (v[i].y - mean) * rstd * ww.y + bb.y;
       const float y2 = (v[i].z - mean) * rstd * ww.z + bb.z;
       const float y3 = (v[i].w - mean) * rstd * ww.w + bb.w;
-      if constexpr (OUT_BF16) {
+      if constexpr (OUT == kLnBf16) {
         reinterpret_cast<uint2*>(static_cast<__nv_bfloat16*>(out) + static_cast<int64_t>(r) * ld_out)[c] =
             make_uint2(pack_bf16x2(y0, y1), pack_bf16x2(y2, y3));
+      } else if constexpr (OUT == kLnSplit3) {
+        const float h0 = __bfloat162float(__float2bfloat16_rn(y0)), h1 = __bfloat162float(__float2bfloat16_rn(y1));
+        const float h2 = __bfloat162float(__float2bfloat16_rn(y2)), h3 = __bfloat162float(__float2bfloat16_rn(y3));
+        uint2* row = reinterpret_cast<uint2*>(static_cast<__nv_bfloat16*>(out) + static_cast<int64_t>(r) * ld_out);
+        const uint2 hi = make_uint2(pack_bf16x2(h0, h1), pack_bf16x2(h2, h3));
+        row[c] = hi;
+        row[nc4 + c] = make_uint2(pack_bf16x2(y0 - h0, y1 - h1), pack_bf16x2(y2 - h2, y3 - h3));
+        row[2 * nc4 + c] = hi;
       } else {
         reinterpret_cast<float4*>(static_cast<float*>(out) + static_cast<int64_t>(r) * ld_out)[c] =
             make_float4(y0, y1, y2, y3);
@@ -89,7 +112,7 @@ __global__ void layernorm_rows_kernel(const float* __restrict__ x, int64_t ldx, 
   }
 }
 
-template <bool OUT_BF16, bool COPY = false>
+template <int OUT, bool COPY = false>
 static int launch_layernorm(const float* x, int64_t ldx, const int32_t* src_rows, int n_rows, int C, const float* w,
                             const float* b, float eps, void* out, int64_t ld_out, cudaStream_t stream,
                             float* copy = nullptr) {
@@ -99,7 +122,7 @@ static int launch_layernorm(const float* x, int64_t ldx, const int32_t* src_rows
   const dim3 grid((n_rows + wpb - 1) / wpb), block(32 * wpb);
 #define SSAM_LN_CASE(K)                                                                                           \
   case K:                                                                                                         \
-    layernorm_rows_kernel<K, OUT_BF16, COPY><<<grid, block, 0, stream>>>(x, ldx, src_rows, n_rows, C, w, b, eps, out, \
+    layernorm_rows_kernel<K, OUT, COPY><<<grid, block, 0, stream>>>(x, ldx, src_rows, n_rows, C, w, b, eps, out, \
                                                                    ld_out, copy);                                 \
     break;
   switch (chunks) {
@@ -109,20 +132,20 @@ static int launch_layernorm(const float* x, int64_t ldx, const int32_t* src_rows
     SSAM_LN_CASE(8)
     SSAM_LN_CASE(16)
     case 3:
-      layernorm_rows_kernel<4, OUT_BF16, COPY><<<grid, block, 0, stream>>>(x, ldx, src_rows, n_rows, C, w, b, eps, out,
+      layernorm_rows_kernel<4, OUT, COPY><<<grid, block, 0, stream>>>(x, ldx, src_rows, n_rows, C, w, b, eps, out,
                                                                      ld_out, copy);
       break;
     case 9: case 10:  // ViT-H (C = 1280): exactly 10 float4 per lane
-      layernorm_rows_kernel<10, OUT_BF16, COPY><<<grid, block, 0, stream>>>(x, ldx, src_rows, n_rows, C, w, b, eps, out,
+      layernorm_rows_kernel<10, OUT, COPY><<<grid, block, 0, stream>>>(x, ldx, src_rows, n_rows, C, w, b, eps, out,
                                                                       ld_out, copy);
       break;
     case 5: case 6: case 7:
-      layernorm_rows_kernel<8, OUT_BF16, COPY><<<grid, block, 0, stream>>>(x, ldx, src_rows, n_rows, C, w, b, eps, out,
+      layernorm_rows_kernel<8, OUT, COPY><<<grid, block, 0, stream>>>(x, ldx, src_rows, n_rows, C, w, b, eps, out,
                                                                      ld_out, copy);
       break;
     default:
       if (chunks > 16) return SSAM_ERR_UNSUPPORTED;
-      layernorm_rows_kernel<16, OUT_BF16, COPY><<<grid, block, 0, stream>>>(x, ldx, src_rows, n_rows, C, w, b, eps, out,
+      layernorm_rows_kernel<16, OUT, COPY><<<grid, block, 0, stream>>>(x, ldx, src_rows, n_rows, C, w, b, eps, out,
                                                                       ld_out, copy);
   }
 #undef SSAM_LN_CASE
@@ -135,16 +158,79 @@ int layernorm_gather(const float* x, int64_t ldx, const int32_t* src_rows, int n
   if (n_rows == 0) return SSAM_OK;
   if (C % 4 || ldx % 4 || ld_out % 4 || ldx < C || ld_out < C) return SSAM_ERR_ALIGN;
   if (!aligned16(x) || !aligned16(w) || !aligned16(b) || (reinterpret_cast<uintptr_t>(out) & 7)) return SSAM_ERR_ALIGN;
-  return launch_layernorm<true>(x, ldx, src_rows, n_rows, C, w, b, eps, out, ld_out, stream);
+  return launch_layernorm<kLnBf16>(x, ldx, src_rows, n_rows, C, w, b, eps, out, ld_out, stream);
 }
 
 int layernorm_rows(const float* x, int n_rows, int C, const float* w, const float* b, float eps, void* out,
-                   int out_bf16, cudaStream_t stream) {
+                   int out_mode, cudaStream_t stream) {
   if (x == nullptr || w == nullptr || b == nullptr || out == nullptr || n_rows < 0 || C <= 0) return SSAM_ERR_INVALID;
+  if (out_mode < kLnF32 || out_mode > kLnSplit3) return SSAM_ERR_INVALID;
   if (n_rows == 0) return SSAM_OK;
   if (C % 4 || !aligned16(x) || !aligned16(w) || !aligned16(b) || !aligned16(out)) return SSAM_ERR_ALIGN;
-  return out_bf16 ? launch_layernorm<true>(x, C, nullptr, n_rows, C, w, b, eps, out, C, stream)
-                  : launch_layernorm<false>(x, C, nullptr, n_rows, C, w, b, eps, out, C, stream);
+  switch (out_mode) {
+    case kLnF32:
+      return launch_layernorm<kLnF32>(x, C, nullptr, n_rows, C, w, b, eps, out, C, stream);
+    case kLnBf16:
+      return launch_layernorm<kLnBf16>(x, C, nullptr, n_rows, C, w, b, eps, out, C, stream);
+    default:
+      return launch_layernorm<kLnSplit3>(x, C, nullptr, n_rows, C, w, b, eps, out, 3 * static_cast<int64_t>(C),
+                                         stream);
+  }
+}
+
+// LayerNorm of channels-last fp32 rows (B, HW, C), stored channels-first fp32
+// (B, C, HW): the neck's last LayerNorm2d and the features' NCHW layout in one
+// pass. A CTA normalises 32 consecutive pixels of one image (a warp per row, the
+// reduction order of layernorm_rows) into a [C][32] shared-memory tile and writes
+// it out as 128-byte channel rows.
+constexpr int kLnNchwMaxC = 256;
+__global__ void __launch_bounds__(256) layernorm_nchw_kernel(const float* __restrict__ x, int HW, int C,
+                                                             const float* __restrict__ w, const float* __restrict__ b,
+                                                             float eps, float* __restrict__ out) {
+  __shared__ float tile[kLnNchwMaxC][33];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int bimg = blockIdx.y, p0 = blockIdx.x * 32;
+  const int nc4 = C >> 2;
+  const float4* w4 = reinterpret_cast<const float4*>(w);
+  const float4* b4 = reinterpret_cast<const float4*>(b);
+  for (int j = warp; j < 32; j += 8) {
+    const int p = p0 + j;
+    if (p >= HW) break;
+    const float4* xr = reinterpret_cast<const float4*>(x + (static_cast<int64_t>(bimg) * HW + p) * C);
+    float4 v[kLnNchwMaxC / 128];
+#pragma unroll
+    for (int i = 0; i < kLnNchwMaxC / 128; ++i) {
+      const int c = lane + 32 * i;
+      v[i] = c < nc4 ? __ldg(xr + c) : make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+    float mean, rstd;
+    ln_row_stats<kLnNchwMaxC / 128>(v, nc4, C, eps, mean, rstd);
+#pragma unroll
+    for (int i = 0; i < kLnNchwMaxC / 128; ++i) {
+      const int c = lane + 32 * i;
+      if (c < nc4) {
+        const float4 ww = __ldg(w4 + c), bb = __ldg(b4 + c);
+        tile[4 * c][j] = (v[i].x - mean) * rstd * ww.x + bb.x;
+        tile[4 * c + 1][j] = (v[i].y - mean) * rstd * ww.y + bb.y;
+        tile[4 * c + 2][j] = (v[i].z - mean) * rstd * ww.z + bb.z;
+        tile[4 * c + 3][j] = (v[i].w - mean) * rstd * ww.w + bb.w;
+      }
+    }
+  }
+  __syncthreads();
+  const int p = p0 + lane;
+  for (int c = warp; c < C; c += 8)
+    if (p < HW) out[(static_cast<int64_t>(bimg) * C + c) * HW + p] = tile[c][lane];
+}
+
+int layernorm_nchw(const float* x, int B, int HW, int C, const float* w, const float* b, float eps, float* out,
+                   cudaStream_t stream) {
+  if (x == nullptr || w == nullptr || b == nullptr || out == nullptr || B <= 0 || HW <= 0 || C <= 0)
+    return SSAM_ERR_INVALID;
+  if (C > kLnNchwMaxC || B > 65535) return SSAM_ERR_UNSUPPORTED;
+  if (C % 4 || !aligned16(x) || !aligned16(w) || !aligned16(b)) return SSAM_ERR_ALIGN;
+  layernorm_nchw_kernel<<<dim3((HW + 31) / 32, B), 256, 0, stream>>>(x, HW, C, w, b, eps, out);
+  return status_from_cuda(cudaGetLastError());
 }
 
 int layernorm_rows_copy(const float* x, int n_rows, int C, const float* w, const float* b, float eps, void* out,
@@ -154,7 +240,7 @@ int layernorm_rows_copy(const float* x, int n_rows, int C, const float* w, const
   if (n_rows == 0) return SSAM_OK;
   if (C % 4 || !aligned16(x) || !aligned16(w) || !aligned16(b) || !aligned16(out) || !aligned16(copy))
     return SSAM_ERR_ALIGN;
-  return launch_layernorm<true, true>(x, C, nullptr, n_rows, C, w, b, eps, out, C, stream, copy);
+  return launch_layernorm<kLnBf16, true>(x, C, nullptr, n_rows, C, w, b, eps, out, C, stream, copy);
 }
 
 // ---------------------------------------------------------------------------

@@ -371,17 +371,22 @@ def nhwc_to_nchw(x: torch.Tensor, B: int, H: int, W: int, C: int, out: torch.Ten
 
 
 def layernorm_rows(x: torch.Tensor, w: torch.Tensor, b: torch.Tensor, eps: float, out_bf16: bool,
-                   out: torch.Tensor | None = None, copy_out: torch.Tensor | None = None) -> torch.Tensor:
+                   out: torch.Tensor | None = None, copy_out: torch.Tensor | None = None,
+                   split3: bool = False) -> torch.Tensor:
     """Row LayerNorm of fp32 x (rows, C). `copy_out` (fp32, x's shape; bf16 output only)
-    also receives x unchanged, read once for both."""
+    also receives x unchanged, read once for both. `split3`: the bf16 3-term split
+    [hi | lo | hi] of the result, (rows, 3C), as split_bf16x3 of the fp32 output."""
     _check_cuda(x, w, b, out, copy_out)
     x2 = x.reshape(-1, x.shape[-1])
     n, C = x2.shape
+    if split3 and (out_bf16 or copy_out is not None):
+        raise ValueError("split3 is its own output mode")
     if out is None:
-        out = torch.empty(n, C, dtype=torch.bfloat16 if out_bf16 else torch.float32, device=x.device)
+        out = torch.empty(n, 3 * C if split3 else C, dtype=torch.bfloat16 if (out_bf16 or split3) else torch.float32,
+                          device=x.device)
     if copy_out is None:
         _lib.call("ssam_layernorm_rows", x2.data_ptr(), n, C, w.data_ptr(), b.data_ptr(), float(eps),
-                  out.data_ptr(), 1 if out_bf16 else 0, _stream(x))
+                  out.data_ptr(), 2 if split3 else (1 if out_bf16 else 0), _stream(x))
         return out
     if not out_bf16:
         raise ValueError("copy_out is supported with the bf16 output")
@@ -389,6 +394,20 @@ def layernorm_rows(x: torch.Tensor, w: torch.Tensor, b: torch.Tensor, eps: float
         raise ValueError("copy_out must be a contiguous fp32 tensor with x's number of elements")
     _lib.call("ssam_layernorm_rows_copy", x2.data_ptr(), n, C, w.data_ptr(), b.data_ptr(), float(eps),
               out.data_ptr(), copy_out.data_ptr(), _stream(x))
+    return out
+
+
+def layernorm_nchw(x: torch.Tensor, B: int, H: int, W: int, w: torch.Tensor, b: torch.Tensor,
+                   eps: float) -> torch.Tensor:
+    """LayerNorm over C of channels-last fp32 rows (B*H*W, C) -> fp32 (B, C, H, W)."""
+    _check_cuda(x, w, b)
+    x2 = x.reshape(-1, x.shape[-1])
+    if x2.dtype != torch.float32 or not x2.is_contiguous() or x2.shape[0] != B * H * W:
+        raise ValueError("x must be contiguous fp32 (B*H*W, C)")
+    C = x2.shape[1]
+    out = torch.empty(B, C, H, W, dtype=torch.float32, device=x.device)
+    _lib.call("ssam_layernorm_nchw", x2.data_ptr(), B, H * W, C, w.data_ptr(), b.data_ptr(), float(eps),
+              out.data_ptr(), _stream(x))
     return out
 
 

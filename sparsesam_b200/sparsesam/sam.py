@@ -366,13 +366,14 @@ def encoder_forward(enc, img: torch.Tensor):
             else:
                 pending = torch.empty_like(x)
                 interm.append(pending.view(B, gh, gw, C))
-    # neck: fp32 activations and weights through the 3-term split (3x K)
+    # neck: fp32 activations and weights through the 3-term split (3x K); the first
+    # LayerNorm2d writes the split operand of the 3x3 convolution, the second the
+    # NCHW features
     y = ops.gemm_bf16(ops.split_bf16x3(x), w.neck0_w, None, epilogue=ops.SSAM_EPI_F32, k_split=3)
-    ya = ops.layernorm_rows(y, w.ln_a_w, w.ln_a_b, w.eps_a, out_bf16=False)
-    cols3 = ops.im2col3x3_nhwc(ops.split_bf16x3(ya).view(B, gh, gw, -1))
+    ya3 = ops.layernorm_rows(y, w.ln_a_w, w.ln_a_b, w.eps_a, out_bf16=False, split3=True)
+    cols3 = ops.im2col3x3_nhwc(ya3.view(B, gh, gw, -1))
     z = ops.gemm_bf16(cols3, w.neck2_w, None, epilogue=ops.SSAM_EPI_F32, k_split=3)
-    z = ops.layernorm_rows(z, w.ln_b_w, w.ln_b_b, w.eps_b, out_bf16=False)
-    feats = ops.nhwc_to_nchw(z, B, gh, gw, z.shape[1])
+    feats = ops.layernorm_nchw(z, B, gh, gw, w.ln_b_w, w.ln_b_b, w.eps_b)
     return feats, interm
 
 

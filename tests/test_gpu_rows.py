@@ -89,6 +89,22 @@ def test_neck_pieces(cuda_device):
     assert torch.equal(xb.view(B, H * W, 32), pos.expand(B, -1, -1))
 
 
+@pytest.mark.parametrize("B,H,W,C", [(2, 64, 64, 256), (3, 7, 9, 32), (1, 5, 13, 256)])
+def test_neck_layernorms_fused(cuda_device, B, H, W, C):
+    """The neck's LayerNorm2d outputs: the 3-term split mode equals split_bf16x3 of
+    the fp32 LayerNorm, and the NCHW mode equals the fp32 LayerNorm transposed, both
+    bit for bit (one reduction order); pixel counts that are not multiples of 32
+    exercise the last partial tile."""
+    g = torch.Generator().manual_seed(3)
+    y = (torch.randn(B * H * W, C, generator=g) * 2 + 0.5).to(cuda_device)
+    lw = torch.randn(C, generator=g).to(cuda_device)
+    lb = torch.randn(C, generator=g).to(cuda_device)
+    ln = ops.layernorm_rows(y, lw, lb, 1e-6, out_bf16=False)
+    assert torch.equal(ops.layernorm_rows(y, lw, lb, 1e-6, out_bf16=False, split3=True), ops.split_bf16x3(ln))
+    assert torch.equal(ops.layernorm_nchw(y, B, H, W, lw, lb, 1e-6), ln.view(B, H, W, C).permute(0, 3, 1, 2))
+    assert ops.device_error() == 0
+
+
 def test_split_bf16x3_parts(cuda_device):
     x = torch.randn(37, 96, device=cuda_device) * 3
     out = ops.split_bf16x3(x).float()
