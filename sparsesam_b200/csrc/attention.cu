@@ -175,7 +175,7 @@ struct AttnCfg {
   // its [P_H | P_W] while the current tile's QK^T is being issued)
   static constexpr int kQBuf = SMALL ? 3 : 2;
   static constexpr int kStages = 2;               // K / V / one-hot stages (3 measured slower for windows)
-  static_assert(kStages == kS && kS == 2, "one commit per block frees S, K / V stage and O: indices g % 2");
+  static_assert(kStages == kS && kS == 2, "stage and S / O indices are g % 2 (one fill per block)");
   static constexpr int kBW = SMALL ? 16 : 64;     // bias columns per table (>= win)
   static constexpr int kNT = 32;                  // rows per table (SMALL), stacked Th ; Tw
   static constexpr int kABCols = kBW;             // 2 x kBW fp16 = kBW columns
@@ -427,9 +427,9 @@ enum {
   kBarQFull = 1,     // [kQBuf <= 3]  loader lanes (cp.async)
   kBarQEmpty = 4,    // [kQBuf <= 3]  UMMA commit after the tile's last QK^T
   kBarKFull = 7,     // [3]  K loader lanes (cp.async)
-  kBarKEmpty = 10,   // [3]  UMMA commit after each QK^T reading the stage
+  kBarKEmpty = 10,   // [3]  compaction: UMMA commit after the fill's last QK^T (else S-full frees K)
   kBarVFull = 13,    // [3]  V loader lanes (cp.async)
-  kBarVEmpty = 16,   // [3]  UMMA commit after each P.V reading the stage
+  kBarVEmpty = 16,   // [3]  compaction: UMMA commit after the fill's last P.V (else O-done frees V)
   kBarPHFull = 19,   //      UMMA commit (SMALL)
   kBarPHFree = 20,   //      K loaders (SMALL)
   kBarABFull = 21,   // [2]  A_bias of the tile is in TMEM (SMALL: K loaders; LARGE: softmax)
@@ -992,7 +992,7 @@ __global__ void __launch_bounds__(attn_threads(SMALL), 1)
         for (int ks = 0; ks < kAttnBN / 16; ++ks)
           umma_f16_ts(tO, tP + ks * 8 + (ks >= kAttnBN / 32 ? 32 : 0), dv + ks * 32, idesc_o,
                       (c.j > 0 || ks > 0) ? 1u : 0u);
-        umma_commit(&bars[kBarODone + (c.g & 1)]);  // also frees S block sbuf
+        umma_commit(&bars[kBarODone + (c.g & 1)]);  // also frees S block sbuf (and, without compaction, V)
         if (SMALL && CP && !((nexts >> (c.lt & 3)) & 1u)) umma_commit(&bars[kBarVEmpty + st]);  // last P.V
         if (SMALL && c.j == c.tb.n - 1) umma_commit(&bars[kBarOFull + ob]);
         return true;
