@@ -51,16 +51,22 @@ __device__ __forceinline__ void gemm_epilogue_chunk(const GemmParams& p, int row
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
       const float4 b = __ldg(b4 + i);
-      v[4 * i + 0] += b.x;
-      v[4 * i + 1] += b.y;
-      v[4 * i + 2] += b.z;
-      v[4 * i + 3] += b.w;
+      const float2 lo = add2(make_float2(v[4 * i + 0], v[4 * i + 1]), make_float2(b.x, b.y));
+      const float2 hi = add2(make_float2(v[4 * i + 2], v[4 * i + 3]), make_float2(b.z, b.w));
+      v[4 * i + 0] = lo.x;
+      v[4 * i + 1] = lo.y;
+      v[4 * i + 2] = hi.x;
+      v[4 * i + 3] = hi.y;
     }
   }
   if constexpr (EPI == SSAM_EPI_BF16 || EPI == SSAM_EPI_GELU_BF16) {
     if constexpr (EPI == SSAM_EPI_GELU_BF16) {
 #pragma unroll
-      for (int i = 0; i < 32; ++i) v[i] = gelu_exact(v[i]);
+      for (int i = 0; i < 16; ++i) {
+        const float2 g = gelu_exact2(make_float2(v[2 * i], v[2 * i + 1]));
+        v[2 * i] = g.x;
+        v[2 * i + 1] = g.y;
+      }
     }
     const int orow = p.out_rows != nullptr ? __ldg(p.out_rows + row) : row;
     if (orow < 0) return;
@@ -113,15 +119,21 @@ __device__ __forceinline__ void gemm_epilogue_chunk_staged(const GemmParams& p, 
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
       const float4 b = __ldg(b4 + i);
-      v[4 * i + 0] += b.x;
-      v[4 * i + 1] += b.y;
-      v[4 * i + 2] += b.z;
-      v[4 * i + 3] += b.w;
+      const float2 lo = add2(make_float2(v[4 * i + 0], v[4 * i + 1]), make_float2(b.x, b.y));
+      const float2 hi = add2(make_float2(v[4 * i + 2], v[4 * i + 3]), make_float2(b.z, b.w));
+      v[4 * i + 0] = lo.x;
+      v[4 * i + 1] = lo.y;
+      v[4 * i + 2] = hi.x;
+      v[4 * i + 3] = hi.y;
     }
   }
   if constexpr (EPI == SSAM_EPI_GELU_BF16) {
 #pragma unroll
-    for (int i = 0; i < 32; ++i) v[i] = gelu_exact(v[i]);
+    for (int i = 0; i < 16; ++i) {
+      const float2 g = gelu_exact2(make_float2(v[2 * i], v[2 * i + 1]));
+      v[2 * i] = g.x;
+      v[2 * i + 1] = g.y;
+    }
   }
   __syncwarp();  // the previous chunk's read-back is done
 #pragma unroll
@@ -186,10 +198,12 @@ __device__ __forceinline__ void gemm_epilogue_chunk_bulk(const GemmParams& p, in
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
       const float4 b = __ldg(b4 + i);
-      v[4 * i + 0] += b.x;
-      v[4 * i + 1] += b.y;
-      v[4 * i + 2] += b.z;
-      v[4 * i + 3] += b.w;
+      const float2 lo = add2(make_float2(v[4 * i + 0], v[4 * i + 1]), make_float2(b.x, b.y));
+      const float2 hi = add2(make_float2(v[4 * i + 2], v[4 * i + 3]), make_float2(b.z, b.w));
+      v[4 * i + 0] = lo.x;
+      v[4 * i + 1] = lo.y;
+      v[4 * i + 2] = hi.x;
+      v[4 * i + 3] = hi.y;
     }
   }
   if constexpr (EPI == SSAM_EPI_GELU_BF16) {
