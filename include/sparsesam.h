@@ -245,6 +245,17 @@ int ssam_broadcast_rows(const float* pos, int B, int T, int C, float* x, void* s
  * permuted to (Cout, 3, 3, Cin). */
 int ssam_im2col3x3_nhwc(const void* in, int B, int H, int W, int C, void* out, void* stream);
 
+/* 3x3 / pad 1 convolution of a channels-last bf16 grid in (B, H, W, Cin) as an
+ * implicit GEMM on the tensor cores (the im2col is never written): out fp32
+ * [B*H*W, Cout] = im2col3x3(in) . w^T (+ bias, which may be NULL), w bf16
+ * [Cout, 9*Cin] in (ky, kx, cin) column order (a Conv2d weight permuted to
+ * (Cout, 3, 3, Cin)); the results equal ssam_im2col3x3_nhwc followed by
+ * ssam_gemm_bf16 with SSAM_EPI_F32 bit for bit. Needs Cin a multiple of 64,
+ * Cout a multiple of 32, W dividing 128 and H*W a multiple of 128
+ * (SSAM_ERR_UNSUPPORTED otherwise). */
+int ssam_conv3x3_nhwc(const void* in, int B, int H, int W, int Cin, const void* w, int Cout, const float* bias,
+                      void* out, void* stream);
+
 /* Channels-last fp32 (B, H*W, C) -> channels-first fp32 (B, C, H*W). */
 int ssam_nhwc_to_nchw(const float* in, int B, int HW, int C, float* out, void* stream);
 

@@ -146,6 +146,11 @@ int ssam_im2col3x3_nhwc(const void* in, int B, int H, int W, int C, void* out, v
   return ssam::im2col3x3_nhwc(in, B, H, W, C, out, static_cast<cudaStream_t>(stream));
 }
 
+int ssam_conv3x3_nhwc(const void* in, int B, int H, int W, int Cin, const void* w, int Cout, const float* bias,
+                      void* out, void* stream) {
+  return ssam::conv3x3_nhwc(in, B, H, W, Cin, w, Cout, bias, out, static_cast<cudaStream_t>(stream));
+}
+
 int ssam_nhwc_to_nchw(const float* in, int B, int HW, int C, float* out, void* stream) {
   return ssam::nhwc_to_nchw(in, B, HW, C, out, static_cast<cudaStream_t>(stream));
 }

@@ -39,6 +39,9 @@ struct GemmParams {
   void* out;
   int64_t ldo;
   const int32_t* out_rows;
+  // implicit 3x3 convolution (pair kernel, CONV): A is a channels-last (B, H, W, Cin)
+  // tensor map, K = 9 Cin in (ky, kx, cin) order, rows are the B*H*W output pixels
+  int conv_w, conv_hw;
 };
 
 template <int EPI>
@@ -452,7 +455,7 @@ struct PairCfg {
 static_assert((2 * kGemmStages + 5) * 8 + 8 <= 256, "mbarrier block overlaps the epilogue staging");
 static_assert(kGemmSmemBytes <= 227 * 1024, "shared memory per CTA");
 
-template <int EPI>
+template <int EPI, bool CONV = false>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGemmThreads, 1)
     gemm_bf16_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                           const GemmParams p) {
@@ -530,7 +533,21 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGemmThreads, 1)
 #pragma unroll
           for (int s = 0; s < PC::kSub; ++s) {
             const int kx = (ks * PC::kSub + s) * kGemmBK;
-            tma_load_2d_pair(sA + stage * PC::kStageABytes + s * kPairABytes, &tmA, bar, kx, mb * kPairBM + rank * 128);
+            if constexpr (CONV) {
+              // this CTA's 128 output pixels are 128 / W whole rows of one image; the
+              // 64 input channels of tap (ky, kx) are the same rows shifted by (ky - 1,
+              // kx - 1), read as one 4-D box (outside the image: zeros, the padding)
+              const int m0 = mb * kPairBM + rank * 128;
+              const int img = m0 / p.conv_hw;
+              const int y0 = (m0 - img * p.conv_hw) / p.conv_w;
+              const int cin = p.K / 9;
+              const int tap = kx / cin;
+              tma_load_4d_pair(sA + stage * PC::kStageABytes + s * kPairABytes, &tmA, bar, kx - tap * cin,
+                               tap % 3 - 1, y0 + tap / 3 - 1, img);
+            } else {
+              tma_load_2d_pair(sA + stage * PC::kStageABytes + s * kPairABytes, &tmA, bar, kx,
+                               mb * kPairBM + rank * 128);
+            }
             tma_load_2d_pair(sB + stage * PC::kStageBBytes + s * kPairBBytes, &tmB, bar, kx, nb * kGemmBN + rank * 128);
           }
           issued_mask |= 1u << stage;
@@ -640,12 +657,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGemmThreads, 1)
   if (warp == 1) tmem_dealloc_pair(tmem_base, kGemmTmemCols);
 }
 
-template <int EPI>
+template <int EPI, bool CONV = false>
 static int launch_gemm_pair(const CUtensorMap& ta, const CUtensorMap& tb, const GemmParams& p, cudaStream_t stream) {
   static PerDeviceOnce configured;
   const int dev = current_device();
   const int st = configured.run(dev, [] {
-    return status_from_cuda(cudaFuncSetAttribute(gemm_bf16_pair_kernel<EPI>,
+    return status_from_cuda(cudaFuncSetAttribute(gemm_bf16_pair_kernel<EPI, CONV>,
                                                  cudaFuncAttributeMaxDynamicSharedMemorySize,
                                                  PairCfg<EPI>::kSmemBytes));
   });
@@ -655,7 +672,7 @@ static int launch_gemm_pair(const CUtensorMap& ta, const CUtensorMap& tb, const 
   const int tiles = m_tiles * n_tiles;
   const int max_pairs = num_sms(dev) / 2;
   const int pairs = tiles < max_pairs ? tiles : max_pairs;
-  gemm_bf16_pair_kernel<EPI><<<2 * pairs, kGemmThreads, PairCfg<EPI>::kSmemBytes, stream>>>(ta, tb, p);
+  gemm_bf16_pair_kernel<EPI, CONV><<<2 * pairs, kGemmThreads, PairCfg<EPI>::kSmemBytes, stream>>>(ta, tb, p);
   return cudaGetLastError() == cudaSuccess ? SSAM_OK : SSAM_ERR_CUDA;
 }
 
@@ -674,6 +691,29 @@ static int launch_gemm(const CUtensorMap& ta, const CUtensorMap& tb, const GemmP
   const int grid = tiles < num_sms(dev) ? tiles : num_sms(dev);
   gemm_bf16_tn_kernel<EPI><<<grid, kGemmThreads, kGemmSmemBytes, stream>>>(ta, tb, p);
   return cudaGetLastError() == cudaSuccess ? SSAM_OK : SSAM_ERR_CUDA;
+}
+
+// 3x3 / pad 1 convolution of a channels-last bf16 grid as an implicit GEMM on the
+// pair kernel: out fp32 [B*H*W, Cout] = im2col3x3(in) . w^T (+ bias), the im2col
+// never materialised. Needs whole image rows per CTA tile (W divides 128, H*W a
+// multiple of 128) and 64-channel K steps within one tap (Cin a multiple of 64).
+int conv3x3_nhwc(const void* in, int B, int H, int W, int Cin, const void* w, int Cout, const float* bias, void* out,
+                 cudaStream_t stream) {
+  if (in == nullptr || w == nullptr || out == nullptr || B <= 0 || H <= 0 || W <= 0 || Cin <= 0 || Cout <= 0)
+    return SSAM_ERR_INVALID;
+  if (Cin % kGemmBK != 0 || Cout % 32 != 0 || W > 128 || 128 % W != 0 || (static_cast<int64_t>(H) * W) % 128 != 0)
+    return SSAM_ERR_UNSUPPORTED;
+  const int64_t M64 = static_cast<int64_t>(B) * H * W, K64 = 9 * static_cast<int64_t>(Cin);
+  if (M64 > INT32_MAX || K64 > INT32_MAX) return SSAM_ERR_UNSUPPORTED;
+  if (!aligned16(in) || !aligned16(w) || !aligned16(out) || (bias != nullptr && !aligned16(bias))) return SSAM_ERR_ALIGN;
+  CUtensorMap ta, tb;
+  int st = make_tmap_nhwc_bf16(&ta, in, B, H, W, Cin, kGemmBK, static_cast<uint32_t>(W), static_cast<uint32_t>(128 / W));
+  if (st != SSAM_OK) return st;
+  st = make_tmap_2d_bf16(&tb, w, static_cast<uint64_t>(Cout), static_cast<uint64_t>(K64), static_cast<uint64_t>(K64),
+                         kGemmBK, 128, CU_TENSOR_MAP_SWIZZLE_128B);
+  if (st != SSAM_OK) return st;
+  GemmParams p{static_cast<int>(M64), Cout, static_cast<int>(K64), bias, out, Cout, nullptr, W, H * W};
+  return launch_gemm_pair<SSAM_EPI_F32, true>(ta, tb, p, stream);
 }
 
 int gemm_bf16(const void* A, int64_t lda, const void* B, int64_t ldb, int M, int N, int K, const float* bias,

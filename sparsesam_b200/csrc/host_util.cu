@@ -37,6 +37,27 @@ static EncodeTiledFn encode_fn() {
   return fn;
 }
 
+// 4-D map over a channels-last bf16 tensor (B, H, W, C): box {box_c, box_w, box_h, 1}
+// with the 128-byte swizzle, so a box of box_c = 64 channels lands in shared memory
+// as box_w * box_h rows of a K-major operand (the layout of a 2-D 64-column box);
+// coordinates outside the tensor read as zeros (the 3x3 convolution's padding).
+int make_tmap_nhwc_bf16(CUtensorMap* map, const void* base, int B, int H, int W, int C, uint32_t box_c, uint32_t box_w,
+                        uint32_t box_h) {
+  EncodeTiledFn fn = encode_fn();
+  if (fn == nullptr) return SSAM_ERR_CUDA;
+  if (!aligned16(base) || (static_cast<uint64_t>(C) * 2) % 16 != 0) return SSAM_ERR_ALIGN;
+  cuuint64_t dims[4] = {static_cast<cuuint64_t>(C), static_cast<cuuint64_t>(W), static_cast<cuuint64_t>(H),
+                        static_cast<cuuint64_t>(B)};
+  cuuint64_t strides[3] = {static_cast<cuuint64_t>(C) * 2, static_cast<cuuint64_t>(W) * C * 2,
+                           static_cast<cuuint64_t>(H) * W * C * 2};
+  cuuint32_t box[4] = {box_c, box_w, box_h, 1};
+  cuuint32_t estr[4] = {1, 1, 1, 1};
+  CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, const_cast<void*>(base), dims, strides, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? SSAM_OK : SSAM_ERR_CUDA;
+}
+
 int make_tmap_2d_bf16(CUtensorMap* map, const void* base, uint64_t rows, uint64_t cols, uint64_t ld, uint32_t box_cols,
                       uint32_t box_rows, CUtensorMapSwizzle swizzle) {
   EncodeTiledFn fn = encode_fn();

@@ -50,12 +50,16 @@ int num_sms(int dev);
 
 // 2-D bf16 tensor map over a row-major [rows, cols] matrix with leading
 // dimension `ld` (elements). Box = box_cols x box_rows; out-of-bounds reads fill 0.
+int make_tmap_nhwc_bf16(CUtensorMap* map, const void* base, int B, int H, int W, int C, uint32_t box_c, uint32_t box_w,
+                        uint32_t box_h);
 int make_tmap_2d_bf16(CUtensorMap* map, const void* base, uint64_t rows, uint64_t cols, uint64_t ld,
                       uint32_t box_cols, uint32_t box_rows, CUtensorMapSwizzle swizzle);
 
 int status_from_cuda(cudaError_t e);
 
 // Entry points implemented in the per-kernel translation units.
+int conv3x3_nhwc(const void* in, int B, int H, int W, int Cin, const void* w, int Cout, const float* bias, void* out,
+                 cudaStream_t stream);
 int gemm_bf16(const void* A, int64_t lda, const void* B, int64_t ldb, int M, int N, int K, const float* bias,
               int epilogue, void* out, int64_t ldo, const int32_t* out_rows, cudaStream_t stream);
 

@@ -362,6 +362,33 @@ def im2col3x3_nhwc(x: torch.Tensor, out: torch.Tensor | None = None) -> torch.Te
     return out
 
 
+def conv3x3_supported(H: int, W: int, Cin: int, Cout: int) -> bool:
+    """Whether conv3x3_nhwc takes this shape (else use im2col3x3_nhwc + gemm_bf16)."""
+    return Cin % 64 == 0 and Cout % 32 == 0 and 0 < W <= 128 and 128 % W == 0 and (H * W) % 128 == 0
+
+
+def conv3x3_nhwc(x: torch.Tensor, B: int, H: int, W: int, w: torch.Tensor,
+                 bias: torch.Tensor | None = None, k_split: int = 1) -> torch.Tensor:
+    """3x3 / pad 1 convolution of channels-last bf16 x (B*H*W, Cin) with w bf16
+    (Cout, 9*Cin) in (ky, kx, cin) order -> fp32 (B*H*W, Cout), as an implicit GEMM
+    (equal, bit for bit, to gemm_bf16(im2col3x3_nhwc(x), w, bias, SSAM_EPI_F32)).
+    `k_split` as in gemm_bf16 (the channels are a k_split-term split operand)."""
+    _check_cuda(x, w, bias)
+    x2 = x.reshape(-1, x.shape[-1])
+    if x2.dtype != torch.bfloat16 or not x2.is_contiguous() or x2.shape[0] != B * H * W:
+        raise ValueError("x must be contiguous bf16 (B*H*W, Cin)")
+    Cin = x2.shape[1]
+    if w.dtype != torch.bfloat16 or not w.is_contiguous() or w.shape[1] != 9 * Cin:
+        raise ValueError("w must be contiguous bf16 (Cout, 9*Cin)")
+    Cout = w.shape[0]
+    out = torch.empty(B * H * W, Cout, dtype=torch.float32, device=x.device)
+    t0 = KernelTimer.begin()
+    _lib.call("ssam_conv3x3_nhwc", x2.data_ptr(), B, H, W, Cin, w.data_ptr(), Cout, _ptr(bias), out.data_ptr(),
+              _stream(x))
+    KernelTimer.end(t0, "gemm", 2.0 * B * H * W * Cout * 9 * Cin / k_split)
+    return out
+
+
 def nhwc_to_nchw(x: torch.Tensor, B: int, H: int, W: int, C: int, out: torch.Tensor | None = None) -> torch.Tensor:
     _check_cuda(x, out)
     if out is None:

@@ -371,8 +371,11 @@ def encoder_forward(enc, img: torch.Tensor):
     # NCHW features
     y = ops.gemm_bf16(ops.split_bf16x3(x), w.neck0_w, None, epilogue=ops.SSAM_EPI_F32, k_split=3)
     ya3 = ops.layernorm_rows(y, w.ln_a_w, w.ln_a_b, w.eps_a, out_bf16=False, split3=True)
-    cols3 = ops.im2col3x3_nhwc(ya3.view(B, gh, gw, -1))
-    z = ops.gemm_bf16(cols3, w.neck2_w, None, epilogue=ops.SSAM_EPI_F32, k_split=3)
+    if ops.conv3x3_supported(gh, gw, ya3.shape[1], w.neck2_w.shape[0]):
+        z = ops.conv3x3_nhwc(ya3, B, gh, gw, w.neck2_w, k_split=3)   # implicit GEMM: no im2col buffer
+    else:
+        cols3 = ops.im2col3x3_nhwc(ya3.view(B, gh, gw, -1))
+        z = ops.gemm_bf16(cols3, w.neck2_w, None, epilogue=ops.SSAM_EPI_F32, k_split=3)
     feats = ops.layernorm_nchw(z, B, gh, gw, w.ln_b_w, w.ln_b_b, w.eps_b)
     return feats, interm
 

@@ -189,3 +189,31 @@ def test_layernorm_rows_copy_out(cuda_device, rows, C):
     out = ops.layernorm_rows(x, w, b, 1e-6, out_bf16=True, copy_out=snap)
     assert torch.equal(out, ref)
     assert torch.equal(snap, x)
+
+
+@pytest.mark.parametrize("B,H,W,Cin,Cout", [(2, 64, 64, 768, 256), (1, 8, 32, 128, 64), (3, 16, 16, 64, 32)])
+def test_conv3x3_implicit_matches_im2col(cuda_device, B, H, W, Cin, Cout):
+    """The implicit-GEMM 3x3 convolution (4-D TMA boxes of the channels-last input,
+    zeros outside the image) equals im2col + GEMM bit for bit, and the fp32
+    convolution to bf16-operand accuracy; unsupported shapes are refused."""
+    g = torch.Generator().manual_seed(9)
+    x = torch.randn(B * H * W, Cin, generator=g).to(torch.bfloat16).to(cuda_device)
+    w = (torch.randn(Cout, 9 * Cin, generator=g) * 0.05).to(torch.bfloat16).to(cuda_device)
+    b = torch.randn(Cout, generator=g).to(cuda_device)
+    assert ops.conv3x3_supported(H, W, Cin, Cout)
+    got = ops.conv3x3_nhwc(x, B, H, W, w, b)
+    ref = ops.gemm_bf16(ops.im2col3x3_nhwc(x.view(B, H, W, Cin)), w, b, epilogue=ops.SSAM_EPI_F32)
+    assert ops.device_error() == 0
+    assert torch.equal(got, ref)
+    conv = torch.nn.functional.conv2d(x.float().view(B, H, W, Cin).permute(0, 3, 1, 2),
+                                      w.float().view(Cout, 3, 3, Cin).permute(0, 3, 1, 2), b, padding=1)
+    conv = conv.permute(0, 2, 3, 1).reshape(-1, Cout)
+    assert (got - conv).abs().max().item() <= 1e-3 * conv.abs().max().item() + 1e-3
+
+
+def test_conv3x3_implicit_refuses_unsupported(cuda_device):
+    x = torch.zeros(1 * 9 * 9, 64, dtype=torch.bfloat16, device=cuda_device)
+    w = torch.zeros(32, 9 * 64, dtype=torch.bfloat16, device=cuda_device)
+    assert not ops.conv3x3_supported(9, 9, 64, 32)
+    with pytest.raises(RuntimeError):
+        ops.conv3x3_nhwc(x, 1, 9, 9, w)
