@@ -245,6 +245,14 @@ int ssam_broadcast_rows(const float* pos, int B, int T, int C, float* x, void* s
  * permuted to (Cout, 3, 3, Cin). */
 int ssam_im2col3x3_nhwc(const void* in, int B, int H, int W, int C, void* out, void* stream);
 
+/* out fp32 [M, N] = A . B^T + bias + addend[(r % addend_rows), :] for every row r
+ * (addend fp32 [addend_rows, N]; bias may be NULL): the SAM stem's patch
+ * embedding with its positional embedding (addend_rows = tokens per image), x
+ * written once. Operands as in ssam_gemm_bf16; M >= 256 (SSAM_ERR_UNSUPPORTED
+ * below), N a multiple of 32. */
+int ssam_gemm_bf16_addend(const void* A, int64_t lda, const void* B, int64_t ldb, int M, int N, int K,
+                          const float* bias, const float* addend, int addend_rows, float* out, void* stream);
+
 /* 3x3 / pad 1 convolution of a channels-last bf16 grid in (B, H, W, Cin) as an
  * implicit GEMM on the tensor cores (the im2col is never written): out fp32
  * [B*H*W, Cout] = im2col3x3(in) . w^T (+ bias, which may be NULL), w bf16

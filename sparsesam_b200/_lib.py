@@ -50,6 +50,8 @@ SIGNATURES: dict[str, tuple] = {
     "ssam_im2col3x3_nhwc": (c_int, [c_ptr, c_int, c_int, c_int, c_int, c_ptr, c_ptr]),
     "ssam_nhwc_to_nchw": (c_int, [c_ptr, c_int, c_int, c_int, c_ptr, c_ptr]),
     "ssam_conv3x3_nhwc": (c_int, [c_ptr, c_int, c_int, c_int, c_int, c_ptr, c_int, c_ptr, c_ptr, c_ptr]),
+    "ssam_gemm_bf16_addend": (c_int, [c_ptr, c_i64, c_ptr, c_i64, c_int, c_int, c_int, c_ptr, c_ptr, c_int, c_ptr,
+                                      c_ptr]),
     "ssam_layernorm_rows": (c_int, [c_ptr, c_int, c_int, c_ptr, c_ptr, c_f32, c_ptr, c_int, c_ptr]),
     "ssam_layernorm_nchw": (c_int, [c_ptr, c_int, c_int, c_int, c_ptr, c_ptr, c_f32, c_ptr, c_ptr]),
     "ssam_layernorm_rows_copy": (c_int, [c_ptr, c_int, c_int, c_ptr, c_ptr, c_f32, c_ptr, c_ptr, c_ptr]),
@@ -83,7 +85,7 @@ KERNELS_PER_CALL = {
     "ssam_check_wait_timeout": 1, "ssam_hilbert_order": 1,
     "ssam_layernorm_gather": 1, "ssam_window_rows": 1, "ssam_gemm_bf16": 1, "ssam_rc_mlp_fwd": 3,
     "ssam_patch_im2col": 1, "ssam_broadcast_rows": 1, "ssam_im2col3x3_nhwc": 1, "ssam_nhwc_to_nchw": 1,
-    "ssam_conv3x3_nhwc": 1,
+    "ssam_conv3x3_nhwc": 1, "ssam_gemm_bf16_addend": 1,
     "ssam_layernorm_rows": 1, "ssam_layernorm_nchw": 1, "ssam_layernorm_rows_copy": 1, "ssam_split_bf16x2": 1,
     "ssam_rc_mlp_fwd_noalloc": 3,
     "ssam_split_bf16x3": 1, "ssam_patch_im2col_split3": 1, "ssam_window_of_raster": 1, "ssam_fill_pad_rows": 1,

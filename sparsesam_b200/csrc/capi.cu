@@ -146,6 +146,12 @@ int ssam_im2col3x3_nhwc(const void* in, int B, int H, int W, int C, void* out, v
   return ssam::im2col3x3_nhwc(in, B, H, W, C, out, static_cast<cudaStream_t>(stream));
 }
 
+int ssam_gemm_bf16_addend(const void* A, int64_t lda, const void* B, int64_t ldb, int M, int N, int K,
+                          const float* bias, const float* addend, int addend_rows, float* out, void* stream) {
+  return ssam::gemm_bf16_addend(A, lda, B, ldb, M, N, K, bias, addend, addend_rows, out,
+                                static_cast<cudaStream_t>(stream));
+}
+
 int ssam_conv3x3_nhwc(const void* in, int B, int H, int W, int Cin, const void* w, int Cout, const float* bias,
                       void* out, void* stream) {
   return ssam::conv3x3_nhwc(in, B, H, W, Cin, w, Cout, bias, out, static_cast<cudaStream_t>(stream));

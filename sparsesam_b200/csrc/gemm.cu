@@ -42,6 +42,9 @@ struct GemmParams {
   // implicit 3x3 convolution (pair kernel, CONV): A is a channels-last (B, H, W, Cin)
   // tensor map, K = 9 Cin in (ky, kx, cin) order, rows are the B*H*W output pixels
   int conv_w, conv_hw;
+  // SSAM_EPI_F32: addend[(r % addend_rows) * N + n] is added to row r (may be null)
+  const float* addend;
+  int addend_rows;
 };
 
 template <int EPI>
@@ -212,6 +215,22 @@ __device__ __forceinline__ void gemm_epilogue_chunk_bulk(const GemmParams& p, in
   if constexpr (EPI == SSAM_EPI_GELU_BF16) {
 #pragma unroll
     for (int i = 0; i < 32; ++i) v[i] = gelu_exact(v[i]);
+  }
+  if constexpr (EPI == SSAM_EPI_F32) {
+    if (p.addend != nullptr && row < p.M) {
+      const float4* a4 = reinterpret_cast<const float4*>(p.addend + static_cast<int64_t>(row % p.addend_rows) * p.N +
+                                                         col0);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const float4 t = __ldg(a4 + i);
+        const float2 lo = add2(make_float2(v[4 * i + 0], v[4 * i + 1]), make_float2(t.x, t.y));
+        const float2 hi = add2(make_float2(v[4 * i + 2], v[4 * i + 3]), make_float2(t.z, t.w));
+        v[4 * i + 0] = lo.x;
+        v[4 * i + 1] = lo.y;
+        v[4 * i + 2] = hi.x;
+        v[4 * i + 3] = hi.y;
+      }
+    }
   }
   const int orow = row < p.M ? (p.out_rows != nullptr ? __ldg(p.out_rows + row) : row) : -1;
   asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
@@ -712,8 +731,29 @@ int conv3x3_nhwc(const void* in, int B, int H, int W, int Cin, const void* w, in
   st = make_tmap_2d_bf16(&tb, w, static_cast<uint64_t>(Cout), static_cast<uint64_t>(K64), static_cast<uint64_t>(K64),
                          kGemmBK, 128, CU_TENSOR_MAP_SWIZZLE_128B);
   if (st != SSAM_OK) return st;
-  GemmParams p{static_cast<int>(M64), Cout, static_cast<int>(K64), bias, out, Cout, nullptr, W, H * W};
+  GemmParams p{static_cast<int>(M64), Cout, static_cast<int>(K64), bias, out, Cout, nullptr, W, H * W, nullptr, 0};
   return launch_gemm_pair<SSAM_EPI_F32, true>(ta, tb, p, stream);
+}
+
+// out fp32 [M, N] = A . B^T + bias + addend[r % addend_rows] (the patch embedding
+// plus its positional embedding, written once): the pair kernel's fp32 epilogue.
+int gemm_bf16_addend(const void* A, int64_t lda, const void* B, int64_t ldb, int M, int N, int K, const float* bias,
+                     const float* addend, int addend_rows, float* out, cudaStream_t stream) {
+  if (A == nullptr || B == nullptr || out == nullptr || addend == nullptr || addend_rows <= 0) return SSAM_ERR_INVALID;
+  if (M <= 0 || N <= 0 || K <= 0 || lda < K || ldb < K) return SSAM_ERR_INVALID;
+  if (N % 32 != 0 || K % 8 != 0 || M < kPairBM) return SSAM_ERR_UNSUPPORTED;
+  if ((lda % 8) || (ldb % 8) || !aligned16(A) || !aligned16(B) || !aligned16(out) || !aligned16(addend) ||
+      (bias != nullptr && !aligned16(bias)))
+    return SSAM_ERR_ALIGN;
+  CUtensorMap ta, tb;
+  int st = make_tmap_2d_bf16(&ta, A, static_cast<uint64_t>(M), static_cast<uint64_t>(K), static_cast<uint64_t>(lda),
+                             kGemmBK, 128, CU_TENSOR_MAP_SWIZZLE_128B);
+  if (st != SSAM_OK) return st;
+  st = make_tmap_2d_bf16(&tb, B, static_cast<uint64_t>(N), static_cast<uint64_t>(K), static_cast<uint64_t>(ldb), kGemmBK,
+                         128, CU_TENSOR_MAP_SWIZZLE_128B);
+  if (st != SSAM_OK) return st;
+  GemmParams p{M, N, K, bias, out, N, nullptr, 0, 0, addend, addend_rows};
+  return launch_gemm_pair<SSAM_EPI_F32>(ta, tb, p, stream);
 }
 
 int gemm_bf16(const void* A, int64_t lda, const void* B, int64_t ldb, int M, int N, int K, const float* bias,
@@ -739,7 +779,7 @@ int gemm_bf16(const void* A, int64_t lda, const void* B, int64_t ldb, int M, int
   st = make_tmap_2d_bf16(&tb, B, static_cast<uint64_t>(N), static_cast<uint64_t>(K), static_cast<uint64_t>(ldb), kGemmBK,
                          kGemmBN, CU_TENSOR_MAP_SWIZZLE_128B);
   if (st != SSAM_OK) return st;
-  GemmParams p{M, N, K, bias, out, ldo, out_rows};
+  GemmParams p{M, N, K, bias, out, ldo, out_rows, 0, 0, nullptr, 0};
   const int pair_tiles = ((M + kPairBM - 1) / kPairBM) * ((N + kGemmBN - 1) / kGemmBN);
   if (M >= kPairBM && pair_tiles >= 64) {
     // 2-SM kernel: 128-row boxes per CTA for both operands

@@ -362,6 +362,27 @@ def im2col3x3_nhwc(x: torch.Tensor, out: torch.Tensor | None = None) -> torch.Te
     return out
 
 
+def gemm_bf16_addend(a: torch.Tensor, b: torch.Tensor, bias: torch.Tensor | None, addend: torch.Tensor,
+                     k_split: int = 1) -> torch.Tensor:
+    """fp32 (M, N) = a @ b.T + bias + addend[r % addend.shape[0]] for every row r
+    (addend fp32 (rows, N), e.g. the positional embedding of each image's tokens)."""
+    _check_cuda(a, b, bias, addend)
+    if a.dtype != torch.bfloat16 or b.dtype != torch.bfloat16:
+        raise TypeError("gemm_bf16_addend takes bf16 operands")
+    M, K = a.shape
+    N = b.shape[0]
+    if b.shape[1] != K:
+        raise ValueError(f"inner dimensions differ: {K} vs {b.shape[1]}")
+    if addend.dtype != torch.float32 or not addend.is_contiguous() or addend.dim() != 2 or addend.shape[1] != N:
+        raise ValueError("addend must be contiguous fp32 (rows, N)")
+    out = torch.empty(M, N, device=a.device, dtype=torch.float32)
+    t0 = KernelTimer.begin()
+    _lib.call("ssam_gemm_bf16_addend", a.data_ptr(), _rowmajor(a, "a"), b.data_ptr(), _rowmajor(b, "b"), M, N, K,
+              _ptr(bias), addend.data_ptr(), addend.shape[0], out.data_ptr(), _stream(a))
+    KernelTimer.end(t0, "gemm", 2.0 * M * N * K / k_split)
+    return out
+
+
 def conv3x3_supported(H: int, W: int, Cin: int, Cout: int) -> bool:
     """Whether conv3x3_nhwc takes this shape (else use im2col3x3_nhwc + gemm_bf16)."""
     return Cin % 64 == 0 and Cout % 32 == 0 and 0 < W <= 128 and 128 % W == 0 and (H * W) % 128 == 0

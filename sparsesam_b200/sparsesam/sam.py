@@ -347,11 +347,15 @@ def encoder_forward(enc, img: torch.Tensor):
     C = conv.weight.shape[0]
     T = gh * gw
     cols = ops.patch_im2col_split3(img.to(torch.float32), p)
-    x = torch.empty(B * T, C, dtype=torch.float32, device=img.device)
-    if w.pos is not None:
+    if w.pos is not None and B * T >= 256:
+        # x = patches . W + b + pos, the positional embedding added in the GEMM epilogue
+        x = ops.gemm_bf16_addend(cols, w.patch_w, w.patch_b, w.pos.view(T, C), k_split=3)
+    elif w.pos is not None:
+        x = torch.empty(B * T, C, dtype=torch.float32, device=img.device)
         ops.broadcast_rows(w.pos, B, x)
         ops.gemm_bf16(cols, w.patch_w, w.patch_b, epilogue=ops.SSAM_EPI_ADD_F32, out=x, k_split=3)
     else:
+        x = torch.empty(B * T, C, dtype=torch.float32, device=img.device)
         ops.gemm_bf16(cols, w.patch_w, w.patch_b, epilogue=ops.SSAM_EPI_F32, out=x, k_split=3)
     interm = []
     n_blocks = len(enc.blocks)

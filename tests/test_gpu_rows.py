@@ -217,3 +217,21 @@ def test_conv3x3_implicit_refuses_unsupported(cuda_device):
     assert not ops.conv3x3_supported(9, 9, 64, 32)
     with pytest.raises(RuntimeError):
         ops.conv3x3_nhwc(x, 1, 9, 9, w)
+
+
+@pytest.mark.parametrize("B,T,K,N", [(2, 4096, 2304, 1280), (16, 1024, 192, 512)])   # both GEMMs on the 2-SM kernel
+def test_gemm_addend_is_broadcast_then_add(cuda_device, B, T, K, N):
+    """The stem's GEMM with the positional embedding added in its epilogue equals
+    the broadcast of the embedding followed by the accumulating GEMM, bit for bit
+    (fp32 addition commutes)."""
+    g = torch.Generator().manual_seed(13)
+    a = torch.randn(B * T, K, generator=g).to(torch.bfloat16).to(cuda_device)
+    w = (torch.randn(N, K, generator=g) * 0.05).to(torch.bfloat16).to(cuda_device)
+    bias = torch.randn(N, generator=g).to(cuda_device)
+    pos = torch.randn(T, N, generator=g).to(cuda_device)
+    got = ops.gemm_bf16_addend(a, w, bias, pos)
+    ref = torch.empty(B * T, N, device=cuda_device)
+    ops.broadcast_rows(pos, B, ref)
+    ops.gemm_bf16(a, w, bias, epilogue=ops.SSAM_EPI_ADD_F32, out=ref)
+    assert ops.device_error() == 0
+    assert torch.equal(got, ref)
