@@ -3,6 +3,7 @@
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
     (N > 1: launched by torchrun, one rank per GPU)
     python bench.py --mode attn | mlp   (BASELINE configs 1 / 2, one GPU, one JSON line per case)
+    python bench.py --mode predictor    (the SAM-HQ evaluation step: encoder + box-prompted HQ decode)
 
 A step is one SparseSAM-patched encoder forward over one batch of synthetic
 1024x1024 images (batch 64 per GPU; images are independent shards, no collective
@@ -411,7 +412,7 @@ def _event_ms(fn, steps: int) -> float:
 def _micro_common(args, dev):
     from sparsesam_b200 import ops
     if int(os.environ.get("WORLD_SIZE", "1")) > 1:
-        raise SystemExit("--mode attn / mlp are single-GPU microbenchmarks")
+        raise SystemExit("--mode attn / mlp / predictor are single-GPU benchmarks")
     return ops, _peaks()
 
 
@@ -558,6 +559,95 @@ def run_mlp_micro(args) -> None:
             **common}), flush=True)
 
 
+def run_predictor(args) -> None:
+    """The HQ-44K evaluation step around the encoder (tasks/sam_hq44k/eval_hq44k.py:87-129)
+    as a throughput benchmark: a step is preprocess -> patched encoder -> one
+    box-prompted HQ decode per image (hq_token_only, the whole batch in one decoder
+    pass) -> masks at 1024^2. Synthetic images with one ellipse each (the dataset is
+    not available) and seeded random weights; the IoU printed is a pipeline check,
+    not a quality figure. value: images in HBM, device-timed; e2e: uint8 images from
+    pinned host memory in and boolean masks out inside every step."""
+    import torch
+    from sparsesam_b200 import _lib, hq, registry
+    from sparsesam_b200.sparsesam.sam import apply_patch
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    ops, peaks = _micro_common(args, dev)
+    arch, batch, ratio = args.arch, args.batch, args.ratio
+    dec_dt = {"fp32": torch.float32, "bf16": torch.bfloat16, "fp16": torch.float16}[args.decoder_dtype]
+    sam = hq.build_sam_hq(arch, device=dev, decoder_dtype=dec_dt)
+    if ratio < 1.0:
+        registry.apply_sam(sam.image_encoder, "sparsesam", ratio=ratio)
+    else:
+        apply_patch(sam.image_encoder, ratio=1.0)
+    images, labels, boxes = hq.synthetic_box_batch(batch, seed=0, img_size=IMG)
+    img_host = images.to(torch.uint8).pin_memory()
+    box_host = boxes.pin_memory()
+    img_dev, box_dev = img_host.to(dev), box_host.to(dev)
+    mask_host = torch.empty(batch, 1, IMG, IMG, dtype=torch.bool).pin_memory()
+    pred = hq.SamPredictor(sam)
+
+    def encode(x_u8):
+        x = sam.preprocess(x_u8)
+        pred.features, pred.interm_features = sam.image_encoder(x)
+        pred.original_size = pred.input_size = (IMG, IMG)
+        pred.is_image_set = True
+
+    def decode(bx):
+        return pred.predict_torch(None, None, boxes=bx, hq_token_only=True)[0]
+
+    def step():
+        encode(img_dev)
+        return decode(box_dev)
+
+    def step_e2e():
+        x = img_host.to(dev, non_blocking=True)
+        bx = box_host.to(dev, non_blocking=True)
+        encode(x)
+        mask_host.copy_(decode(bx), non_blocking=True)
+        torch.cuda.current_stream().synchronize()
+
+    with torch.no_grad():
+        for _ in range(args.warmup):
+            step()
+        torch.cuda.synchronize()
+        clocks = ClockSampler(0)
+        clocks.start()
+        launches0 = _lib.launch_count
+        ms = _event_ms(step, args.steps)
+        launches = (_lib.launch_count - launches0) // max(1, args.steps)
+        clk = clocks.stop()
+        enc_ms = _event_ms(lambda: encode(img_dev), args.steps)
+        dec_ms = _event_ms(lambda: decode(box_dev), args.steps)
+        step_e2e()
+        ms_e2e = _event_ms(step_e2e, args.steps)
+        masks = step()
+        iou = hq.compute_iou(masks, labels.to(dev)).item()
+        biou = hq.compute_boundary_iou(masks[:4], labels[:4].to(dev)).item()
+    if ops.device_error() != 0:
+        raise RuntimeError("device error flag raised")
+    flops_img = encoder_flops(arch, ratio)
+    print(json.dumps({
+        "metric": f"SAM-HQ predictor images/sec @1024², {arch}, d={ratio} (encoder + one box-prompted HQ decode "
+                  "per image)",
+        "value": batch / ms * 1e3, "unit": "images/s", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": ms, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": f"bf16 encoder, {args.decoder_dtype} decoder", "data": "synthetic",
+        "config": {"workload": f"SAM-HQ {arch} predictor: preprocess, SparseSAM encoder, HQ mask decoder with one "
+                               "box per image in one decoder pass, masks upsampled to 1024x1024 "
+                               "(eval_hq44k.py:87-129 step)",
+                   "per_gpu_batch": batch, "ratio": ratio,
+                   "l2": "inputs larger than L2: {:.0f} MB of images per step".format(img_host.numel() / 1e6)},
+        "e2e": {"value": batch / ms_e2e * 1e3, "unit": "images/s", "h2d_bytes_per_step": img_host.numel() +
+                box_host.numel() * 4, "d2h_bytes_per_step": mask_host.numel()},
+        "legs_ms": {"encoder": enc_ms, "decode (prompt encoder, HQ decoder, mask upsampling)": dec_ms},
+        "encoder_tflops": flops_img * batch / enc_ms / 1e9,
+        "gpu_launches": launches,
+        "iou_check": {"iou": iou, "boundary_iou_first4": biou,
+                      "note": "random weights: a pipeline check, not segmentation quality"},
+        "clocks": clk}), flush=True)
+
+
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -568,8 +658,11 @@ def main() -> None:
     ap.add_argument("--ratio", type=float, default=RATIO, help="SparseSAM density (1.0: dense control)")
     ap.add_argument("--arch", choices=("vit_h", "vit_l", "vit_b"), default=ARCH)
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--mode", choices=("encoder", "attn", "mlp"), default="encoder",
-                    help="encoder: the headline metric; attn / mlp: BASELINE configs 1 / 2 microbenchmarks")
+    ap.add_argument("--decoder-dtype", choices=("fp16", "bf16", "fp32"), default="fp16",
+                    help="predictor mode: the prompt encoder / HQ decoder dtype (the reference runs fp16)")
+    ap.add_argument("--mode", choices=("encoder", "attn", "mlp", "predictor"), default="encoder",
+                    help="encoder: the headline metric; attn / mlp: BASELINE configs 1 / 2 microbenchmarks; "
+                         "predictor: the SAM-HQ evaluation step (encoder + box-prompted HQ decode)")
     args = ap.parse_args()
     if args.warmup < 3 and args.impl == "ours":
         args.warmup = 3
@@ -579,6 +672,8 @@ def main() -> None:
         run_attn_micro(args)
     elif args.mode == "mlp":
         run_mlp_micro(args)
+    elif args.mode == "predictor":
+        run_predictor(args)
     else:
         run_ours(args)
 

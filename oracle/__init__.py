@@ -11,6 +11,9 @@ fallback.
                (flash_attn.py:1519-1551 semantics)                  [torch fp32]
   encoder.py   SparseSAM-patched SAM ViT encoder forward
                (sam.py:168-290 + the SAM host model)                 [torch fp32]
+  decoder.py   SAM-HQ box-prompted decode and mask resizing, the
+               checker of the predictor around the encoder
+               (eval_hq44k.py:87-129; SAM-HQ itself is unvendored)  [torch fp64]
 
 Pinned against golden vectors produced by running the reference's own
 algos/sparsesam code on CPU (tests/golden/make_golden.py).
