@@ -280,6 +280,16 @@ int ssam_layernorm_rows(const float* x, int n_rows, int C, const float* w, const
 int ssam_layernorm_nchw(const float* x, int B, int HW, int C, const float* w, const float* b, float eps,
                         float* out, void* stream);
 
+/* Channel LayerNorm (biased variance, eps) of half-precision channels-last rows
+ * [rows, C], with an exact GELU after it when gelu = 1: the SAM-HQ mask decoder's
+ * LayerNorm2d -> GELU pairs on its NHWC maps (replaces the torch LayerNorm2d and
+ * nn.GELU that SAM-HQ's MaskDecoderHQ applies after its transposed convolutions,
+ * called from tasks/sam_hq44k/eval_hq44k.py:87-129 through predict_torch).
+ * dtype 0: fp16, 1: bf16 (x, w, b and out alike). C in {32, 64, 128, 256}
+ * (SSAM_ERR_UNSUPPORTED otherwise); x, w, b, out 16-byte aligned and out not overlapping x. */
+int ssam_layernorm_gelu_half(const void* x, int64_t rows, int C, const void* w, const void* b, float eps, int gelu,
+                             int dtype, void* out, void* stream);
+
 /* Row LayerNorm fp32 -> bf16 that also stores its input rows unchanged to
  * copy (fp32 [n_rows, C], 16-byte aligned). The encoder keeps its intermediate
  * embedding after a global-attention block (the token grid the SAM-HQ encoder

@@ -54,6 +54,7 @@ SIGNATURES: dict[str, tuple] = {
                                       c_ptr]),
     "ssam_layernorm_rows": (c_int, [c_ptr, c_int, c_int, c_ptr, c_ptr, c_f32, c_ptr, c_int, c_ptr]),
     "ssam_layernorm_nchw": (c_int, [c_ptr, c_int, c_int, c_int, c_ptr, c_ptr, c_f32, c_ptr, c_ptr]),
+    "ssam_layernorm_gelu_half": (c_int, [c_ptr, c_i64, c_int, c_ptr, c_ptr, c_f32, c_int, c_int, c_ptr, c_ptr]),
     "ssam_layernorm_rows_copy": (c_int, [c_ptr, c_int, c_int, c_ptr, c_ptr, c_f32, c_ptr, c_ptr, c_ptr]),
     "ssam_split_bf16x2": (c_int, [c_ptr, c_int, c_int, c_ptr, c_ptr]),
     "ssam_split_bf16x3": (c_int, [c_ptr, c_int, c_int, c_ptr, c_ptr]),
@@ -87,6 +88,7 @@ KERNELS_PER_CALL = {
     "ssam_patch_im2col": 1, "ssam_broadcast_rows": 1, "ssam_im2col3x3_nhwc": 1, "ssam_nhwc_to_nchw": 1,
     "ssam_conv3x3_nhwc": 1, "ssam_gemm_bf16_addend": 1,
     "ssam_layernorm_rows": 1, "ssam_layernorm_nchw": 1, "ssam_layernorm_rows_copy": 1, "ssam_split_bf16x2": 1,
+    "ssam_layernorm_gelu_half": 1,
     "ssam_rc_mlp_fwd_noalloc": 3,
     "ssam_split_bf16x3": 1, "ssam_patch_im2col_split3": 1, "ssam_window_of_raster": 1, "ssam_fill_pad_rows": 1,
     "ssam_zstride_keep": 1,

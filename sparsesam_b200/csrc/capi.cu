@@ -171,6 +171,11 @@ int ssam_layernorm_nchw(const float* x, int B, int HW, int C, const float* w, co
   return ssam::layernorm_nchw(x, B, HW, C, w, b, eps, out, static_cast<cudaStream_t>(stream));
 }
 
+int ssam_layernorm_gelu_half(const void* x, int64_t rows, int C, const void* w, const void* b, float eps, int gelu,
+                             int dtype, void* out, void* stream) {
+  return ssam::layernorm_half(x, rows, C, w, b, eps, gelu, dtype, out, static_cast<cudaStream_t>(stream));
+}
+
 int ssam_layernorm_rows_copy(const float* x, int n_rows, int C, const float* w, const float* b, float eps,
                              void* out_bf16, float* copy, void* stream) {
   return ssam::layernorm_rows_copy(x, n_rows, C, w, b, eps, out_bf16, copy, static_cast<cudaStream_t>(stream));

@@ -60,6 +60,8 @@ int status_from_cuda(cudaError_t e);
 // Entry points implemented in the per-kernel translation units.
 int conv3x3_nhwc(const void* in, int B, int H, int W, int Cin, const void* w, int Cout, const float* bias, void* out,
                  cudaStream_t stream);
+int layernorm_half(const void* x, int64_t rows, int C, const void* w, const void* b, float eps, int gelu, int dtype,
+                   void* out, cudaStream_t stream);
 int gemm_bf16_addend(const void* A, int64_t lda, const void* B, int64_t ldb, int M, int N, int K, const float* bias,
                      const float* addend, int addend_rows, float* out, cudaStream_t stream);
 int gemm_bf16(const void* A, int64_t lda, const void* B, int64_t ldb, int M, int N, int K, const float* bias,

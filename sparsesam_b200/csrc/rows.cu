@@ -233,6 +233,133 @@ int layernorm_nchw(const float* x, int B, int HW, int C, const float* w, const f
   return status_from_cuda(cudaGetLastError());
 }
 
+// ---------------------------------------------------------------------------
+// Channel LayerNorm (eps, biased variance) with an optional exact GELU after it,
+// on half-precision channels-last rows (fp16 or bf16 in, weights and out): the
+// SAM-HQ mask decoder's LayerNorm2d -> GELU pairs on its NHWC maps of 32 .. 256
+// channels (millions of short rows, where a row per warp would leave most lanes
+// idle). C / 8 threads per row, one 16-byte vector of 8 channels each; the row's
+// sums are shuffle reductions inside its lane group, the mean first, then the
+// mean of squared deviations from the registers. A grid-stride loop over row
+// groups keeps every lane of a warp in the loop (rows past the end load zeros
+// and store nothing), so the full-mask shuffles are always well defined.
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ void unpack8(uint4 r, float (&v)[8], const __half*) {
+  const __half2* h = reinterpret_cast<const __half2*>(&r);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float2 f = __half22float2(h[i]);
+    v[2 * i] = f.x;
+    v[2 * i + 1] = f.y;
+  }
+}
+__device__ __forceinline__ void unpack8(uint4 r, float (&v)[8], const __nv_bfloat16*) {
+  const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&r);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float2 f = __bfloat1622float2(h[i]);
+    v[2 * i] = f.x;
+    v[2 * i + 1] = f.y;
+  }
+}
+__device__ __forceinline__ uint4 pack8(const float (&v)[8], const __half*) {
+  uint4 r;
+  __half2* h = reinterpret_cast<__half2*>(&r);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) h[i] = __floats2half2_rn(v[2 * i], v[2 * i + 1]);
+  return r;
+}
+__device__ __forceinline__ uint4 pack8(const float (&v)[8], const __nv_bfloat16*) {
+  uint4 r;
+  __nv_bfloat162* h = reinterpret_cast<__nv_bfloat162*>(&r);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) h[i] = __floats2bfloat162_rn(v[2 * i], v[2 * i + 1]);
+  return r;
+}
+
+constexpr int kLnHalfThreads = 256;
+template <typename T, int C, bool GELU>
+__global__ void __launch_bounds__(kLnHalfThreads) layernorm_half_kernel(const T* __restrict__ x, int64_t rows,
+                                                                         const T* __restrict__ w,
+                                                                         const T* __restrict__ b, float eps,
+                                                                         T* __restrict__ out) {
+  constexpr int kTpr = C / 8;                    // threads per row
+  constexpr int kRows = kLnHalfThreads / kTpr;   // rows per CTA per step
+  const int sub = threadIdx.x % kTpr;
+  float wv[8], bv[8];
+  unpack8(__ldg(reinterpret_cast<const uint4*>(w) + sub), wv, w);
+  unpack8(__ldg(reinterpret_cast<const uint4*>(b) + sub), bv, b);
+  for (int64_t r0 = static_cast<int64_t>(blockIdx.x) * kRows; r0 < rows;
+       r0 += static_cast<int64_t>(gridDim.x) * kRows) {
+    const int64_t row = r0 + threadIdx.x / kTpr;
+    const bool valid = row < rows;
+    float v[8];
+    const uint4 raw = valid ? __ldg(reinterpret_cast<const uint4*>(x + row * C) + sub) : make_uint4(0, 0, 0, 0);
+    unpack8(raw, v, x);
+    float s = ((v[0] + v[1]) + (v[2] + v[3])) + ((v[4] + v[5]) + (v[6] + v[7]));
+#pragma unroll
+    for (int o = kTpr / 2; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+    const float mean = s / C;
+    float q = 0.f;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      v[i] -= mean;
+      q = fmaf(v[i], v[i], q);
+    }
+#pragma unroll
+    for (int o = kTpr / 2; o > 0; o >>= 1) q += __shfl_xor_sync(0xffffffffu, q, o);
+    const float rstd = rsqrtf(q / C + eps);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const float y = fmaf(v[i] * rstd, wv[i], bv[i]);
+      v[i] = GELU ? gelu_exact(y) : y;
+    }
+    if (valid) reinterpret_cast<uint4*>(out + row * C)[sub] = pack8(v, out);
+  }
+}
+
+template <typename T, int C>
+static int launch_layernorm_half(const void* x, int64_t rows, const void* w, const void* b, float eps, int gelu,
+                                 void* out, cudaStream_t stream) {
+  constexpr int kRows = kLnHalfThreads / (C / 8);
+  const int dev = current_device();
+  const int64_t want = (rows + kRows - 1) / kRows;
+  const int64_t cap = static_cast<int64_t>(dev >= 0 ? num_sms(dev) : 148) * 8;  // 8 resident CTAs per SM
+  const int grid = static_cast<int>(want < cap ? want : cap);
+  const T* xp = static_cast<const T*>(x);
+  const T* wp = static_cast<const T*>(w);
+  const T* bp = static_cast<const T*>(b);
+  T* op = static_cast<T*>(out);
+  if (gelu)
+    layernorm_half_kernel<T, C, true><<<grid, kLnHalfThreads, 0, stream>>>(xp, rows, wp, bp, eps, op);
+  else
+    layernorm_half_kernel<T, C, false><<<grid, kLnHalfThreads, 0, stream>>>(xp, rows, wp, bp, eps, op);
+  return status_from_cuda(cudaGetLastError());
+}
+
+template <typename T>
+static int dispatch_layernorm_half(const void* x, int64_t rows, int C, const void* w, const void* b, float eps,
+                                   int gelu, void* out, cudaStream_t stream) {
+  switch (C) {
+    case 32: return launch_layernorm_half<T, 32>(x, rows, w, b, eps, gelu, out, stream);
+    case 64: return launch_layernorm_half<T, 64>(x, rows, w, b, eps, gelu, out, stream);
+    case 128: return launch_layernorm_half<T, 128>(x, rows, w, b, eps, gelu, out, stream);
+    case 256: return launch_layernorm_half<T, 256>(x, rows, w, b, eps, gelu, out, stream);
+    default: return SSAM_ERR_UNSUPPORTED;
+  }
+}
+
+int layernorm_half(const void* x, int64_t rows, int C, const void* w, const void* b, float eps, int gelu, int dtype,
+                   void* out, cudaStream_t stream) {
+  if (x == nullptr || w == nullptr || b == nullptr || out == nullptr || rows < 0 || C <= 0) return SSAM_ERR_INVALID;
+  if ((dtype != 0 && dtype != 1) || (gelu != 0 && gelu != 1)) return SSAM_ERR_INVALID;
+  if (C != 32 && C != 64 && C != 128 && C != 256) return SSAM_ERR_UNSUPPORTED;
+  if (!aligned16(x) || !aligned16(w) || !aligned16(b) || !aligned16(out)) return SSAM_ERR_ALIGN;
+  if (rows == 0) return SSAM_OK;
+  return dtype == 0 ? dispatch_layernorm_half<__half>(x, rows, C, w, b, eps, gelu, out, stream)
+                    : dispatch_layernorm_half<__nv_bfloat16>(x, rows, C, w, b, eps, gelu, out, stream);
+}
+
 int layernorm_rows_copy(const float* x, int n_rows, int C, const float* w, const float* b, float eps, void* out,
                         float* copy, cudaStream_t stream) {
   if (x == nullptr || w == nullptr || b == nullptr || out == nullptr || copy == nullptr || n_rows < 0 || C <= 0)

@@ -48,18 +48,49 @@ import torch
 import torch.nn as nn
 import torch.nn.functional as F
 
-from . import host
+from . import host, ops
 from .host import SAM_PIXEL_MEAN, SAM_PIXEL_STD
 
 
 class LayerNorm2d(host.LayerNorm2d):
-    """Channel LayerNorm of an NCHW map (eps 1e-6, parameters `weight` / `bias`)
-    computed in one pass over the channels-last view: the decoder keeps its maps
-    in channels-last memory, where that view is contiguous."""
+    """Channel LayerNorm of an NCHW map (eps 1e-6, parameters `weight` / `bias`),
+    followed by the exact GELU when `gelu` (the decoder's LayerNorm2d -> GELU
+    pairs; the GELU slot of the Sequential is then an nn.Identity, which keeps the
+    checkpoint's parameter names). Computed on the channels-last view, which is
+    contiguous for the decoder's channels-last maps: on CUDA half-precision maps
+    by ssam_layernorm_gelu_half (one pass, GELU fused), elsewhere by torch."""
+
+    def __init__(self, num_channels: int, eps: float = 1e-6, gelu: bool = False):
+        super().__init__(num_channels, eps)
+        self.gelu = gelu
 
     def forward(self, x: torch.Tensor) -> torch.Tensor:
-        y = F.layer_norm(x.permute(0, 2, 3, 1), (x.shape[1],), self.weight, self.bias, self.eps)
+        nhwc = x.permute(0, 2, 3, 1)
+        if (x.is_cuda and x.dtype in (torch.float16, torch.bfloat16) and self.weight.dtype == x.dtype
+                and x.shape[1] in ops.LN_HALF_CHANNELS and nhwc.is_contiguous()):
+            y = ops.layernorm_gelu_half(nhwc, self.weight, self.bias, self.eps, self.gelu)
+        else:
+            y = F.layer_norm(nhwc, (x.shape[1],), self.weight, self.bias, self.eps)
+            if self.gelu:
+                y = F.gelu(y)
         return y.permute(0, 3, 1, 2)
+
+
+class RowLayerNorm(nn.LayerNorm):
+    """nn.LayerNorm over the last dimension (same parameters); on CUDA
+    half-precision rows of 32 .. 256 channels computed by ssam_layernorm_gelu_half
+    (the two-way transformer's norm of the 4096 image tokens per prompt)."""
+
+    def forward(self, x: torch.Tensor) -> torch.Tensor:
+        if (x.is_cuda and x.dtype in (torch.float16, torch.bfloat16) and self.weight is not None
+                and self.weight.dtype == x.dtype and x.shape[-1] in ops.LN_HALF_CHANNELS and x.is_contiguous()):
+            return ops.layernorm_gelu_half(x, self.weight, self.bias, self.eps, False)
+        return super().forward(x)
+
+
+def _ln_gelu(c: int):
+    """LayerNorm2d with the GELU fused, and the Identity that holds the GELU's slot."""
+    return LayerNorm2d(c, gelu=True), nn.Identity()
 
 
 def _channels_last(x: torch.Tensor) -> torch.Tensor:
@@ -125,8 +156,8 @@ class PromptEncoder(nn.Module):
         self.mask_input_size = (4 * image_embedding_size[0], 4 * image_embedding_size[1])
         c4 = mask_in_chans // 4
         self.mask_downscaling = nn.Sequential(
-            nn.Conv2d(1, c4, kernel_size=2, stride=2), LayerNorm2d(c4), nn.GELU(),
-            nn.Conv2d(c4, mask_in_chans, kernel_size=2, stride=2), LayerNorm2d(mask_in_chans), nn.GELU(),
+            nn.Conv2d(1, c4, kernel_size=2, stride=2), *_ln_gelu(c4),
+            nn.Conv2d(c4, mask_in_chans, kernel_size=2, stride=2), *_ln_gelu(mask_in_chans),
             nn.Conv2d(mask_in_chans, embed_dim, kernel_size=1),
         )
         self.no_mask_embed = nn.Embedding(1, embed_dim)
@@ -243,7 +274,7 @@ class TwoWayAttentionBlock(nn.Module):
         self.norm2 = nn.LayerNorm(embedding_dim)
         self.mlp = DecoderMLPBlock(embedding_dim, mlp_dim)
         self.norm3 = nn.LayerNorm(embedding_dim)
-        self.norm4 = nn.LayerNorm(embedding_dim)
+        self.norm4 = RowLayerNorm(embedding_dim)       # over the image tokens
         self.cross_attn_image_to_token = DecoderAttention(embedding_dim, num_heads, attention_downsample_rate)
         self.skip_first_layer_pe = skip_first_layer_pe
 
@@ -335,7 +366,7 @@ class MaskDecoderHQ(nn.Module):
         self.iou_token = nn.Embedding(1, c)
         self.mask_tokens = nn.Embedding(n_sam, c)
         self.output_upscaling = nn.Sequential(
-            nn.ConvTranspose2d(c, c // 4, kernel_size=2, stride=2), LayerNorm2d(c // 4), nn.GELU(),
+            nn.ConvTranspose2d(c, c // 4, kernel_size=2, stride=2), *_ln_gelu(c // 4),
             nn.ConvTranspose2d(c // 4, c // 8, kernel_size=2, stride=2), nn.GELU(),
         )
         self.output_hypernetworks_mlps = nn.ModuleList([MLP(c, c, c // 8, 3) for _ in range(n_sam)])
@@ -345,15 +376,15 @@ class MaskDecoderHQ(nn.Module):
         self.hf_mlp = MLP(c, c, c // 8, 3)
         self.num_mask_tokens = n_sam + 1
         self.compress_vit_feat = nn.Sequential(
-            nn.ConvTranspose2d(vit_dim, c, kernel_size=2, stride=2), LayerNorm2d(c), nn.GELU(),
+            nn.ConvTranspose2d(vit_dim, c, kernel_size=2, stride=2), *_ln_gelu(c),
             nn.ConvTranspose2d(c, c // 8, kernel_size=2, stride=2),
         )
         self.embedding_encoder = nn.Sequential(
-            nn.ConvTranspose2d(c, c // 4, kernel_size=2, stride=2), LayerNorm2d(c // 4), nn.GELU(),
+            nn.ConvTranspose2d(c, c // 4, kernel_size=2, stride=2), *_ln_gelu(c // 4),
             nn.ConvTranspose2d(c // 4, c // 8, kernel_size=2, stride=2),
         )
         self.embedding_maskfeature = nn.Sequential(
-            nn.Conv2d(c // 8, c // 4, 3, 1, 1), LayerNorm2d(c // 4), nn.GELU(),
+            nn.Conv2d(c // 8, c // 4, 3, 1, 1), *_ln_gelu(c // 4),
             nn.Conv2d(c // 4, c // 8, 3, 1, 1),
         )
 
@@ -631,7 +662,7 @@ def init_prompt_decoder_weights(model: nn.Module, seed: int = 1) -> nn.Module:
                 host._trunc_normal_(w, 1.0 / math.sqrt(max(1, fan_in)), gen)
                 if mod.bias is not None:
                     mod.bias.zero_()
-            elif isinstance(mod, (nn.LayerNorm, LayerNorm2d)):
+            elif isinstance(mod, (nn.LayerNorm, LayerNorm2d)):      # RowLayerNorm included
                 mod.weight.fill_(1.0)
                 mod.bias.zero_()
             elif isinstance(mod, nn.Embedding):

@@ -459,6 +459,27 @@ def layernorm_nchw(x: torch.Tensor, B: int, H: int, W: int, w: torch.Tensor, b: 
     return out
 
 
+LN_HALF_CHANNELS = (32, 64, 128, 256)
+
+
+def layernorm_gelu_half(x: torch.Tensor, w: torch.Tensor, b: torch.Tensor, eps: float,
+                        gelu: bool) -> torch.Tensor:
+    """Channel LayerNorm (+ exact GELU) of fp16 / bf16 channels-last rows (..., C),
+    C in LN_HALF_CHANNELS; w, b of x's dtype. Returns a new tensor of x's shape."""
+    _check_cuda(x, w, b)
+    if x.dtype not in (torch.float16, torch.bfloat16) or w.dtype != x.dtype or b.dtype != x.dtype:
+        raise ValueError("x, w and b must share one half-precision dtype")
+    if not x.is_contiguous() or not w.is_contiguous() or not b.is_contiguous():
+        raise ValueError("x, w and b must be contiguous")
+    C = x.shape[-1]
+    out = torch.empty_like(x)
+    if x.numel() == 0:
+        return out
+    _lib.call("ssam_layernorm_gelu_half", x.data_ptr(), x.numel() // C, C, w.data_ptr(), b.data_ptr(),
+              float(eps), int(bool(gelu)), 0 if x.dtype == torch.float16 else 1, out.data_ptr(), _stream(x))
+    return out
+
+
 def split_bf16x2(x: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
     """fp32 (rows, C) -> bf16 (rows, 2C) = [hi | lo] with hi + lo ~= x."""
     _check_cuda(x, out)

@@ -3,7 +3,7 @@ import pytest
 import torch
 import torch.nn.functional as F
 
-from sparsesam_b200 import host, ops
+from sparsesam_b200 import _lib, host, ops
 
 pytestmark = pytest.mark.gpu
 
@@ -235,3 +235,38 @@ def test_gemm_addend_is_broadcast_then_add(cuda_device, B, T, K, N):
     ops.gemm_bf16(a, w, bias, epilogue=ops.SSAM_EPI_ADD_F32, out=ref)
     assert ops.device_error() == 0
     assert torch.equal(got, ref)
+
+
+@pytest.mark.parametrize("C", [32, 64, 128, 256])
+@pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16])
+@pytest.mark.parametrize("gelu", [False, True])
+def test_layernorm_gelu_half_rows(cuda_device, C, dtype, gelu):
+    """ssam_layernorm_gelu_half (the SAM-HQ decoder's LayerNorm2d -> GELU on
+    channels-last maps) against torch fp32 LayerNorm (+ exact GELU) of the same
+    half-precision inputs; rows not a multiple of a CTA's row group (the tail)."""
+    g = torch.Generator().manual_seed(C)
+    rows = 3 * 1184 * (256 // (C // 8)) + 37        # more row groups than the grid's CTAs, plus a tail
+    x = (torch.randn(rows, C, generator=g) * 3 + 1.5).to(dtype).to(cuda_device)
+    w = (torch.rand(C, generator=g) + 0.5).to(dtype).to(cuda_device)
+    b = (torch.randn(C, generator=g) * 0.1).to(dtype).to(cuda_device)
+    y = ops.layernorm_gelu_half(x, w, b, 1e-6, gelu)
+    ref = torch.nn.functional.layer_norm(x.float(), (C,), w.float(), b.float(), 1e-6)
+    if gelu:
+        ref = torch.nn.functional.gelu(ref)
+    # the output's own rounding (fp16: 2^-11, bf16: 2^-8 of the value) plus fp32 arithmetic
+    rel = 2.0 ** -11 if dtype == torch.float16 else 2.0 ** -8
+    err = (y.float() - ref).abs()
+    assert (err <= rel * ref.abs() + 2e-4).all(), err.max().item()
+    assert y.dtype == dtype and y.shape == x.shape
+
+
+def test_layernorm_gelu_half_refuses(cuda_device):
+    x = torch.zeros(10, 48, dtype=torch.float16, device=cuda_device)
+    w = torch.ones(48, dtype=torch.float16, device=cuda_device)
+    with pytest.raises(_lib.SparseSAMError):
+        ops.layernorm_gelu_half(x, w, w.clone(), 1e-6, True)          # C = 48: unsupported
+    x = torch.zeros(10, 64, dtype=torch.float16, device=cuda_device)
+    w = torch.ones(64, dtype=torch.float16, device=cuda_device)
+    with pytest.raises(ValueError):
+        ops.layernorm_gelu_half(x, w.bfloat16(), w.bfloat16(), 1e-6, True)   # mixed dtypes
+    assert ops.layernorm_gelu_half(x[:0], w, w.clone(), 1e-6, False).numel() == 0
