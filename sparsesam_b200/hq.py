@@ -691,7 +691,12 @@ def build_sam_hq(arch: str = "vit_l", checkpoint: Optional[str] = None, seed: in
     sam = SamHQ(enc, prompt, decoder).to(device)
     if checkpoint is not None:
         state = torch.load(checkpoint, map_location=device)
-        sam.load_state_dict(state.get("model", state) if isinstance(state, dict) else state, strict=False)
+        if isinstance(state, dict) and "model" in state:
+            state = state["model"]
+        # extra entries are tolerated; a parameter of this model left unset is an error
+        missing = sam.load_state_dict(state, strict=False).missing_keys
+        if missing:
+            raise KeyError(f"checkpoint {checkpoint} lacks {len(missing)} parameters, e.g. {missing[:3]}")
     sam.prompt_encoder.to(decoder_dtype)
     sam.mask_decoder.to(decoder_dtype)
     return sam.eval()

@@ -148,6 +148,21 @@ def test_checkpoint_layout(sam):
     assert all(torch.equal(a, b) for a, b in zip(other.state_dict().values(), sd.values()))
 
 
+def test_checkpoint_loading(sam, tmp_path):
+    """sam_model_registry[arch](checkpoint=...) loads a saved state dict by name;
+    extra entries are tolerated, a missing parameter is an error."""
+    path = tmp_path / "sam_hq_vit_b.pth"
+    sd = dict(sam.state_dict())
+    sd["some_extra_buffer"] = torch.zeros(1)
+    torch.save(sd, path)
+    loaded = hq.sam_model_registry["vit_b"](checkpoint=str(path), img_size=IMG, seed=7)
+    assert all(torch.equal(a, sd[k]) for k, a in loaded.state_dict().items())
+    del sd["mask_decoder.hf_token.weight"]
+    torch.save(sd, path)
+    with pytest.raises(KeyError):
+        hq.sam_model_registry["vit_b"](checkpoint=str(path), img_size=IMG)
+
+
 def _np_boxes(m):
     out = []
     for mi in m:
