@@ -15,10 +15,11 @@ and reading only that module's parameters by name:
 * LayerNorms from their moments; bilinear resizing (align_corners=False, the
   half-pixel convention) from its index arithmetic.
 
-Parity with SAM-HQ itself is unpinned: neither its source nor a checkpoint is
-available here. Parity of the product module with this restatement, and of the
-GPU encoder + decoder with oracle.encoder + this restatement, is what the tests
-check.
+SAM-HQ's own source and checkpoints are not available here; the product module
+is also checked against the third-party SamModel / SamHQModel of the installed
+transformers package (tests/test_hq_third_party.py). Parity of the product module
+with this restatement, and of the GPU encoder + decoder with oracle.encoder + this
+restatement, is what the other tests check.
 """
 from __future__ import annotations
 

@@ -26,7 +26,9 @@ is an independent implementation of the published architecture:
 
 Parameter and buffer names follow SAM-HQ's checkpoint layout, so the state dict
 of a `sam_hq_vit_*.pth` checkpoint loads into `SamHQ` (none is present here:
-the weights are seeded random, `init_prompt_decoder_weights`).
+the weights are seeded random, `init_prompt_decoder_weights`). The arithmetic is
+checked against the SamModel / SamHQModel implementations of the transformers
+package with the same weights mapped onto their parameter names.
 
 Differences by design:
 * `SamPredictor.set_torch_image` takes a batch of images, and `predict_torch`
