@@ -565,8 +565,10 @@ def run_predictor(args) -> None:
     box-prompted HQ decode per image (hq_token_only, the whole batch in one decoder
     pass) -> masks at 1024^2. Synthetic images with one ellipse each (the dataset is
     not available) and seeded random weights; the IoU printed is a pipeline check,
-    not a quality figure. value: images in HBM, device-timed; e2e: uint8 images from
-    pinned host memory in and boolean masks out inside every step."""
+    not a quality figure. The timed step is captured once as a CUDA graph and
+    replayed (hq.GraphedBoxStep): at small batches the eager step is launch-bound.
+    value: images in HBM, device-timed; e2e: uint8 images from pinned host memory
+    in and boolean masks out inside every step."""
     import torch
     from sparsesam_b200 import _lib, hq, registry
     from sparsesam_b200.sparsesam.sam import apply_patch
@@ -600,28 +602,40 @@ def run_predictor(args) -> None:
         encode(img_dev)
         return decode(box_dev)
 
-    def step_e2e():
-        x = img_host.to(dev, non_blocking=True)
-        bx = box_host.to(dev, non_blocking=True)
-        encode(x)
-        mask_host.copy_(decode(bx), non_blocking=True)
-        torch.cuda.current_stream().synchronize()
-
     with torch.no_grad():
         for _ in range(args.warmup):
             step()
         torch.cuda.synchronize()
-        clocks = ClockSampler(0)
-        clocks.start()
         launches0 = _lib.launch_count
-        ms = _event_ms(step, args.steps)
+        eager_ms = _event_ms(step, args.steps)
         launches = (_lib.launch_count - launches0) // max(1, args.steps)
-        clk = clocks.stop()
         enc_ms = _event_ms(lambda: encode(img_dev), args.steps)
         dec_ms = _event_ms(lambda: decode(box_dev), args.steps)
+        # the timed step: the whole step captured once as a CUDA graph and replayed
+        graphed = hq.GraphedBoxStep(sam, batch)
+
+        def step_graph():
+            return graphed(img_dev, box_dev)[0]
+
+        def step_e2e():
+            graphed.images.copy_(img_host, non_blocking=True)
+            graphed.boxes.copy_(box_host, non_blocking=True)
+            graphed.graph.replay()
+            mask_host.copy_(graphed.masks, non_blocking=True)
+            torch.cuda.current_stream().synchronize()
+
+        for _ in range(args.warmup):
+            step_graph()
+        torch.cuda.synchronize()
+        clocks = ClockSampler(0)
+        clocks.start()
+        ms = _event_ms(step_graph, args.steps)
+        clk = clocks.stop()
         step_e2e()
         ms_e2e = _event_ms(step_e2e, args.steps)
-        masks = step()
+        masks = step_graph().clone()
+        if not torch.equal(mask_host.to(dev), masks):
+            raise RuntimeError("end-to-end masks differ from the device replay")
         iou = hq.compute_iou(masks, labels.to(dev)).item()
         biou = hq.compute_boundary_iou(masks[:4], labels[:4].to(dev)).item()
     if ops.device_error() != 0:
@@ -640,7 +654,10 @@ def run_predictor(args) -> None:
                    "l2": "inputs larger than L2: {:.0f} MB of images per step".format(img_host.numel() / 1e6)},
         "e2e": {"value": batch / ms_e2e * 1e3, "unit": "images/s", "h2d_bytes_per_step": img_host.numel() +
                 box_host.numel() * 4, "d2h_bytes_per_step": mask_host.numel()},
-        "legs_ms": {"encoder": enc_ms, "decode (prompt encoder, HQ decoder, mask upsampling)": dec_ms},
+        "legs_ms": {"encoder": enc_ms, "decode (prompt encoder, HQ decoder, mask upsampling)": dec_ms,
+                    "eager step (no graph)": eager_ms},
+        "timed": "the step captured once as a CUDA graph (hq.GraphedBoxStep) and replayed; legs and the eager "
+                 "step from eager launches",
         "encoder_tflops": flops_img * batch / enc_ms / 1e9,
         "gpu_launches": launches,
         "iou_check": {"iou": iou, "boundary_iou_first4": biou,

@@ -131,8 +131,9 @@ class PositionEmbeddingRandom(nn.Module):
         """Encoding of pixel coordinates (..., 2) = (x, y) in an image of size (h, w)."""
         h, w = image_size
         g = self.positional_encoding_gaussian_matrix
-        p = coords.to(g.dtype) / torch.tensor([float(w), float(h)], dtype=g.dtype, device=coords.device)
-        return self._fourier(p)
+        c = coords.to(g.dtype)
+        # scalar divisors: no host-to-device copy (the step can be captured in a CUDA graph)
+        return self._fourier(torch.stack([c[..., 0] / w, c[..., 1] / h], dim=-1))
 
 
 class PromptEncoder(nn.Module):
@@ -838,6 +839,57 @@ def process_batch(predictor: SamPredictor, images: torch.Tensor, labels_boxes: t
         "iou": compute_iou(masks, labels_ori).item(),
         "boundary_iou": compute_boundary_iou(masks, labels_ori).item(),
     }
+
+
+class GraphedBoxStep:
+    """One predictor step for a fixed batch of square images — preprocess, image
+    encoder, one box prompt per image through the prompt encoder and decoder, masks
+    resized to the image size and thresholded — captured once as a CUDA graph and
+    replayed. At small batches the eager step is launch-bound (the decoder alone is
+    a few hundred short kernels); a replay issues them with one launch.
+
+    step = GraphedBoxStep(sam, batch)
+    masks, iou, low_res = step(images, boxes)   # images (B, 3, S, S) 0..255, boxes (B, 4)
+
+    The outputs are the graph's own buffers, overwritten by the next call (clone to
+    keep). The model's weights and the patch state are read when captured: capture
+    again after changing either."""
+
+    def __init__(self, sam: SamHQ, batch: int, hq_token_only: bool = True, multimask_output: bool = False,
+                 image_dtype: torch.dtype = torch.uint8, warmup: int = 2):
+        dev = sam.device
+        if dev.type != "cuda":
+            raise ValueError("GraphedBoxStep needs the model on a CUDA device")
+        s = sam.image_encoder.img_size
+        self.sam = sam
+        self.images = torch.zeros(batch, 3, s, s, dtype=image_dtype, device=dev)
+        self.boxes = torch.zeros(batch, 4, dtype=torch.float32, device=dev)
+        self.boxes[:, 2:] = s - 1
+        pred = SamPredictor(sam)
+
+        def body():
+            x = sam.preprocess(self.images)
+            pred.features, pred.interm_features = sam.image_encoder(x)
+            pred.original_size = pred.input_size = (s, s)
+            pred.is_image_set = True
+            return pred.predict_torch(None, None, boxes=self.boxes, multimask_output=multimask_output,
+                                      hq_token_only=hq_token_only)
+
+        side = torch.cuda.Stream(dev)
+        side.wait_stream(torch.cuda.current_stream(dev))
+        with torch.no_grad(), torch.cuda.stream(side):
+            for _ in range(warmup):   # library work spaces and autotuning outside the capture
+                body()
+        torch.cuda.current_stream(dev).wait_stream(side)
+        self.graph = torch.cuda.CUDAGraph()
+        with torch.no_grad(), torch.cuda.graph(self.graph):
+            self.masks, self.iou, self.low_res = body()
+
+    def __call__(self, images: torch.Tensor, boxes: torch.Tensor):
+        self.images.copy_(images, non_blocking=True)
+        self.boxes.copy_(boxes, non_blocking=True)
+        self.graph.replay()
+        return self.masks, self.iou, self.low_res
 
 
 def synthetic_box_batch(batch: int, seed: int, img_size: int = 1024, device="cpu"):

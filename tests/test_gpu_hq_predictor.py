@@ -102,3 +102,26 @@ def test_process_batch_on_gpu(cuda_device):
         assert torch.allclose(low_b[i:i + 1], low_i, rtol=1e-3, atol=1e-3 * low_i.abs().max().item())
     ious = [hq.mask_iou(m_b[i, 0], r["labels"][i, 0].to(cuda_device)).item() for i in range(2)]
     assert abs(out["iou"] - sum(ious) / 2) < 1e-6
+
+
+@pytest.mark.parametrize("batch", [1, 2])
+def test_graphed_step_replays_the_eager_step(cuda_device, batch):
+    """GraphedBoxStep (the whole predictor step captured as one CUDA graph) gives the
+    eager step's results, replay after replay, with new inputs copied in each time."""
+    r = _setup(cuda_device)
+    sam = r["sam"]
+    step = hq.GraphedBoxStep(sam, batch)
+    pred = hq.SamPredictor(sam)
+    for trial in range(2):
+        images, _, boxes = hq.synthetic_box_batch(batch, seed=10 + trial)
+        images = images.to(torch.uint8).to(cuda_device)
+        boxes = boxes.to(cuda_device)
+        masks, iou, low = step(images, boxes)
+        with torch.no_grad():
+            pred.set_torch_image(images, (1024, 1024))
+            m_e, iou_e, low_e = pred.predict_torch(None, None, boxes=boxes, multimask_output=False,
+                                                   hq_token_only=True)
+        torch.cuda.synchronize()
+        assert torch.allclose(low, low_e, rtol=1e-4, atol=1e-4 * low_e.abs().max().item())
+        assert torch.allclose(iou, iou_e, rtol=1e-4, atol=1e-5)
+        assert (masks ^ m_e).float().mean().item() < 1e-4
