@@ -165,6 +165,30 @@ def cpu_baseline(sample_images: int = 1) -> dict:
                       f" {dt:.1f} s"}
 
 
+def cpu_baseline_predictor(arch: str, ratio: float) -> dict:
+    """The predictor step's CPU restatement (oracle/: the patched encoder and the
+    box-prompted HQ decode with its mask resize) on this host's cores, one image."""
+    import torch
+
+    from oracle import decoder as odec
+    from oracle import encoder as oenc
+    from sparsesam_b200 import hq
+    cores = len(os.sched_getaffinity(0))
+    torch.set_num_threads(cores)
+    sam = hq.build_sam_hq(arch)
+    sd = sam.state_dict()
+    images, _, boxes = hq.synthetic_box_batch(1, seed=0, img_size=IMG)
+    t0 = time.perf_counter()
+    with torch.no_grad():
+        feats, interm = oenc.encoder_forward(sam.image_encoder, sam.preprocess(images), ratio)
+        low, _ = odec.decode_boxes(sd, feats, interm[0], boxes, (IMG, IMG), False, True)
+        _ = odec.postprocess(low, IMG, (IMG, IMG), (IMG, IMG)) > 0
+    dt = time.perf_counter() - t0
+    return {"value": 1 / dt, "unit": "images/s", "cores": cores, "kind": "port",
+            "sample": f"1 image of the same workload ({arch}, 1024^2, d={ratio}: encoder fp32, decode fp64), "
+                      f"torch on CPU, {dt:.1f} s"}
+
+
 def shard_seed(rank: int) -> int:
     """Seed of rank `rank`'s image shard: every rank encodes its own images."""
     return 1000 + rank
@@ -662,7 +686,8 @@ def run_predictor(args) -> None:
         "gpu_launches": launches,
         "iou_check": {"iou": iou, "boundary_iou_first4": biou,
                       "note": "random weights: a pipeline check, not segmentation quality"},
-        "clocks": clk}), flush=True)
+        "clocks": clk,
+        **({} if args.no_cpu_baseline else {"cpu_baseline": cpu_baseline_predictor(arch, ratio)})}), flush=True)
 
 
 def main() -> None:
