@@ -24,6 +24,11 @@ SHAPES = [
     (16384, 256, 136),   # 2-SM path, ragged K tail inside the last stage's first sub-tile
     (20000, 1280, 320),  # 2-SM path, M tail inside a CTA pair
     (16500, 768, 1280),  # 2-SM path, M tail in the second CTA of the last pair
+    # small-batch ViT-L shapes (partial last wave of the 74 SM pairs)
+    (16384, 1024, 1024),  # ViT-L batch-4 proj
+    (4916, 1024, 512),    # ViT-L batch-4 fc2 on the keep rows (K shortened)
+    (4916, 4096, 256),    # ViT-L batch-4 fc1 on the keep rows (K shortened)
+    (16384, 992, 200),    # ragged last N tile, ragged K
 ]
 
 
