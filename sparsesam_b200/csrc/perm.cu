@@ -360,14 +360,28 @@ __global__ void stripe_sort_kernel(const StripeArgs a) {
   }
 }
 
+// threads: the block size for small rows (G <= 256); rows of more groups get as many
+// warps as the variant's registers allow (up to 1024 threads): each warp walks its
+// groups one at a time with one group's gathers in flight, so a row's two passes are
+// latency chains whose length is groups per warp — with fewer rows than SMs (a
+// global grid at small batches) nothing else hides them.
 template <int GS, int CH>
 static int launch_stripe(const StripeArgs& a, int rows, int threads, size_t smem, cudaStream_t stream) {
   static PerDeviceOnce configured;
+  static std::atomic<int> max_threads{256};
   const int st = configured.run(current_device(), [] {
+    cudaFuncAttributes attr;
+    int e = status_from_cuda(cudaFuncGetAttributes(&attr, stripe_sort_kernel<GS, CH>));
+    if (e != SSAM_OK) return e;
+    const int by_regs = attr.numRegs > 0 ? (65536 / (attr.numRegs * 32)) * 32 : 256;
+    int t = by_regs < attr.maxThreadsPerBlock ? by_regs : attr.maxThreadsPerBlock;
+    t = t > 1024 ? 1024 : (t < 256 ? 256 : t);
+    max_threads.store(t, std::memory_order_relaxed);
     return status_from_cuda(
         cudaFuncSetAttribute(stripe_sort_kernel<GS, CH>, cudaFuncAttributeMaxDynamicSharedMemorySize, 160 * 1024));
   });
   if (st != SSAM_OK) return st;
+  if (a.G > 256) threads = max_threads.load(std::memory_order_relaxed);
   stripe_sort_kernel<GS, CH><<<rows, threads, smem, stream>>>(a);
   return status_from_cuda(cudaGetLastError());
 }
